@@ -1,0 +1,416 @@
+"""Decode-attention benchmark of the InnerQ hot path on B200.
+
+    python bench.py [--gpus N --steps K --warmup W]            # this framework
+    python bench.py --impl reference [--steps K --warmup W]     # reference CPU path
+
+Workload (the metric's configuration): Llama-3-8B attention
+shape — 32 layers, 32 query / 8 KV heads, head_dim 128 — batch 32, context
+32768, 4-bit InnerQ cache (K channel groups of 32, symmetric, normalised, flush
+1; V token groups of 32, symmetric, flush 32; 32 sink + 96 recent fp16 tokens).
+K = N(0,1) x exp(N(0,1)) per channel, V = N(0,1), q = N(0,1), fp16, seeded.
+
+One step = one decode token through all 32 layers: append the new K/V token
+(quantize-and-pack) and run the fused decode attention per layer.  With N
+GPUs the 8 KV heads (and their query heads) are partitioned across ranks and
+the per-layer outputs are all-gathered over NCCL once per step.
+
+`value` is algorithmic HBM bytes per step (packed codes + scales + fp16 sink /
+recent + normalisation factor + q + out, summed over all ranks) / time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+import types
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode attn HBM GB/s (4-bit QK^T+AV, Llama-3-8B attention shape)"
+D = 128
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--hq", type=int, default=32)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--kbits", type=int, default=4)
+    ap.add_argument("--vbits", type=int, default=4)
+    ap.add_argument("--group", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+def cache_kw(a):
+    return dict(k_bits=a.kbits, v_bits=a.vbits, key_group_size=a.group, value_group_size=a.group,
+                key_flush_size=1, value_flush_size=max(32, a.group), key_w_sink=32, value_w_sink=32,
+                key_w_recent=96, value_w_recent=96, key_normalize=True,
+                key_quantize_over_token=False, value_quantize_over_token=True)
+
+
+def side_bytes(n_q, n_sink, n_recent, bits, group, over_token, asym=False, norm=False):
+    """Algorithmic bytes one (b, kv-head) reads for one side."""
+    z = 2 if asym else 1
+    if over_token:
+        b = n_q * bits * D // 8 + (n_q // group) * D * 2 * z
+    else:
+        b = n_q * (bits * D // 8 + (D // group) * 2 * z)
+    b += (n_sink + n_recent) * D * 2
+    if norm:
+        b += D * 2
+    return b
+
+
+def layer_bytes(layer, B, Hkv, Hq):
+    k, v = layer.key_side, layer.value_side
+    per_bh = side_bytes(k.n_q, k.n_sink, k.n_recent, k.bits, k.group, False, k.mode == 1, k.normalize) \
+        + side_bytes(v.n_q, v.n_sink, v.n_recent, v.bits, v.group, True, v.mode == 1)
+    return B * Hkv * per_bh + 2 * B * Hq * D * 2
+
+
+# --------------------------------------------------------------- clocks ---
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------- CPU reference ---
+def cpu_reference_sample(a, seconds=None, steps=None, warmup=0):
+    """The reference's CPU algorithm (oracle port of cache.py + the HF
+    consumer): per decode step, append the token, dequantize the whole cache
+    in fp32, cast, and run fp32 GQA attention.  Sample = one layer, batch 1,
+    all KV heads, full context; KV heads run on a thread pool (numpy releases
+    the GIL).  Returns (GB/s, cores, sample description, seconds per step)."""
+    import concurrent.futures as cf
+
+    import numpy as np
+
+    from oracle import cache_ref as C
+    kw = cache_kw(a)
+    S = a.ctx
+    cores = min(a.hkv, os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    rep = a.hq // a.hkv
+
+    def one_head(h):
+        r = np.random.default_rng(h)
+        k = (r.standard_normal((1, 1, S - 1, D), dtype=np.float32)
+             * np.exp(r.standard_normal(D)).astype(np.float32)).astype(np.float16).astype(np.float32)
+        v = r.standard_normal((1, 1, S - 1, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+        layer = C.OracleLayer(C.CacheConfig(**kw), "fp16")
+        layer.update(k, v)
+        return layer
+
+    with cf.ThreadPoolExecutor(cores) as ex:
+        layers = list(ex.map(one_head, range(a.hkv)))
+    q = rng.standard_normal((1, rep, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    newk = rng.standard_normal((1, 1, 1, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+
+    def head_step(layer):
+        K, V = layer.update(newk, newk)
+        Kf = K[0, 0].astype(np.float32)
+        Vf = V[0, 0].astype(np.float32)
+        logits = (q[0] @ Kf.T) / math.sqrt(D)
+        m = logits.max(-1, keepdims=True)
+        p = np.exp(logits - m)
+        return (p / p.sum(-1, keepdims=True)) @ Vf
+
+    def step():
+        with cf.ThreadPoolExecutor(cores) as ex:
+            list(ex.map(head_step, layers))
+
+    for _ in range(warmup):
+        step()
+    times = []
+    t_end = time.perf_counter() + (seconds or 1e9)
+    n = 0
+    while True:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+        n += 1
+        if (steps is not None and n >= steps) or (steps is None and time.perf_counter() > t_end):
+            break
+    k0 = layers[0].k
+    v0 = layers[0].v
+    per_bh = side_bytes(k0.n_quantized(), k0.sink.shape[2], k0.recent.shape[2], a.kbits, a.group,
+                        False, norm=True) \
+        + side_bytes(v0.n_quantized(), v0.sink.shape[2], v0.recent.shape[2], a.vbits, a.group, True)
+    nbytes = a.hkv * per_bh + 2 * a.hq * D * 2
+    t = statistics.median(times)
+    sample = (f"1 layer, batch 1, {a.hkv} kv heads x {a.hq // a.hkv} q heads, context {S}, "
+              f"{len(times)} steps; KV heads on {cores} threads")
+    return nbytes / t / 1e9, cores, sample, t
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    gbs, cores, sample, t = cpu_reference_sample(a, steps=a.steps, warmup=a.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s",
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic",
+        "config": {"workload": "C1: Llama-3-8B attention shape, 4-bit InnerQ cache, decode step",
+                   "batch": a.batch, "context": a.ctx, "layers": a.layers,
+                   "reference_sample": sample},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- ours ---
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    from innerq_b200 import _lib
+    from innerq_b200.cache import InnerqDynamicLayer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    assert a.hkv % world == 0, "KV heads must divide across GPUs"
+    hkv, hq = a.hkv // world, a.hq // world
+    B, L = a.batch, a.layers
+    kw = cache_kw(a)
+    conf = types.SimpleNamespace(_attn_implementation="innerq", **kw)
+
+    # ---- build the resident cache: prefill ctx-1 tokens per layer
+    layers = []
+    g = torch.Generator(device=dev)
+    for li in range(L):
+        g.manual_seed(1000 * li + rank)
+        k = torch.randn((B, hkv, a.ctx - 1, D), device=dev, generator=g)
+        k *= torch.exp(torch.randn(D, device=dev, generator=g))
+        k = k.half()
+        v = torch.randn((B, hkv, a.ctx - 1, D), device=dev, generator=g).half()
+        layer = InnerqDynamicLayer(conf, li)
+        layer.update(k, v)
+        del k, v
+        layers.append(layer)
+    torch.cuda.synchronize()
+
+    NPOOL = 8
+    g.manual_seed(7 + rank)
+    qs = torch.randn((NPOOL, L, B, hq, 1, D), device=dev, generator=g).half()
+    ks = torch.randn((NPOOL, L, B, hkv, 1, D), device=dev, generator=g).half()
+    vs = torch.randn((NPOOL, L, B, hkv, 1, D), device=dev, generator=g).half()
+    out = torch.empty((L, B, hq, D), device=dev, dtype=torch.float16)
+    gathered = torch.empty((world, L, B, hq, D), device=dev, dtype=torch.float16) if world > 1 else None
+
+    def step(i, q=None, k=None, v=None):
+        q = qs[i % NPOOL] if q is None else q
+        k = ks[i % NPOOL] if k is None else k
+        v = vs[i % NPOOL] if v is None else v
+        for li, layer in enumerate(layers):
+            layer.update(k[li], v[li])
+            layer.attend(q[li], out=out[li])
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+
+    def bytes_now():
+        return sum(layer_bytes(l, B, hkv, hq) for l in layers)
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    for i in range(max(3, a.warmup)):
+        step(i)
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    # ---- device-resident timed region
+    sampler = ClockSampler(local)
+    nbytes = 0
+    sync_all()
+    sampler.start()
+    launches0 = _lib.launch_count[0]
+    ev0.record(stream)
+    for i in range(a.steps):
+        nbytes += bytes_now()
+        step(i)
+    ev1.record(stream)
+    sync_all()
+    clocks = sampler.stop()
+    launches = _lib.launch_count[0] - launches0
+    ms = max_over_ranks(ev0.elapsed_time(ev1)) / a.steps
+    total_bytes = max_over_ranks(nbytes / a.steps) * world  # ranks hold equal shares
+    value = total_bytes / (ms * 1e-3) / 1e9
+
+    # ---- kernel roofline: attention launches alone (attention + its merge)
+    sync_all()
+    ev0.record(stream)
+    reps = 3
+    for r in range(reps):
+        for li, layer in enumerate(layers):
+            layer.attend(qs[0][li], out=out[li])
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    per_launch_ms = ev0.elapsed_time(ev1) / (reps * L)
+    per_launch_bytes = sum(layer_bytes(l, B, hkv, hq) for l in layers) / L
+    achieved = per_launch_bytes / (per_launch_ms * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers
+    qh = qs[0].cpu().pin_memory()
+    kh = ks[0].cpu().pin_memory()
+    vh = vs[0].cpu().pin_memory()
+    outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    qd, kd, vd = torch.empty_like(qs[0]), torch.empty_like(ks[0]), torch.empty_like(vs[0])
+    sync_all()
+    e2e_bytes = 0
+    ev0.record(stream)
+    for i in range(a.steps):
+        e2e_bytes += bytes_now()
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        step(i, qd, kd, vd)
+        outh.copy_(out, non_blocking=True)
+    ev1.record(stream)
+    sync_all()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / a.steps
+    e2e_value = max_over_ranks(e2e_bytes / a.steps) * world / (e2e_ms * 1e-3) / 1e9
+    h2d = (qh.numel() + kh.numel() + vh.numel()) * 2 * world
+    d2h = outh.numel() * 2 * world
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        gbs, cores, sample, _ = cpu_reference_sample(a, seconds=a.cpu_seconds, warmup=1)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": sample}
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "decode_attn_traffic.json")))
+        traffic = round(tr["dram_bytes_per_algorithmic_byte"] * per_launch_bytes)
+    except (OSError, KeyError, ValueError):
+        pass
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded N(0,1) K with exp(N(0,1)) channel outliers, N(0,1) V and q)",
+            "config": {
+                "workload": "C1: decode step over a 32-layer Llama-3-8B-shaped 4-bit InnerQ cache",
+                "batch": B, "context": a.ctx, "layers": L, "q_heads": a.hq, "kv_heads": a.hkv,
+                "head_dim": D, "k_bits": a.kbits, "v_bits": a.vbits, "group": a.group,
+                "parallelism": f"kv-head shards x{world}",
+                "l2": f"inputs larger than L2 ({total_bytes / 1e9:.1f} GB of cache read per step)",
+                "us_per_layer": round(ms * 1e3 / L, 2),
+            },
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "decode_attn_kernel (+ lse_merge)",
+                         "per_launch_bytes": int(per_launch_bytes),
+                         "per_launch_us": round(per_launch_ms * 1e3, 2),
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,187 @@
+/*
+ * innerq_b200 — C ABI of the B200 (sm_100a) InnerQ decode hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and element strides,
+ * enqueues work on the caller's CUDA stream (`stream`, a cudaStream_t passed
+ * as void*; NULL = the legacy default stream) and allocates nothing.  Every
+ * entry point returns INNERQ_OK (0) or a negative INNERQ_ERR_* status;
+ * innerq_last_error() then describes the failure (per calling thread).
+ *
+ * Geometry: head_dim D must be 128.  Tensors named [B][H][T][D] are indexed
+ * with element strides (sb, sh, st) and a contiguous last dimension.
+ * Element types are 16-bit: `dtype` = INNERQ_DT_F16 or INNERQ_DT_BF16 for the
+ * model activations and for stored scales / zero points / normalisation
+ * factors (the reference keeps those in the input dtype).
+ *
+ * Packed store of one of K or V ("side"), per (b, h):
+ *   codes  [B][H][cap_tiles][innerq_tile_bytes(bits)]   32 tokens per tile
+ *   scale  channel groups: [B][H][cap_tiles * 32][D / group]   (tile-swizzled)
+ *          token groups:   [B][H][cap_tiles * 32 / group][D]   (dim-swizzled)
+ *   zero   same shape as scale, asymmetric mode only
+ * Role K uses the row layout (tokens are rows of the QK^T A operand) and role
+ * V the col layout (dims are rows of the PV A operand); see
+ * innerq_b200/csrc/common.cuh for the bit-level layout.
+ *
+ * Supported combinations: role K with channel groups (group 32/64/128),
+ * role V with token groups (group 32/64/128); bits 2, 3, 4; symmetric or
+ * asymmetric.  These are the InnerQ layouts (key_quantize_over_token=False,
+ * value_quantize_over_token=True, the reference defaults, cache.py:87-88).
+ */
+#ifndef INNERQ_B200_H
+#define INNERQ_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define INNERQ_ABI_VERSION 1
+
+enum {
+  INNERQ_OK = 0,
+  INNERQ_ERR_ARG = -1,         /* bad size, pointer, alignment or stride */
+  INNERQ_ERR_UNSUPPORTED = -2, /* valid for the reference, not built here */
+  INNERQ_ERR_CUDA = -3         /* a CUDA launch or runtime call failed */
+};
+enum { INNERQ_DT_F16 = 0, INNERQ_DT_BF16 = 1 };
+enum { INNERQ_SYM = 0, INNERQ_ASYM = 1 };         /* quant.py:43-46 QMode */
+enum { INNERQ_ROLE_K = 0, INNERQ_ROLE_V = 1 };
+
+/* Version of this ABI (INNERQ_ABI_VERSION). */
+int innerq_abi_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+const char* innerq_last_error(void);
+
+/* Bytes of one packed 32-token tile of one (b, h) at `bits` (D = 128). */
+int64_t innerq_tile_bytes(int bits);
+
+/*
+ * Key normalisation factor f[b][h][d] = dtype(sqrt(max_t |x[b][h][t][d]|)).
+ * Replaces the factor computation of InnerqDynamicLayer.normalize_keys
+ * (src/innerq/cache.py:121-126).  out_f is contiguous [B][H][D].
+ */
+int innerq_norm_factor(const void* x, int dtype, int B, int H, int T, int D, int64_t sb,
+                       int64_t sh, int64_t st, void* out_f, void* stream);
+
+/*
+ * Quantize T tokens x[B][H][T][D] and pack them into a store at packed token
+ * index t_offset (the cache-append quantizer).  Replaces quantize_sym /
+ * quantize_asym and their channel-/token-dim wrappers
+ * (src/innerq/quant.py:58-81, 95-119) as called by
+ * InnerqDynamicLayer.initialize_*_q / quantize_new_* (cache.py:187-210,
+ * 314-365), with the torch.cat onto the store replaced by an in-place write.
+ * norm_f (nullable, [B][H][D]) divides x first, in the dtype (cache.py:125).
+ * Token groups need T % group == 0 and t_offset % group == 0.  The store
+ * must hold t_offset + T tokens (cap_tiles * 32).
+ */
+int innerq_quant_pack(const void* x, int dtype, int B, int H, int T, int D, int64_t sb,
+                      int64_t sh, int64_t st, int bits, int group, int mode, int role,
+                      int over_token, const void* norm_f, void* codes, void* scale, void* zero,
+                      int64_t cap_tiles, int64_t t_offset, void* stream);
+
+/*
+ * Reference-format views of packed tokens [t_begin, t_begin + n): the int32
+ * codes, sign tensor and scale / zero-point tensors that quant.py:58-131
+ * returns (magnitudes + dtype signs for symmetric, raw codes + min for
+ * asymmetric).  out_sign / out_zero may be NULL.  All outputs contiguous:
+ * codes and signs [B][H][n][D]; scale and zero [B][H][n][D/group] (channel
+ * groups) or [B][H][n/group][D] (token groups).
+ */
+int innerq_unpack_ref(const void* codes, const void* scale, const void* zero, int dtype, int B,
+                      int H, int64_t t_begin, int64_t n, int D, int bits, int group, int mode,
+                      int role, int over_token, int64_t cap_tiles, int32_t* out_codes,
+                      void* out_sign, void* out_scale, void* out_zero, void* stream);
+
+/*
+ * Materialise dequantized tokens [t_begin, t_begin + n) in the model dtype
+ * exactly as InnerqDynamicLayer.get_*_deq (cache.py:235-281) does:
+ * dtype(fp32(c) * fp32(s) * sign [+ fp32(min)] [* fp32(norm_f)]).
+ * out is [B][H][n][D] with strides (ob, oh, ot).
+ */
+int innerq_dequant(const void* codes, const void* scale, const void* zero, int dtype, int B, int H,
+                   int64_t t_begin, int64_t n, int D, int bits, int group, int mode, int role,
+                   int over_token, int64_t cap_tiles, const void* norm_f, void* out, int64_t ob,
+                   int64_t oh, int64_t ot, void* stream);
+
+/*
+ * Dequantize reference-format tensors to fp32: the dequantize_{channeldim,
+ * tokendim}_{sym,asym} functions of src/innerq/quant.py:83-93, 121-131.
+ * codes int32 [n_outer][T][D]; scale (dtype) [n_outer][T][D/group] for
+ * channel groups or [n_outer][T/group][D] for token groups; zp_or_sign is the
+ * dtype sign tensor [n_outer][T][D] (symmetric) or the zero point shaped like
+ * scale (asymmetric).  out fp32 [n_outer][T][D].  Any D divisible by group.
+ */
+int innerq_dequant_ref(const int32_t* codes, const void* scale, const void* zp_or_sign, int dtype,
+                       int64_t n_outer, int T, int D, int group, int mode, int over_token,
+                       float* out, void* stream);
+
+/* One side (K or V) of the cache as the fused decode attention reads it.
+ * Token order is [sink | quantized | recent] (cache.py:235-276). */
+typedef struct {
+  const void* codes;   /* packed store (NULL when n_q == 0) */
+  const void* scale;
+  const void* zero;    /* asymmetric only */
+  int64_t cap_tiles;
+  const void* sink;    /* [B][H][n_sink][D] dtype, strides below */
+  int64_t sink_sb, sink_sh, sink_st;
+  const void* recent;  /* [B][H][n_recent][D] dtype */
+  int64_t rec_sb, rec_sh, rec_st;
+  int32_t n_sink, n_q, n_recent;
+  int32_t bits;        /* 2, 3, 4 (ignored when n_q == 0) */
+  int32_t group;
+  int32_t mode;        /* INNERQ_SYM / INNERQ_ASYM */
+  int32_t over_token;  /* 0 for K (channel groups), 1 for V (token groups) */
+} innerq_side;
+
+typedef struct {
+  int32_t struct_size; /* sizeof(innerq_attn_args) */
+  int32_t dtype;
+  int32_t B, Hq, Hkv, D;
+  const void* q;       /* [B][Hq][D] with strides (q_sb, q_sh) */
+  int64_t q_sb, q_sh;
+  const void* key_norm;/* [B][Hkv][D] contiguous normalisation factor, or NULL */
+  innerq_side k, v;
+  float softmax_scale; /* the reference consumer uses head_dim^-0.5 */
+  int32_t n_splits;    /* 0 = choose for the GPU; else the split-KV count */
+  int32_t tile_lo, tile_hi; /* 0,0 = all tiles; else a sub-range (context sharding) */
+} innerq_attn_args;
+
+/* Number of 32-token tiles the fused kernel iterates for these args, and the
+ * split count it will use (n_splits resolved). */
+int innerq_attn_plan(const innerq_attn_args* args, int32_t* n_tiles, int32_t* n_splits);
+
+/* Workspace bytes innerq_decode_attn needs (the split-KV partials). */
+int64_t innerq_decode_attn_workspace(const innerq_attn_args* args);
+
+/*
+ * Fused decode attention for one query token per sequence:
+ *   out[b][hq] = softmax(q[b][hq] . K[b][hq/G]^T * scale) V[b][hq/G]
+ * reading the packed K/V and fp16 sink / recent tokens directly.  Replaces
+ * InnerqDynamicLayer.get_deq_tensors (cache.py:278-281) followed by the HF
+ * sdpa consumer.  workspace (>= innerq_decode_attn_workspace bytes, 16-byte
+ * aligned) holds the split partials.  out [B][Hq][D] dtype with strides
+ * (o_sb, o_sh); lse (nullable, [B][Hq] fp32) receives log2-sum-exp2 of the
+ * scaled logits.
+ */
+int innerq_decode_attn(const innerq_attn_args* args, void* workspace, int64_t workspace_bytes,
+                       void* out, int64_t o_sb, int64_t o_sh, float* lse, void* stream);
+
+/*
+ * Partials only: part_o [B][Hq][n_splits][D] fp32 (unnormalised), part_m and
+ * part_l [B][Hq][n_splits] (log2-domain running max and sum).  For context
+ * sharding across GPUs: gather the partials, then innerq_lse_merge.
+ */
+int innerq_decode_attn_partials(const innerq_attn_args* args, float* part_o, float* part_m,
+                                float* part_l, void* stream);
+
+/* Merge split partials: out[row] = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s,
+ * rows = B * rows_per_b, out row (b, h) at b*o_sb + h*o_sh. */
+int innerq_lse_merge(const float* part_o, const float* part_m, const float* part_l, int B,
+                     int rows_per_b, int n_splits, int D, int dtype, void* out, int64_t o_sb,
+                     int64_t o_sh, float* lse, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* INNERQ_B200_H */

@@ -1,0 +1,116 @@
+"""Fused decode attention over the packed InnerQ cache (host side).
+
+``decode_attention`` is the consumer half of the hot path: for one query
+token per sequence it computes ``softmax(q K^T * scale) V`` over
+``[sink | packed middle | recent]`` directly from the packed store, in place
+of the reference's full dequantize (``src/innerq/cache.py:278-281``) followed
+by Hugging Face sdpa with ``repeat_kv``.  Split-KV partials are merged with a
+log-sum-exp merge; ``decode_attention_partials`` + ``lse_merge`` expose the
+two halves for context sharding across GPUs.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+
+from . import _lib
+from .store import PackedSide, dtype_code, require_cuda, stream_ptr
+
+_WORKSPACE: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.type, device.index)
+    t = _WORKSPACE.get(key)
+    if t is None or t.numel() < nbytes:
+        t = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WORKSPACE[key] = t
+    return t
+
+
+def _q3(q: torch.Tensor) -> torch.Tensor:
+    if q.dim() == 4:
+        if q.shape[2] != 1:
+            raise ValueError("decode attention takes one query token per sequence")
+        q = q[:, :, 0]
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    return q
+
+
+def build_args(q: torch.Tensor, k: PackedSide, v: PackedSide, scale: float | None = None,
+               n_splits: int = 0, tile_range: tuple[int, int] | None = None) -> _lib.AttnArgs:
+    require_cuda(q, "query")
+    q = _q3(q)
+    B, Hq, D = q.shape
+    if q.dtype != k.dtype:
+        raise TypeError(f"query dtype {q.dtype} != cache dtype {k.dtype}")
+    a = _lib.AttnArgs()
+    a.struct_size = C.sizeof(_lib.AttnArgs)
+    a.dtype = dtype_code(q.dtype)
+    a.B, a.Hq, a.Hkv, a.D = B, Hq, k.H, D
+    a.q = q.data_ptr()
+    a.q_sb, a.q_sh = q.stride(0), q.stride(1)
+    a.key_norm = k.norm_f.data_ptr() if (k.normalize and k.norm_f is not None and k.n_q) else None
+    a.k = k.side_struct()
+    a.v = v.side_struct()
+    a.softmax_scale = float(scale if scale is not None else 1.0 / math.sqrt(D))
+    a.n_splits = int(n_splits)
+    if tile_range is not None:
+        a.tile_lo, a.tile_hi = tile_range
+    a._keep = q  # keep a contiguous copy alive for the launch
+    return a
+
+
+def plan(args: _lib.AttnArgs) -> tuple[int, int]:
+    nt, ns = C.c_int32(), C.c_int32()
+    _lib.call("innerq_attn_plan", C.byref(args), C.byref(nt), C.byref(ns))
+    return nt.value, ns.value
+
+
+def decode_attention(q: torch.Tensor, k: PackedSide, v: PackedSide, scale: float | None = None,
+                     n_splits: int = 0, out: torch.Tensor | None = None,
+                     lse: torch.Tensor | None = None) -> torch.Tensor:
+    """out [B, Hq, D] in the query dtype."""
+    args = build_args(q, k, v, scale, n_splits)
+    ws_bytes = _lib.load().innerq_decode_attn_workspace(C.byref(args))
+    if ws_bytes < 0:
+        raise _lib.InnerqError("innerq_decode_attn_workspace", -1, _lib.last_error())
+    ws = _workspace(q.device, ws_bytes)
+    if out is None:
+        out = torch.empty((args.B, args.Hq, args.D), dtype=q.dtype, device=q.device)
+    _lib.call("innerq_decode_attn", C.byref(args), ws.data_ptr(), ws.numel(), out.data_ptr(),
+              out.stride(0), out.stride(1), None if lse is None else lse.data_ptr(),
+              stream_ptr(q.device))
+    return out
+
+
+def decode_attention_partials(q: torch.Tensor, k: PackedSide, v: PackedSide,
+                              scale: float | None = None, n_splits: int = 0,
+                              tile_range: tuple[int, int] | None = None):
+    """Split partials (o [B,Hq,S,D] fp32 unnormalised, m, l [B,Hq,S] log2 domain)."""
+    args = build_args(q, k, v, scale, n_splits, tile_range)
+    _, ns = plan(args)
+    B, Hq, D = args.B, args.Hq, args.D
+    po = torch.empty((B, Hq, ns, D), dtype=torch.float32, device=q.device)
+    pm = torch.empty((B, Hq, ns), dtype=torch.float32, device=q.device)
+    pl = torch.empty((B, Hq, ns), dtype=torch.float32, device=q.device)
+    _lib.call("innerq_decode_attn_partials", C.byref(args), po.data_ptr(), pm.data_ptr(),
+              pl.data_ptr(), stream_ptr(q.device))
+    return po, pm, pl
+
+
+def lse_merge(po: torch.Tensor, pm: torch.Tensor, pl: torch.Tensor, dtype: torch.dtype,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge split partials along dim 2 into out [B, Hq, D] of dtype."""
+    require_cuda(po, "partials")
+    po, pm, pl = po.contiguous(), pm.contiguous(), pl.contiguous()
+    B, Hq, ns, D = po.shape
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=dtype, device=po.device)
+    _lib.call("innerq_lse_merge", po.data_ptr(), pm.data_ptr(), pl.data_ptr(), B, Hq, ns, D,
+              dtype_code(dtype), out.data_ptr(), out.stride(0), out.stride(1), None,
+              stream_ptr(po.device))
+    return out

@@ -1,0 +1,274 @@
+"""Drop-in for ``innerq.cache`` (``src/innerq/cache.py`` of mthcom/innerq) on B200.
+
+``InnerqDynamicLayer`` keeps the reference constructor, the 15 config
+attributes with the same defaults (``cache.py:70-119``), the prefill / flush
+semantics and the Hugging Face ``CacheLayerMixin`` protocol
+(``update`` / ``get_seq_length`` / ``get_mask_sizes`` ...), but stores the
+quantized middle packed on the GPU (``innerq_b200.store.PackedSide``) and
+appends with the quantize-and-pack kernel instead of ``torch.cat``.
+
+``update`` returns what the reference returns: the raw K/V on the prefill
+call (``cache.py:390-392``) and, on decode calls, the full dequantized
+``[sink | middle | recent]`` K/V in the model dtype, bit-exact with the
+reference's ``get_deq_tensors`` (``cache.py:278-281``).  When the layer is
+driven by the ``"innerq"`` attention function (``innerq_b200.models``), the
+decode call skips that materialisation and the attention kernel reads the
+packed store directly.
+
+The reference-format attributes (``keys_q``, ``keys_scale_factor``,
+``keys_zp_sign``, ``keys_sink``, ``keys_recent``,
+``key_normalization_factor`` and the ``values_*`` ones) are computed on
+access.  Signs read back from the packed store are 0 where the code is 0
+(codes x signs is bit-exact; the sign of a value that quantized to 0 is not
+stored).
+"""
+from __future__ import annotations
+
+from collections.abc import Iterable
+from typing import Any
+
+import torch
+from transformers.cache_utils import Cache, CacheLayerMixin
+
+from . import _lib
+from .quant import QMode
+from .store import PackedSide
+
+
+class InnerqDynamicLayer(CacheLayerMixin):
+    """cache.py:61-419."""
+    is_sliding = False
+
+    def __init__(self, config, layer_idx):
+        self.parse_config(config)
+        self.layer_idx = layer_idx
+        self.cumulative_length = 0
+        self.fused = bool(getattr(config, "_attn_implementation", None) == "innerq")
+        super().__init__()
+
+    # cache.py:70-119
+    def parse_config(self, config):
+        self.key_bits = getattr(config, 'k_bits', 16)
+        self.value_bits = getattr(config, 'v_bits', 16)
+        self.key_quantize = False if self.key_bits >= 16 else True
+        self.value_quantize = False if self.value_bits >= 16 else True
+
+        self.key_group_size = getattr(config, 'key_group_size', 32)
+        self.value_group_size = getattr(config, 'value_group_size', 32)
+        self.key_w_recent = getattr(config, 'key_w_recent', 32)
+        self.value_w_recent = getattr(config, 'value_w_recent', 32)
+        self.key_w_sink = getattr(config, 'key_w_sink', 0)
+        self.value_w_sink = getattr(config, 'value_w_sink', 0)
+        self.key_flush_size = getattr(config, 'key_flush_size', 32)
+        self.value_flush_size = getattr(config, 'value_flush_size', 32)
+        self.key_normalize = getattr(config, 'key_normalize', False)
+
+        self.key_quantize_over_token = getattr(config, 'key_quantize_over_token', False)
+        self.value_quantize_over_token = getattr(config, 'value_quantize_over_token', True)
+
+        self.key_quantize_mode = QMode.from_str(getattr(config, 'key_quantize_mode', 'symmetric'))
+        self.value_quantize_mode = QMode.from_str(getattr(config, 'value_quantize_mode', 'symmetric'))
+
+        for name, m, on in (("key", self.key_quantize_mode, self.key_quantize),
+                            ("value", self.value_quantize_mode, self.value_quantize)):
+            if on and m == QMode.HYBRID:
+                raise NotImplementedError(f"{name}_quantize_mode='hybrid' is not built in the packed store")
+
+        def mode(m):
+            return _lib.ASYM if m == QMode.ASYM else _lib.SYM
+
+        self._k = PackedSide(_lib.ROLE_K, self.key_bits, self.key_group_size, mode(self.key_quantize_mode),
+                             self.key_quantize_over_token, self.key_w_sink, self.key_w_recent,
+                             self.key_flush_size, normalize=bool(self.key_normalize) and self.key_quantize)
+        self._v = PackedSide(_lib.ROLE_V, self.value_bits, self.value_group_size,
+                             mode(self.value_quantize_mode), self.value_quantize_over_token,
+                             self.value_w_sink, self.value_w_recent, self.value_flush_size)
+
+    # ----------------------------------------------- reference-format views
+    @property
+    def key_normalization_factor(self):
+        f = self._k.norm_f
+        return None if f is None else f.unsqueeze(2)
+
+    @property
+    def keys_sink(self):
+        return self._k.sink
+
+    @property
+    def values_sink(self):
+        return self._v.sink
+
+    @property
+    def keys_recent(self):
+        return self._k.recent
+
+    @property
+    def values_recent(self):
+        return self._v.recent
+
+    def _kviews(self):
+        return self._k.ref_views()
+
+    def _vviews(self):
+        return self._v.ref_views()
+
+    @property
+    def keys_q(self):
+        return self._kviews()[0]
+
+    @property
+    def keys_scale_factor(self):
+        return self._kviews()[1]
+
+    @property
+    def keys_zp_sign(self):
+        return self._kviews()[2]
+
+    @property
+    def values_q(self):
+        return self._vviews()[0]
+
+    @property
+    def values_scale_factor(self):
+        return self._vviews()[1]
+
+    @property
+    def values_zp_sign(self):
+        return self._vviews()[2]
+
+    @property
+    def key_side(self) -> PackedSide:
+        return self._k
+
+    @property
+    def value_side(self) -> PackedSide:
+        return self._v
+
+    # ------------------------------------------------------------- protocol
+    def lazy_initialization(self, key_states: torch.Tensor, value_states: torch.Tensor) -> None:
+        """cache.py:226-233."""
+        self.dtype, self.device = key_states.dtype, key_states.device
+        self._k.prefill(key_states)
+        self._v.prefill(value_states)
+        self.is_initialized = True
+
+    def add_to_cache(self, key_states: torch.Tensor, value_states: torch.Tensor) -> None:
+        """cache.py:367-380."""
+        self._k.append(key_states)
+        self._v.append(value_states)
+
+    def get_deq_tensors(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """cache.py:278-281, materialised by the dequant kernel."""
+        return self._k.materialize(), self._v.materialize()
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor,
+               cache_kwargs: dict[str, Any] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """cache.py:382-396."""
+        self.cumulative_length += key_states.shape[-2]
+        if not self.is_initialized:
+            self.lazy_initialization(key_states, value_states)
+            return key_states, value_states
+        self.add_to_cache(key_states, value_states)
+        if self.fused and key_states.shape[-2] == 1:
+            # the "innerq" attention function reads the packed store
+            key_states._innerq_layer = self
+            return key_states, value_states
+        return self.get_deq_tensors()
+
+    def attend(self, query: torch.Tensor, scaling: float | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """Fused decode attention of query [B, Hq, 1, D] over this layer."""
+        from .attention import decode_attention
+        return decode_attention(query, self._k, self._v, scaling, out=out)
+
+    def get_mask_sizes(self, cache_position) -> tuple[int, int]:
+        """cache.py:398-402; also takes the int query_length of transformers >= 5.5."""
+        kv_offset = 0
+        query_length = cache_position if isinstance(cache_position, int) else cache_position.shape[0]
+        kv_length = self.get_seq_length() + query_length
+        return kv_length, kv_offset
+
+    def get_seq_length(self) -> int:
+        return self.cumulative_length
+
+    def get_max_cache_shape(self) -> int:
+        return -1
+
+    def crop(self, max_length: int) -> None:
+        raise ValueError('This function is not implementable for quantized cache. It leads to the '
+                         'loss of accuracy on the recent tokens')
+
+    def batch_repeat_interleave(self, repeats: int) -> None:
+        raise Exception('This function is not implemented yet.')
+
+    def batch_select_indices(self, indices: torch.Tensor) -> None:
+        raise Exception('This function is not implemented yet.')
+
+
+class InnerqDynamicSlidingWindowLayer(InnerqDynamicLayer):
+    """cache.py:421-461.  The reference crops with ``[:, :, -window, :]``
+    (``cache.py:443-444``), which keeps a single token and drops a dim; this
+    layer crops to the last ``window`` tokens, which is what the surrounding
+    code intends.  The fused path is not used for sliding layers."""
+    is_sliding = True
+
+    def __init__(self, config, layer_idx: int, sliding_window: int):
+        super().__init__(config, layer_idx)
+        self.fused = False
+        self.sliding_window = sliding_window
+        self.cumulative_length = 0
+        self._sliding_window_tensor = torch.tensor(self.sliding_window, dtype=torch.long)
+
+    def lazy_initialization(self, key_states, value_states) -> None:
+        super().lazy_initialization(key_states, value_states)
+        self._sliding_window_tensor = self._sliding_window_tensor.to(self.device)
+
+    def update(self, key_states, value_states, cache_kwargs=None):
+        k, v = super().update(key_states, value_states, cache_kwargs)
+        if self.cumulative_length - key_states.shape[-2] > self.sliding_window:
+            k = k[:, :, -self.sliding_window:, :]
+            v = v[:, :, -self.sliding_window:, :]
+        return k, v
+
+    def get_mask_sizes(self, cache_position) -> tuple[int, int]:
+        query_length = cache_position if isinstance(cache_position, int) else cache_position.shape[0]
+        is_full = self.cumulative_length >= self.sliding_window
+        kv_offset = max(self.cumulative_length - self.sliding_window + 1, 0)
+        if is_full:
+            kv_length = self.sliding_window - 1 + query_length
+        else:
+            kv_length = self.cumulative_length + query_length
+        return kv_length, kv_offset
+
+    def get_max_cache_shape(self) -> int:
+        return self.sliding_window
+
+
+class DynamicCache(Cache):
+    """cache.py:463-496: one layer per decoder layer, sliding or full."""
+
+    def __init__(self, ddp_cache_data: Iterable[tuple[torch.Tensor | None, ...]] | None = None,
+                 config=None, offloading: bool = False, offload_only_non_sliding: bool = False):
+        layers = []
+        if config is not None:
+            decoder_config = config.get_text_config(decoder=True)
+            sliding_window = getattr(decoder_config, "sliding_window", None) or getattr(
+                decoder_config, "attention_chunk_size", None)
+            layer_types = getattr(decoder_config, "layer_types", None)
+            if layer_types is None:
+                layer_types = ["sliding_attention" if sliding_window is not None else "full_attention"
+                               for _ in range(decoder_config.num_hidden_layers)]
+            if hasattr(decoder_config, "num_kv_shared_layers"):
+                layer_types = layer_types[: -decoder_config.num_kv_shared_layers]
+            for layer_idx, layer_type in enumerate(layer_types):
+                if layer_type in ("sliding_attention", "chunked_attention"):
+                    layers.append(InnerqDynamicSlidingWindowLayer(config=config, layer_idx=layer_idx,
+                                                                  sliding_window=sliding_window))
+                else:
+                    layers.append(InnerqDynamicLayer(config=config, layer_idx=layer_idx))
+        super().__init__(layers=layers, offloading=offloading,
+                         offload_only_non_sliding=offload_only_non_sliding)
+
+    def __iter__(self):
+        for layer in self.layers:
+            yield layer.keys, layer.values, getattr(layer, "_sliding_window_tensor", None)

@@ -1,0 +1,318 @@
+// C-ABI entry points of libinnerq_b200.so (declared in include/innerq_b200.h):
+// argument validation, split-KV planning and kernel dispatch.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/innerq_b200.h"
+#include "decode_attn.cuh"
+#include "innerq_internal.h"
+
+using namespace innerq;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return INNERQ_OK;
+  if (e == cudaErrorNotSupported)
+    return fail(INNERQ_ERR_UNSUPPORTED, "%s: combination not supported", what);
+  return fail(INNERQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, int n) { return ((uintptr_t)p % n) == 0; }
+
+int check_common(int dtype, int D, int bits, int group, int mode, int role, int over_token) {
+  if (dtype != INNERQ_DT_F16 && dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype %d", dtype);
+  if (D != kD) return fail(INNERQ_ERR_UNSUPPORTED, "head_dim %d (only 128 is built)", D);
+  if (bits < 2 || bits > 4) return fail(INNERQ_ERR_UNSUPPORTED, "bits %d (2, 3, 4 are built)", bits);
+  if (mode != INNERQ_SYM && mode != INNERQ_ASYM) return fail(INNERQ_ERR_ARG, "mode %d", mode);
+  if (group != 32 && group != 64 && group != 128)
+    return fail(INNERQ_ERR_UNSUPPORTED, "group size %d (32, 64, 128 are built)", group);
+  if (role == INNERQ_ROLE_K && over_token)
+    return fail(INNERQ_ERR_UNSUPPORTED, "keys grouped over tokens are not built");
+  if (role == INNERQ_ROLE_V && !over_token)
+    return fail(INNERQ_ERR_UNSUPPORTED, "values grouped over channels are not built");
+  if (role != INNERQ_ROLE_K && role != INNERQ_ROLE_V) return fail(INNERQ_ERR_ARG, "role %d", role);
+  return INNERQ_OK;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+struct Plan {
+  int S, t_first, n_tiles, tile_lo, tile_hi, n_splits, tps, R, bk, bv;
+};
+
+int check_side(const innerq_side& s, int dtype, int role, const char* name) {
+  if (s.n_sink < 0 || s.n_q < 0 || s.n_recent < 0) return fail(INNERQ_ERR_ARG, "%s: negative count", name);
+  if (s.n_q > 0) {
+    int rc = check_common(dtype, kD, s.bits, s.group, s.mode, role, s.over_token);
+    if (rc) return rc;
+    if (!s.codes || !s.scale || (s.mode == INNERQ_ASYM && !s.zero))
+      return fail(INNERQ_ERR_ARG, "%s: missing store pointer", name);
+    if (!aligned(s.codes, 16) || !aligned(s.scale, 16) || (s.zero && !aligned(s.zero, 16)))
+      return fail(INNERQ_ERR_ARG, "%s: store pointers must be 16-byte aligned", name);
+    if ((int64_t)s.n_q > s.cap_tiles * 32) return fail(INNERQ_ERR_ARG, "%s: n_q beyond capacity", name);
+    if (role == INNERQ_ROLE_V && s.n_q % 32) return fail(INNERQ_ERR_ARG, "%s: n_q %% 32", name);
+  }
+  if (s.n_sink > 0 && (!s.sink || !aligned(s.sink, 4) || (s.sink_st % 2) || (s.sink_sh % 2) || (s.sink_sb % 2)))
+    return fail(INNERQ_ERR_ARG, "%s: sink pointer / strides must be 4-byte aligned", name);
+  if (s.n_recent > 0 && (!s.recent || !aligned(s.recent, 4) || (s.rec_st % 2) || (s.rec_sh % 2) || (s.rec_sb % 2)))
+    return fail(INNERQ_ERR_ARG, "%s: recent pointer / strides must be 4-byte aligned", name);
+  return INNERQ_OK;
+}
+
+int make_plan(const innerq_attn_args* a, Plan& p) {
+  if (!a) return fail(INNERQ_ERR_ARG, "null args");
+  if (a->struct_size != (int32_t)sizeof(innerq_attn_args))
+    return fail(INNERQ_ERR_ARG, "struct_size %d != %d (ABI mismatch)", a->struct_size, (int)sizeof(innerq_attn_args));
+  if (a->dtype != INNERQ_DT_F16 && a->dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype");
+  if (a->D != kD) return fail(INNERQ_ERR_UNSUPPORTED, "head_dim %d (only 128 is built)", a->D);
+  if (a->B <= 0 || a->Hkv <= 0 || a->Hq <= 0 || a->Hq % a->Hkv) return fail(INNERQ_ERR_ARG, "head counts");
+  p.R = a->Hq / a->Hkv;
+  if (p.R != 1 && p.R != 2 && p.R != 4 && p.R != 8)
+    return fail(INNERQ_ERR_UNSUPPORTED, "GQA ratio %d (1, 2, 4, 8 are built)", p.R);
+  if (!a->q) return fail(INNERQ_ERR_ARG, "q is null");
+  int rc = check_side(a->k, a->dtype, INNERQ_ROLE_K, "k");
+  if (rc) return rc;
+  rc = check_side(a->v, a->dtype, INNERQ_ROLE_V, "v");
+  if (rc) return rc;
+  const int64_t Sk = (int64_t)a->k.n_sink + a->k.n_q + a->k.n_recent;
+  const int64_t Sv = (int64_t)a->v.n_sink + a->v.n_q + a->v.n_recent;
+  if (Sk != Sv) return fail(INNERQ_ERR_ARG, "K holds %lld tokens, V holds %lld", (long long)Sk, (long long)Sv);
+  if (Sk > (1ll << 30)) return fail(INNERQ_ERR_ARG, "context too long");
+  p.S = (int)Sk;
+  const int vs = a->v.n_sink;
+  p.t_first = a->v.n_q > 0 ? vs - 32 * ((vs + 31) / 32) : 0;
+  p.n_tiles = (p.S - p.t_first + 31) / 32;
+  p.tile_lo = a->tile_lo, p.tile_hi = a->tile_hi;
+  if (p.tile_lo == 0 && p.tile_hi == 0) p.tile_hi = p.n_tiles;
+  if (p.tile_lo < 0 || p.tile_hi > p.n_tiles || p.tile_lo > p.tile_hi)
+    return fail(INNERQ_ERR_ARG, "tile range [%d, %d) outside [0, %d)", p.tile_lo, p.tile_hi, p.n_tiles);
+  const int ntr = p.tile_hi - p.tile_lo;
+  int splits = a->n_splits;
+  if (splits <= 0) {
+    const int bh = a->B * a->Hkv;
+    const int slots = sm_count() * (p.R == 8 ? 2 : 3);
+    splits = (8 * slots + bh - 1) / bh;
+    splits = splits < 1 ? 1 : splits;
+    const int max_by_work = ntr / 8 > 1 ? ntr / 8 : 1;
+    if (splits > max_by_work) splits = max_by_work;
+  }
+  if (splits > 65535) splits = 65535;
+  p.tps = ntr > 0 ? (ntr + splits - 1) / splits : 1;
+  p.n_splits = ntr > 0 ? (ntr + p.tps - 1) / p.tps : 1;
+  p.bk = a->k.n_q > 0 ? a->k.bits : 4;
+  p.bv = a->v.n_q > 0 ? a->v.bits : 4;
+  return INNERQ_OK;
+}
+
+DevSide dev_side(const innerq_side& s) {
+  DevSide d;
+  d.codes = (const uint8_t*)s.codes;
+  d.scale = (const uint16_t*)s.scale;
+  d.zero = (const uint16_t*)s.zero;
+  d.cap_tiles = s.cap_tiles;
+  d.sink = (const uint16_t*)s.sink;
+  d.sk_b = s.sink_sb; d.sk_h = s.sink_sh; d.sk_t = s.sink_st;
+  d.rec = (const uint16_t*)s.recent;
+  d.rc_b = s.rec_sb; d.rc_h = s.rec_sh; d.rc_t = s.rec_st;
+  d.n_sink = s.n_sink; d.n_q = s.n_q; d.n_rec = s.n_recent;
+  d.group = s.n_q > 0 ? s.group : 32;
+  d.asym = s.n_q > 0 && s.mode == INNERQ_ASYM;
+  return d;
+}
+
+int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm, float* pl,
+                 cudaStream_t st) {
+  DevArgs d;
+  d.k = dev_side(a->k);
+  d.v = dev_side(a->v);
+  d.q = (const uint16_t*)a->q;
+  d.q_b = a->q_sb;
+  d.q_h = a->q_sh;
+  d.kf = (const uint16_t*)a->key_norm;
+  d.B = a->B; d.Hq = a->Hq; d.Hkv = a->Hkv; d.S = p.S;
+  d.t_first = p.t_first;
+  d.tile_lo = p.tile_lo; d.tile_hi = p.tile_hi;
+  d.tiles_per_split = p.tps; d.n_splits = p.n_splits;
+  d.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  d.po = po; d.pm = pm; d.pl = pl;
+  dim3 grid(p.n_splits, a->Hkv, a->B);
+  cudaError_t e;
+  switch (p.bk) {
+    case 2: e = launch_attn_k2(d, p.bv, p.R, a->dtype, grid, st); break;
+    case 3: e = launch_attn_k3(d, p.bv, p.R, a->dtype, grid, st); break;
+    default: e = launch_attn_k4(d, p.bv, p.R, a->dtype, grid, st); break;
+  }
+  return cuda_status(e, "decode_attn");
+}
+
+int64_t ws_bytes(const innerq_attn_args* a, const Plan& p) {
+  const int64_t rows = (int64_t)a->B * a->Hq * p.n_splits;
+  return rows * kD * 4 + 2 * ((rows * 4 + 255) / 256 * 256);
+}
+
+}  // namespace
+
+extern "C" {
+
+int innerq_abi_version(void) { return INNERQ_ABI_VERSION; }
+const char* innerq_last_error(void) { return g_err; }
+int64_t innerq_tile_bytes(int bits) { return (bits >= 2 && bits <= 4) ? tile_bytes(bits) : -1; }
+
+int innerq_norm_factor(const void* x, int dtype, int B, int H, int T, int D, int64_t sb, int64_t sh,
+                       int64_t st, void* out_f, void* stream) {
+  if (dtype != INNERQ_DT_F16 && dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype");
+  if (D != kD) return fail(INNERQ_ERR_UNSUPPORTED, "head_dim %d", D);
+  if (B <= 0 || H <= 0 || T <= 0 || !x || !out_f) return fail(INNERQ_ERR_ARG, "empty input");
+  return cuda_status(launch_norm_factor(x, dtype, B, H, T, sb, sh, st, out_f, (cudaStream_t)stream),
+                     "norm_factor");
+}
+
+int innerq_quant_pack(const void* x, int dtype, int B, int H, int T, int D, int64_t sb, int64_t sh,
+                      int64_t st, int bits, int group, int mode, int role, int over_token,
+                      const void* norm_f, void* codes, void* scale, void* zero, int64_t cap_tiles,
+                      int64_t t_offset, void* stream) {
+  int rc = check_common(dtype, D, bits, group, mode, role, over_token);
+  if (rc) return rc;
+  if (B < 0 || H < 0 || T < 0 || t_offset < 0) return fail(INNERQ_ERR_ARG, "negative size");
+  if (B == 0 || H == 0 || T == 0) return INNERQ_OK;
+  if (!x || !codes || !scale || (mode == INNERQ_ASYM && !zero)) return fail(INNERQ_ERR_ARG, "null pointer");
+  if (!aligned(codes, 16) || !aligned(scale, 2)) return fail(INNERQ_ERR_ARG, "store alignment");
+  if (t_offset + T > cap_tiles * 32) return fail(INNERQ_ERR_ARG, "store capacity %lld tokens < %lld",
+                                                (long long)(cap_tiles * 32), (long long)(t_offset + T));
+  if (over_token) {
+    if (T % group || t_offset % group)
+      return fail(INNERQ_ERR_ARG, "token groups need T (%d) and t_offset (%lld) divisible by group %d", T,
+                  (long long)t_offset, group);
+  } else {
+    if (!aligned(x, 8) || (sb % 4) || (sh % 4) || (st % 4))
+      return fail(INNERQ_ERR_ARG, "channel-group input must be 8-byte aligned rows");
+  }
+  if (norm_f && over_token) return fail(INNERQ_ERR_UNSUPPORTED, "normalisation with token groups");
+  return cuda_status(launch_pack(x, dtype, B, H, T, sb, sh, st, bits, group, mode == INNERQ_ASYM,
+                                 role == INNERQ_ROLE_V, over_token, norm_f, codes, scale, zero,
+                                 cap_tiles, t_offset, (cudaStream_t)stream),
+                     "quant_pack");
+}
+
+int innerq_unpack_ref(const void* codes, const void* scale, const void* zero, int dtype, int B, int H,
+                      int64_t t_begin, int64_t n, int D, int bits, int group, int mode, int role,
+                      int over_token, int64_t cap_tiles, int32_t* out_codes, void* out_sign,
+                      void* out_scale, void* out_zero, void* stream) {
+  int rc = check_common(dtype, D, bits, group, mode, role, over_token);
+  if (rc) return rc;
+  if (n < 0 || t_begin < 0 || t_begin + n > cap_tiles * 32) return fail(INNERQ_ERR_ARG, "token range");
+  if (over_token && (t_begin % group || n % group)) return fail(INNERQ_ERR_ARG, "token-group range");
+  if (n == 0) return INNERQ_OK;
+  if (!codes || !scale || !out_codes || !out_scale || (mode == INNERQ_ASYM && !zero))
+    return fail(INNERQ_ERR_ARG, "null pointer");
+  return cuda_status(launch_unpack_ref(codes, scale, zero, dtype, B, H, n, bits, group,
+                                       mode == INNERQ_ASYM, role == INNERQ_ROLE_V, over_token,
+                                       cap_tiles, t_begin, out_codes, out_sign, out_scale, out_zero,
+                                       (cudaStream_t)stream),
+                     "unpack_ref");
+}
+
+int innerq_dequant(const void* codes, const void* scale, const void* zero, int dtype, int B, int H,
+                   int64_t t_begin, int64_t n, int D, int bits, int group, int mode, int role,
+                   int over_token, int64_t cap_tiles, const void* norm_f, void* out, int64_t ob,
+                   int64_t oh, int64_t ot, void* stream) {
+  int rc = check_common(dtype, D, bits, group, mode, role, over_token);
+  if (rc) return rc;
+  if (n < 0 || t_begin < 0 || t_begin + n > cap_tiles * 32) return fail(INNERQ_ERR_ARG, "token range");
+  if (n == 0) return INNERQ_OK;
+  if (!codes || !scale || !out || (mode == INNERQ_ASYM && !zero)) return fail(INNERQ_ERR_ARG, "null pointer");
+  return cuda_status(launch_dequant(codes, scale, zero, dtype, B, H, n, bits, group,
+                                    mode == INNERQ_ASYM, role == INNERQ_ROLE_V, over_token, cap_tiles,
+                                    t_begin, norm_f, out, ob, oh, ot, (cudaStream_t)stream),
+                     "dequant");
+}
+
+int innerq_dequant_ref(const int32_t* codes, const void* scale, const void* zp_or_sign, int dtype,
+                       int64_t n_outer, int T, int D, int group, int mode, int over_token, float* out,
+                       void* stream) {
+  if (dtype != INNERQ_DT_F16 && dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype");
+  if (mode != INNERQ_SYM && mode != INNERQ_ASYM) return fail(INNERQ_ERR_ARG, "mode");
+  if (n_outer < 0 || T < 0 || D <= 0 || group <= 0) return fail(INNERQ_ERR_ARG, "sizes");
+  if ((over_token ? T : D) % group) return fail(INNERQ_ERR_ARG, "group %d does not divide the grouped dim", group);
+  if (n_outer == 0 || T == 0) return INNERQ_OK;
+  if (!codes || !scale || !zp_or_sign || !out) return fail(INNERQ_ERR_ARG, "null pointer");
+  return cuda_status(launch_dequant_ref(codes, scale, zp_or_sign, dtype, n_outer, T, D, group,
+                                        mode == INNERQ_ASYM, over_token, out, (cudaStream_t)stream),
+                     "dequant_ref");
+}
+
+int innerq_attn_plan(const innerq_attn_args* args, int32_t* n_tiles, int32_t* n_splits) {
+  Plan p;
+  int rc = make_plan(args, p);
+  if (rc) return rc;
+  if (n_tiles) *n_tiles = p.n_tiles;
+  if (n_splits) *n_splits = p.n_splits;
+  return INNERQ_OK;
+}
+
+int64_t innerq_decode_attn_workspace(const innerq_attn_args* args) {
+  Plan p;
+  if (make_plan(args, p)) return -1;
+  return ws_bytes(args, p);
+}
+
+int innerq_decode_attn_partials(const innerq_attn_args* args, float* part_o, float* part_m,
+                                float* part_l, void* stream) {
+  Plan p;
+  int rc = make_plan(args, p);
+  if (rc) return rc;
+  if (!part_o || !part_m || !part_l) return fail(INNERQ_ERR_ARG, "null partials");
+  return run_partials(args, p, part_o, part_m, part_l, (cudaStream_t)stream);
+}
+
+int innerq_decode_attn(const innerq_attn_args* args, void* workspace, int64_t workspace_bytes,
+                       void* out, int64_t o_sb, int64_t o_sh, float* lse, void* stream) {
+  Plan p;
+  int rc = make_plan(args, p);
+  if (rc) return rc;
+  if (!out) return fail(INNERQ_ERR_ARG, "out is null");
+  const int64_t need = ws_bytes(args, p);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
+    return fail(INNERQ_ERR_ARG, "workspace %lld bytes < %lld needed (or misaligned)",
+                (long long)workspace_bytes, (long long)need);
+  const int64_t rows = (int64_t)args->B * args->Hq * p.n_splits;
+  float* po = (float*)workspace;
+  float* pm = po + rows * kD;
+  float* pl = (float*)((char*)pm + (rows * 4 + 255) / 256 * 256);
+  rc = run_partials(args, p, po, pm, pl, (cudaStream_t)stream);
+  if (rc) return rc;
+  return cuda_status(launch_lse_merge(po, pm, pl, args->B * args->Hq, args->Hq, p.n_splits,
+                                      args->dtype, out, o_sb, o_sh, lse, (cudaStream_t)stream),
+                     "lse_merge");
+}
+
+int innerq_lse_merge(const float* part_o, const float* part_m, const float* part_l, int B,
+                     int rows_per_b, int n_splits, int D, int dtype, void* out, int64_t o_sb,
+                     int64_t o_sh, float* lse, void* stream) {
+  if (D != kD) return fail(INNERQ_ERR_UNSUPPORTED, "head_dim %d", D);
+  if (dtype != INNERQ_DT_F16 && dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype");
+  if (B < 0 || rows_per_b < 0 || n_splits <= 0) return fail(INNERQ_ERR_ARG, "sizes");
+  if (!part_o || !part_m || !part_l || !out) return fail(INNERQ_ERR_ARG, "null pointer");
+  return cuda_status(launch_lse_merge(part_o, part_m, part_l, B * rows_per_b, rows_per_b, n_splits,
+                                      dtype, out, o_sb, o_sh, lse, (cudaStream_t)stream),
+                     "lse_merge");
+}
+
+}  // extern "C"

@@ -1,0 +1,34 @@
+// Internal launcher declarations shared by the C-ABI layer (capi.cu) and the
+// kernel translation units.  Not part of the public ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace innerq {
+struct DevArgs;
+
+cudaError_t launch_norm_factor(const void* x, int dt, int B, int H, int T, int64_t sb, int64_t sh,
+                               int64_t st, void* f, cudaStream_t s);
+cudaError_t launch_pack(const void* x, int dt, int B, int H, int T, int64_t sb, int64_t sh,
+                        int64_t st, int bits, int group, int asym, int role_v, int over_token,
+                        const void* nf, void* codes, void* scale, void* zero, int64_t cap_tiles,
+                        int64_t t_off, cudaStream_t s);
+cudaError_t launch_unpack_ref(const void* codes, const void* scale, const void* zero, int dt, int B,
+                              int H, int64_t n, int bits, int group, int asym, int role_v,
+                              int over_token, int64_t cap_tiles, int64_t t_begin, int32_t* oc,
+                              void* os, void* osc, void* oz, cudaStream_t s);
+cudaError_t launch_dequant(const void* codes, const void* scale, const void* zero, int dt, int B,
+                           int H, int64_t n, int bits, int group, int asym, int role_v,
+                           int over_token, int64_t cap_tiles, int64_t t_begin, const void* nf,
+                           void* out, int64_t ob, int64_t oh, int64_t ot, cudaStream_t s);
+cudaError_t launch_lse_merge(const float* po, const float* pm, const float* pl, int rows,
+                             int rows_per_b, int n_splits, int dt, void* out, int64_t o_b,
+                             int64_t o_h, float* lse, cudaStream_t s);
+cudaError_t launch_dequant_ref(const int32_t* c, const void* s, const void* zs, int dt, int64_t n_outer,
+                               int T, int D, int group, int asym, int over_token, float* out,
+                               cudaStream_t st);
+// decode attention, one translation unit per K bit width
+cudaError_t launch_attn_k2(const DevArgs& a, int bv, int R, int dt, dim3 grid, cudaStream_t s);
+cudaError_t launch_attn_k3(const DevArgs& a, int bv, int R, int dt, dim3 grid, cudaStream_t s);
+cudaError_t launch_attn_k4(const DevArgs& a, int bv, int R, int dt, dim3 grid, cudaStream_t s);
+}  // namespace innerq

@@ -1,0 +1,466 @@
+// Cache-append quantize-and-pack, key normalisation factor, reference-format
+// unpack and dequantize kernels.
+//
+// Arithmetic follows quant.py of mthcom/innerq op by op, each op computed in
+// fp32 and rounded to the input dtype (fp16 or bf16, RNE), which is what a
+// torch fp16/bf16 op does:
+//   symmetric  (quant.py:95-111):  s = h(max|x| / (2^(b-1)-1)),
+//                                  c = rint(clamp(h(|x| / s), 0, 2^(b-1)-1))
+//   asymmetric (quant.py:58-73):   s = h(h(max-min) / (2^b-1)),
+//                                  c = rint(clamp(h(h(x-min) / s), 0, 2^b-1))
+// Division is the IEEE fp32 '/' (this file must not be built with fast math).
+// A group whose scale is 0 makes the reference divide 0/0 (NaN, stored as
+// INT32_MIN); the packed format stores code 0 there, which dequantizes to the
+// same value.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "innerq_internal.h"
+
+namespace innerq {
+
+template <int BITS>
+__device__ __forceinline__ int qmax_sym() { return (1 << (BITS - 1)) - 1; }
+
+__device__ __forceinline__ int code_of(float q, float qmax) {
+  if (q != q) return 0;  // NaN from a zero scale
+  return (int)rintf(fminf(fmaxf(q, 0.f), qmax));
+}
+
+// --------------------------------------------------------------------------
+// K normalisation factor (cache.py:124): f = sqrt(max_t |x|) per (b, h, d)
+// --------------------------------------------------------------------------
+template <int DT>
+__global__ void norm_factor_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh,
+                                   int64_t st, int H, int T, uint16_t* __restrict__ f) {
+  const int bh = blockIdx.x, b = bh / H, h = bh % H, d = threadIdx.x;
+  const uint16_t* p = x + b * sb + h * sh + d;
+  float mx = 0.f;
+  for (int t = 0; t < T; ++t) mx = fmaxf(mx, fabsf(to_f<DT>(p[(int64_t)t * st])));
+  f[(int64_t)bh * kD + d] = from_f<DT>(sqrtf(mx));
+}
+
+// --------------------------------------------------------------------------
+// Row layout, channel groups (K): one warp per token row.
+// --------------------------------------------------------------------------
+template <int DT, int BITS>
+__global__ void __launch_bounds__(128)
+pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st,
+                        int H, int T, const uint16_t* __restrict__ nf, int group, int asym,
+                        uint8_t* __restrict__ codes, uint16_t* __restrict__ scale,
+                        uint16_t* __restrict__ zero, int64_t cap_tiles, int64_t t_off,
+                        int64_t n_rows) {
+  __shared__ uint8_t cbuf[4][kD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+  if (row >= n_rows) return;
+  const int t = (int)(row % T);
+  const int64_t bh = row / T;
+  const int h = (int)(bh % H), b = (int)(bh / H);
+  const uint16_t* xr = x + b * sb + h * sh + (int64_t)t * st + 4 * lane;
+  const uint2 raw = *reinterpret_cast<const uint2*>(xr);
+  float v[4] = {to_f<DT>(raw.x & 0xffff), to_f<DT>(raw.x >> 16), to_f<DT>(raw.y & 0xffff),
+                to_f<DT>(raw.y >> 16)};
+  if (nf) {  // cache.py:125 key_states / factor, in the dtype
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = rnd<DT>(v[i] / to_f<DT>(nf[bh * kD + 4 * lane + i]));
+  }
+  const int gl = group / 4;  // lanes per group
+  float s, z = 0.f;
+  int u[4];
+  if (!asym) {
+    float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    for (int o = 1; o < gl; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float qmax = (float)qmax_sym<BITS>();
+    s = rnd<DT>(mx / qmax);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = code_of(rnd<DT>(fabsf(v[i]) / s), qmax);
+      u[i] = (v[i] < 0.f ? -c : c) + (1 << (BITS - 1));
+    }
+  } else {
+    float mn = fminf(fminf(v[0], v[1]), fminf(v[2], v[3]));
+    float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+    for (int o = 1; o < gl; o <<= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    const float qmax = (float)((1 << BITS) - 1);
+    s = rnd<DT>(rnd<DT>(mx - mn) / qmax);
+    z = mn;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) u[i] = code_of(rnd<DT>(rnd<DT>(v[i] - mn) / s), qmax);
+  }
+  const int64_t p = t_off + t;
+  const int64_t ti = p >> 5;
+  const int r = (int)(p & 31);
+  const int ng = kD / group;
+  if (lane % gl == 0) {
+    const int g = lane / gl;
+    const int64_t si = (bh * cap_tiles + ti) * 32 * ng + row_scale_idx(r, g, ng);
+    scale[si] = from_f<DT>(s);
+    if (asym) zero[si] = from_f<DT>(z);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) cbuf[warp][4 * lane + i] = (uint8_t)u[i];
+  __syncwarp();
+  if (lane < 4) {
+    const int tq = lane;
+    uint32_t w[4] = {0, 0, 0, 0};
+    uint32_t wh = 0;
+    for (int c = 0; c < 32; ++c) {
+      const int kb = c >> 2, hi8 = (c >> 1) & 1, e = c & 1;
+      const uint32_t uc = cbuf[warp][kb * 16 + hi8 * 8 + 2 * tq + e];
+      if (BITS == 4) {
+        w[kb >> 1] |= uc << (4 * ((kb & 1) * 2 + hi8 + 4 * e));
+      } else {
+        w[kb >> 2] |= (uc & 3u) << (2 * ((kb & 3) * 2 + hi8 + 8 * e));
+        if (BITS == 3) wh |= (uc >> 2) << (kb * 2 + hi8 + 16 * e);
+      }
+    }
+    uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
+    const int lane2 = (r & 7) * 4 + tq, j = r >> 3;
+    if (BITS == 4) {
+      *reinterpret_cast<uint4*>(tb + lane2 * 64 + j * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      *reinterpret_cast<uint2*>(tb + lane2 * 32 + j * 8) = make_uint2(w[0], w[1]);
+      if (BITS == 3) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = wh;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Col layout, token groups (V): one CTA of 128 threads (one per dim) per
+// group of `group` tokens.
+// --------------------------------------------------------------------------
+template <int DT, int BITS>
+__global__ void __launch_bounds__(128)
+pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st,
+                      int group, int asym, uint8_t* __restrict__ codes,
+                      uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
+                      int64_t cap_tiles, int64_t t_off) {
+  __shared__ uint8_t cb[128][kD];
+  const int gi = blockIdx.x, h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
+  const int64_t bh = (int64_t)b * H + h;
+  const int d = threadIdx.x;
+  const uint16_t* xp = x + b * sb + h * sh + (int64_t)gi * group * st + d;
+  float s, z = 0.f;
+  if (!asym) {
+    float mx = 0.f;
+    for (int t = 0; t < group; ++t) mx = fmaxf(mx, fabsf(to_f<DT>(xp[(int64_t)t * st])));
+    const float qmax = (float)qmax_sym<BITS>();
+    s = rnd<DT>(mx / qmax);
+    for (int t = 0; t < group; ++t) {
+      const float v = to_f<DT>(xp[(int64_t)t * st]);
+      const int c = code_of(rnd<DT>(fabsf(v) / s), qmax);
+      cb[t][d] = (uint8_t)((v < 0.f ? -c : c) + (1 << (BITS - 1)));
+    }
+  } else {
+    float mn = INFINITY, mx = -INFINITY;
+    for (int t = 0; t < group; ++t) {
+      const float v = to_f<DT>(xp[(int64_t)t * st]);
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
+    const float qmax = (float)((1 << BITS) - 1);
+    s = rnd<DT>(rnd<DT>(mx - mn) / qmax);
+    z = mn;
+    for (int t = 0; t < group; ++t) {
+      const float v = to_f<DT>(xp[(int64_t)t * st]);
+      cb[t][d] = (uint8_t)code_of(rnd<DT>(rnd<DT>(v - mn) / s), qmax);
+    }
+  }
+  const int64_t groups_cap = cap_tiles * 32 / group;
+  const int64_t gglob = (t_off + (int64_t)gi * group) / group;
+  const int64_t si = (bh * groups_cap + gglob) * kD + col_scale_idx(d);
+  scale[si] = from_f<DT>(s);
+  if (asym) zero[si] = from_f<DT>(z);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
+  for (int tile = warp; tile < group / 32; tile += 4) {
+    uint32_t w[16];
+    uint32_t wh[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = 0;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int hi8 = 0; hi8 < 2; ++hi8)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int dd = mt * 16 + hh * 8 + gid;
+              const int r = kb * 16 + hi8 * 8 + 2 * tq + e;
+              const uint32_t uc = cb[tile * 32 + r][dd];
+              if (BITS == 4) {
+                w[mt * 2 + hh] |= uc << (4 * (kb * 2 + hi8 + 4 * e));
+              } else {
+                w[mt] |= (uc & 3u) << (2 * (hh * 4 + kb * 2 + hi8 + 8 * e));
+                if (BITS == 3)
+                  wh[mt >> 1] |= (uc >> 2) << ((mt & 1) * 8 + hh * 4 + kb * 2 + hi8 + 16 * e);
+              }
+            }
+    const int64_t ti = (t_off + (int64_t)gi * group) / 32 + tile;
+    uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
+    if (BITS == 4) {
+      uint4* o = reinterpret_cast<uint4*>(tb + lane * 64);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    } else {
+      uint4* o = reinterpret_cast<uint4*>(tb + lane * 32);
+      o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      if (BITS == 3)
+        *reinterpret_cast<uint4*>(tb + 1024 + lane * 16) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Code extraction at (packed token p, dim d) for either layout
+// --------------------------------------------------------------------------
+__device__ __forceinline__ int extract_code(const uint8_t* store_bh, int bits, int role_v,
+                                            int64_t p, int d) {
+  const int64_t ti = p >> 5;
+  const int r = (int)(p & 31);
+  const uint8_t* tb = store_bh + ti * tile_bytes(bits);
+  const BitPos bp = role_v ? col_pos(bits, r, d) : row_pos(bits, r, d);
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(tb + bp.off);
+  if (bits == 4) return (w >> bp.shift) & 15u;
+  int u = (w >> bp.shift) & 3u;
+  if (bits == 3) {
+    const uint32_t wh = *reinterpret_cast<const uint32_t*>(tb + bp.hoff);
+    u |= ((wh >> bp.hshift) & 1u) << 2;
+  }
+  return u;
+}
+
+// scale / zero element index of (packed token p, dim d) inside one (b,h) store
+__device__ __forceinline__ int64_t scale_index(int role_v, int over_token, int group,
+                                               int64_t cap_tiles, int64_t p, int d) {
+  if (!over_token) {  // channel groups: row-layout tiles
+    const int ng = kD / group;
+    return (p >> 5) * 32 * ng + row_scale_idx((int)(p & 31), d / group, ng);
+  }
+  return (p / group) * kD + col_scale_idx(d);
+}
+
+// Reference-format views (quant.py return values): int32 codes (magnitudes
+// for symmetric), fp16/bf16 signs, and scale / zero point tensors.
+template <int DT>
+__global__ void unpack_ref_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__ scale,
+                                  const uint16_t* __restrict__ zero, int H, int64_t n, int bits,
+                                  int group, int asym, int role_v, int over_token, int64_t cap_tiles,
+                                  int64_t t_begin, int32_t* __restrict__ oc, uint16_t* __restrict__ os,
+                                  uint16_t* __restrict__ osc, uint16_t* __restrict__ oz, int64_t total) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int d = (int)(i % kD);
+  const int64_t tn = (i / kD) % n;
+  const int64_t bh = i / (kD * n);
+  const int64_t p = t_begin + tn;
+  const int64_t groups_cap = cap_tiles * 32 / group;
+  const int64_t per_bh_scales = over_token ? groups_cap * kD : cap_tiles * 32 * (kD / group);
+  const int u = extract_code(codes + bh * cap_tiles * tile_bytes(bits), bits, role_v, p, d);
+  if (asym) {
+    oc[i] = u;
+  } else {
+    const int v = u - (1 << (bits - 1));
+    oc[i] = v < 0 ? -v : v;
+    if (os) os[i] = from_f<DT>(v > 0 ? 1.f : (v < 0 ? -1.f : 0.f));
+  }
+  const int64_t si = bh * per_bh_scales + scale_index(role_v, over_token, group, cap_tiles, p, d);
+  if (!over_token) {
+    if (d % group == 0) {
+      const int64_t o = (bh * n + tn) * (kD / group) + d / group;
+      osc[o] = scale[si];
+      if (asym && oz) oz[o] = zero[si];
+    }
+  } else if (tn % group == 0) {
+    const int64_t o = (bh * (n / group) + tn / group) * kD + d;
+    osc[o] = scale[si];
+    if (asym && oz) oz[o] = zero[si];
+  }
+}
+
+// Materialised dequantization in the model dtype, exactly as cache.py:241-281:
+// fp32(c)*fp32(s) (*sign | +zero) [*f], then cast to the dtype.
+template <int DT>
+__global__ void dequant_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__ scale,
+                               const uint16_t* __restrict__ zero, int H, int64_t n, int bits, int group,
+                               int asym, int role_v, int over_token, int64_t cap_tiles, int64_t t_begin,
+                               const uint16_t* __restrict__ nf, uint16_t* __restrict__ out, int64_t ob,
+                               int64_t oh, int64_t ot, int64_t total) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int d = (int)(i % kD);
+  const int64_t tn = (i / kD) % n;
+  const int64_t bh = i / (kD * n);
+  const int64_t p = t_begin + tn;
+  const int64_t groups_cap = cap_tiles * 32 / group;
+  const int64_t per_bh_scales = over_token ? groups_cap * kD : cap_tiles * 32 * (kD / group);
+  const int u = extract_code(codes + bh * cap_tiles * tile_bytes(bits), bits, role_v, p, d);
+  const int64_t si = bh * per_bh_scales + scale_index(role_v, over_token, group, cap_tiles, p, d);
+  const float s = to_f<DT>(scale[si]);
+  float val;
+  if (asym) {
+    val = (float)u * s + to_f<DT>(zero[si]);
+  } else {
+    val = (float)(u - (1 << (bits - 1))) * s;
+  }
+  if (nf) val = val * to_f<DT>(nf[bh * kD + d]);
+  const int b = (int)(bh / H), h = (int)(bh % H);
+  out[b * ob + h * oh + tn * ot + d] = from_f<DT>(val);
+}
+
+// --------------------------------------------------------------------------
+// Split-KV log-sum-exp merge: out = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s
+// --------------------------------------------------------------------------
+template <int DT>
+__global__ void lse_merge_kernel(const float* __restrict__ po, const float* __restrict__ pm,
+                                 const float* __restrict__ pl, int n_splits, int rows_per_b,
+                                 uint16_t* __restrict__ out, int64_t o_b, int64_t o_h,
+                                 float* __restrict__ lse_out) {
+  const int row = blockIdx.x, d = threadIdx.x;
+  const float* m = pm + (int64_t)row * n_splits;
+  const float* l = pl + (int64_t)row * n_splits;
+  float M = -INFINITY;
+  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, m[s]);
+  float num = 0.f, den = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < n_splits; ++s) {
+      const float w = m[s] == -INFINITY ? 0.f : exp2f(m[s] - M);
+      num += w * po[((int64_t)row * n_splits + s) * kD + d];
+      den += w * l[s];
+    }
+  }
+  const int b = row / rows_per_b, h = row % rows_per_b;
+  out[b * o_b + h * o_h + d] = from_f<DT>(den > 0.f ? num / den : 0.f);
+  if (lse_out && d == 0) lse_out[row] = den > 0.f ? M + log2f(den) : -INFINITY;
+}
+
+
+// Dequantize reference-format tensors (quant.py:83-93, 121-131): int32 codes,
+// dtype scale and dtype sign (symmetric) or zero point (asymmetric), fp32 out.
+template <int DT>
+__global__ void dequant_ref_kernel(const int32_t* __restrict__ c, const uint16_t* __restrict__ s,
+                                   const uint16_t* __restrict__ zs, int T, int D, int group, int asym,
+                                   int over_token, float* __restrict__ out, int64_t total) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int d = (int)(i % D);
+  const int64_t t = (i / D) % T;
+  const int64_t o = i / ((int64_t)D * T);
+  const int64_t si = over_token ? (o * (T / group) + t / group) * D + d
+                                : (o * T + t) * (D / group) + d / group;
+  float v = (float)c[i] * to_f<DT>(s[si]);
+  if (asym) v = v + to_f<DT>(zs[si]);
+  else v = v * to_f<DT>(zs[i]);
+  out[i] = v;
+}
+
+// ------------------------------------------------------------ launchers ---
+#define DT_DISPATCH(dt, ...)            \
+  if ((dt) == F16) {                    \
+    constexpr int DTC = F16;            \
+    __VA_ARGS__;                        \
+  } else {                              \
+    constexpr int DTC = BF16;           \
+    __VA_ARGS__;                        \
+  }
+#define BITS_DISPATCH(bits, ...)        \
+  if ((bits) == 2) {                    \
+    constexpr int BC = 2;               \
+    __VA_ARGS__;                        \
+  } else if ((bits) == 3) {             \
+    constexpr int BC = 3;               \
+    __VA_ARGS__;                        \
+  } else {                              \
+    constexpr int BC = 4;               \
+    __VA_ARGS__;                        \
+  }
+
+cudaError_t launch_norm_factor(const void* x, int dt, int B, int H, int T, int64_t sb, int64_t sh,
+                               int64_t st, void* f, cudaStream_t s) {
+  DT_DISPATCH(dt, norm_factor_kernel<DTC><<<B * H, kD, 0, s>>>(
+                      (const uint16_t*)x, sb, sh, st, H, T, (uint16_t*)f));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack(const void* x, int dt, int B, int H, int T, int64_t sb, int64_t sh,
+                        int64_t st, int bits, int group, int asym, int role_v, int over_token,
+                        const void* nf, void* codes, void* scale, void* zero, int64_t cap_tiles,
+                        int64_t t_off, cudaStream_t s) {
+  if (!role_v && !over_token) {
+    const int64_t rows = (int64_t)B * H * T;
+    const unsigned grid = (unsigned)((rows + 3) / 4);
+    DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC><<<grid, 128, 0, s>>>(
+                                            (const uint16_t*)x, sb, sh, st, H, T,
+                                            (const uint16_t*)nf, group, asym, (uint8_t*)codes,
+                                            (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off, rows)));
+  } else if (role_v && over_token) {
+    dim3 grid(T / group, H, B);
+    DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_col_token_kernel<DTC, BC><<<grid, 128, 0, s>>>(
+                                            (const uint16_t*)x, sb, sh, st, group, asym,
+                                            (uint8_t*)codes, (uint16_t*)scale, (uint16_t*)zero,
+                                            cap_tiles, t_off)));
+  } else {
+    return cudaErrorNotSupported;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_unpack_ref(const void* codes, const void* scale, const void* zero, int dt, int B,
+                              int H, int64_t n, int bits, int group, int asym, int role_v,
+                              int over_token, int64_t cap_tiles, int64_t t_begin, int32_t* oc,
+                              void* os, void* osc, void* oz, cudaStream_t s) {
+  const int64_t total = (int64_t)B * H * n * kD;
+  if (total == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((total + 255) / 256);
+  DT_DISPATCH(dt, unpack_ref_kernel<DTC><<<grid, 256, 0, s>>>(
+                      (const uint8_t*)codes, (const uint16_t*)scale, (const uint16_t*)zero, H, n,
+                      bits, group, asym, role_v, over_token, cap_tiles, t_begin, oc,
+                      (uint16_t*)os, (uint16_t*)osc, (uint16_t*)oz, total));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant(const void* codes, const void* scale, const void* zero, int dt, int B,
+                           int H, int64_t n, int bits, int group, int asym, int role_v,
+                           int over_token, int64_t cap_tiles, int64_t t_begin, const void* nf,
+                           void* out, int64_t ob, int64_t oh, int64_t ot, cudaStream_t s) {
+  const int64_t total = (int64_t)B * H * n * kD;
+  if (total == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((total + 255) / 256);
+  DT_DISPATCH(dt, dequant_kernel<DTC><<<grid, 256, 0, s>>>(
+                      (const uint8_t*)codes, (const uint16_t*)scale, (const uint16_t*)zero, H, n,
+                      bits, group, asym, role_v, over_token, cap_tiles, t_begin,
+                      (const uint16_t*)nf, (uint16_t*)out, ob, oh, ot, total));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lse_merge(const float* po, const float* pm, const float* pl, int rows,
+                             int rows_per_b, int n_splits, int dt, void* out, int64_t o_b,
+                             int64_t o_h, float* lse, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  DT_DISPATCH(dt, lse_merge_kernel<DTC><<<rows, kD, 0, s>>>(po, pm, pl, n_splits, rows_per_b,
+                                                            (uint16_t*)out, o_b, o_h, lse));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_ref(const int32_t* c, const void* s, const void* zs, int dt, int64_t n_outer,
+                               int T, int D, int group, int asym, int over_token, float* out,
+                               cudaStream_t st) {
+  const int64_t total = n_outer * T * D;
+  if (total == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((total + 255) / 256);
+  DT_DISPATCH(dt, dequant_ref_kernel<DTC><<<grid, 256, 0, st>>>(c, (const uint16_t*)s,
+                                                                (const uint16_t*)zs, T, D, group, asym,
+                                                                over_token, out, total));
+  return cudaGetLastError();
+}
+
+}  // namespace innerq

@@ -1,0 +1,268 @@
+"""GPU-resident store of one side (K or V) of one InnerQ cache layer.
+
+Token order matches the reference layer (``src/innerq/cache.py:235-276``):
+``[sink (dtype) | quantized middle (packed) | recent window (dtype)]``.
+
+* sink:   ``[B, H, n_sink, D]`` fixed at prefill (``cache.py:135-155``).
+* middle: packed 2/3/4-bit tiles of 32 tokens plus per-group scales / zero
+          points, written in place by ``innerq_quant_pack`` at the append
+          position (the reference ``torch.cat``\\ s onto the store,
+          ``cache.py:337-339, 363-365``).  Capacity grows by doubling.
+* recent: a FIFO window ``[B, H, cap, D]`` in the dtype; the oldest
+          ``flush_size`` tokens are quantized and popped when the window holds
+          at least ``flush_size`` (``cache.py:283-307``).
+
+All compute goes through ``libinnerq_b200.so``; torch only allocates and
+copies device memory.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+
+D_SUPPORTED = 128
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float16:
+        return _lib.DT_F16
+    if dt == torch.bfloat16:
+        return _lib.DT_BF16
+    raise TypeError(f"innerq_b200 kernels take float16 or bfloat16 tensors, got {dt}")
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(t: torch.Tensor, what: str):
+    if not t.is_cuda:
+        raise RuntimeError(f"{what} must be a CUDA tensor: innerq_b200 has no CPU path")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+class PackedSide:
+    """One of K / V of one layer."""
+
+    def __init__(self, role: int, bits: int, group: int, mode: int, over_token: bool,
+                 w_sink: int, w_recent: int, flush: int, normalize: bool = False):
+        self.role, self.bits, self.group, self.mode = role, bits, group, mode
+        self.over_token = bool(over_token)
+        self.w_sink, self.w_recent, self.flush = w_sink, w_recent, flush
+        self.normalize = normalize
+        self.quantize = bits < 16
+        self.dtype = self.device = None
+        self.B = self.H = self.D = 0
+        self.sink = None
+        self.codes = self.scale = self.zero = None
+        self.cap_tiles = 0
+        self.n_q = 0
+        self.norm_f = None            # [B, H, D] dtype
+        self._rbuf = None             # recent FIFO buffer [B, H, cap, D]
+        self._r0 = 0
+        self._rn = 0
+        self.headroom = 1024          # tokens of spare packed capacity per growth
+
+    # ------------------------------------------------------------- geometry
+    def _check_supported(self):
+        if not self.quantize:
+            return
+        if self.bits not in (2, 3, 4):
+            raise NotImplementedError(f"{self.bits}-bit codes are not built (2, 3, 4 are)")
+        if self.group not in (32, 64, 128):
+            raise NotImplementedError(f"group size {self.group} is not built (32, 64, 128 are)")
+        if self.role == _lib.ROLE_K and self.over_token:
+            raise NotImplementedError("keys grouped over tokens (KIVI layout) are not built")
+        if self.role == _lib.ROLE_V and not self.over_token:
+            raise NotImplementedError("values grouped over channels are not built")
+        if self.D != D_SUPPORTED:
+            raise NotImplementedError(f"head_dim {self.D} is not built (128 is)")
+
+    @property
+    def n_sink(self) -> int:
+        return 0 if self.sink is None else self.sink.shape[2]
+
+    @property
+    def n_recent(self) -> int:
+        return self._rn
+
+    @property
+    def recent(self) -> torch.Tensor:
+        return self._rbuf[:, :, self._r0:self._r0 + self._rn]
+
+    @property
+    def n_tokens(self) -> int:
+        return self.n_sink + self.n_q + self.n_recent
+
+    # ------------------------------------------------------------ storage
+    def _alloc_store(self, tokens: int):
+        tb = _lib.load().innerq_tile_bytes(self.bits)
+        cap_tiles = max(4, (tokens + 31) // 32)
+        if self.over_token:
+            cap_tiles = (cap_tiles * 32 + self.group - 1) // self.group * self.group // 32
+        B, H, D = self.B, self.H, self.D
+        codes = torch.empty((B, H, cap_tiles, tb), dtype=torch.uint8, device=self.device)
+        if self.over_token:
+            sshape = (B, H, cap_tiles * 32 // self.group, D)
+        else:
+            sshape = (B, H, cap_tiles * 32, D // self.group)
+        scale = torch.empty(sshape, dtype=self.dtype, device=self.device)
+        zero = torch.empty(sshape, dtype=self.dtype, device=self.device) if self.mode == _lib.ASYM else None
+        if self.codes is not None and self.n_q > 0:
+            nt = (self.n_q + 31) // 32
+            codes[:, :, :nt].copy_(self.codes[:, :, :nt])
+            ns = (self.n_q // self.group) if self.over_token else nt * 32
+            scale[:, :, :ns].copy_(self.scale[:, :, :ns])
+            if zero is not None:
+                zero[:, :, :ns].copy_(self.zero[:, :, :ns])
+        self.codes, self.scale, self.zero, self.cap_tiles = codes, scale, zero, cap_tiles
+
+    def reserve(self, n_quantized: int):
+        """Make room for n_quantized packed tokens (grows by doubling)."""
+        if self.codes is None:
+            self._alloc_store(n_quantized + self.headroom)
+        elif n_quantized > self.cap_tiles * 32:
+            cap = self.cap_tiles * 32
+            self._alloc_store(max(n_quantized, cap + max(self.headroom, cap // 4)))
+
+    def _recent_reserve(self, n_new: int):
+        need = self._rn + n_new
+        if self._rbuf is not None and self._r0 + need <= self._rbuf.shape[2]:
+            return
+        cap = max(need, self.w_recent + self.flush + 32, 2 * self._rn)
+        if self._rbuf is None or cap > self._rbuf.shape[2]:
+            buf = torch.empty((self.B, self.H, cap, self.D), dtype=self.dtype, device=self.device)
+        else:
+            buf = torch.empty_like(self._rbuf)
+        if self._rn:
+            buf[:, :, :self._rn].copy_(self.recent)
+        self._rbuf, self._r0 = buf, 0
+
+    def _push_recent(self, x: torch.Tensor):
+        self._recent_reserve(x.shape[2])
+        self._rbuf[:, :, self._r0 + self._rn:self._r0 + self._rn + x.shape[2]].copy_(x)
+        self._rn += x.shape[2]
+
+    # ---------------------------------------------------------- quantize
+    def _quantize(self, x: torch.Tensor):
+        """Quantize-and-pack x [B, H, T, D] at the append position."""
+        T = x.shape[2]
+        if T == 0:
+            return
+        if self.over_token:
+            assert T % self.group == 0  # quant.py:99
+        if self.normalize and self.norm_f is None:
+            # cache.py:124: factor from the first chunk that gets quantized
+            self.norm_f = torch.empty((self.B, self.H, self.D), dtype=self.dtype, device=self.device)
+            _lib.call("innerq_norm_factor", x.data_ptr(), dtype_code(self.dtype), self.B, self.H, T,
+                      self.D, x.stride(0), x.stride(1), x.stride(2), self.norm_f.data_ptr(),
+                      stream_ptr(self.device))
+        self.reserve(self.n_q + T)
+        if x.stride(3) != 1 or (not self.over_token and (x.data_ptr() % 8 or x.stride(0) % 4 or x.stride(1) % 4
+                                                        or x.stride(2) % 4)):
+            x = x.contiguous()
+        _lib.call("innerq_quant_pack", x.data_ptr(), dtype_code(self.dtype), self.B, self.H, T, self.D,
+                  x.stride(0), x.stride(1), x.stride(2), self.bits, self.group, self.mode, self.role,
+                  int(self.over_token), _ptr(self.norm_f if self.normalize else None),
+                  self.codes.data_ptr(), self.scale.data_ptr(), _ptr(self.zero), self.cap_tiles,
+                  self.n_q, stream_ptr(self.device))
+        self.n_q += T
+
+    # ---------------------------------------------------- reference logic
+    def prefill(self, x: torch.Tensor):
+        """Lazy initialisation (cache.py:135-185, 187-210) from prefill tokens."""
+        require_cuda(x, "key/value states")
+        self.dtype, self.device = x.dtype, x.device
+        dtype_code(self.dtype)
+        self.B, self.H, T, self.D = x.shape
+        self._check_supported()
+        n_sink = min(self.w_sink, T) if self.quantize else 0
+        self.sink = x[:, :, :n_sink].contiguous()
+        x = x[:, :, n_sink:]
+        T = x.shape[2]
+        if self.quantize:
+            r = min(self.w_recent, T)
+            if self.over_token:
+                while (T - r) % self.flush != 0:
+                    r -= 1
+        else:
+            r = T
+        nq = T - r
+        self._push_recent(x[:, :, nq:])
+        if self.quantize and nq > 0:
+            self._quantize(x[:, :, :nq])
+
+    def append(self, x: torch.Tensor):
+        """One decode update (cache.py:283-307 then 314-380)."""
+        require_cuda(x, "key/value states")
+        self._push_recent(x)
+        if self.quantize and self._rn >= self.flush:
+            out = self._rbuf[:, :, self._r0:self._r0 + self.flush]
+            self._quantize(out)
+            self._r0 += self.flush
+            self._rn -= self.flush
+
+    # ------------------------------------------------------------- views
+    def materialize(self) -> torch.Tensor:
+        """[sink | dequant(middle) | recent] in the dtype (cache.py:235-281)."""
+        out = torch.empty((self.B, self.H, self.n_tokens, self.D), dtype=self.dtype, device=self.device)
+        ns, nq = self.n_sink, self.n_q
+        if ns:
+            out[:, :, :ns].copy_(self.sink)
+        if nq:
+            mid = out[:, :, ns:ns + nq]
+            _lib.call("innerq_dequant", self.codes.data_ptr(), self.scale.data_ptr(), _ptr(self.zero),
+                      dtype_code(self.dtype), self.B, self.H, 0, nq, self.D, self.bits, self.group,
+                      self.mode, self.role, int(self.over_token), self.cap_tiles,
+                      _ptr(self.norm_f if self.normalize else None), mid.data_ptr(),
+                      mid.stride(0), mid.stride(1), mid.stride(2), stream_ptr(self.device))
+        if self._rn:
+            out[:, :, ns + nq:].copy_(self.recent)
+        return out
+
+    def ref_views(self):
+        """(int32 codes, scale, sign | zero) exactly as quant.py returns them for
+        the quantized tokens, or (None, None, None)."""
+        if self.n_q == 0:
+            return None, None, None
+        B, H, D, n = self.B, self.H, self.D, self.n_q
+        codes = torch.empty((B, H, n, D), dtype=torch.int32, device=self.device)
+        if self.over_token:
+            sshape = (B, H, n // self.group, D)
+        else:
+            sshape = (B, H, n, D // self.group)
+        scale = torch.empty(sshape, dtype=self.dtype, device=self.device)
+        if self.mode == _lib.ASYM:
+            zs = torch.empty(sshape, dtype=self.dtype, device=self.device)
+            sign = None
+        else:
+            zs = torch.empty((B, H, n, D), dtype=self.dtype, device=self.device)
+            sign = zs
+        _lib.call("innerq_unpack_ref", self.codes.data_ptr(), self.scale.data_ptr(), _ptr(self.zero),
+                  dtype_code(self.dtype), B, H, 0, n, D, self.bits, self.group, self.mode, self.role,
+                  int(self.over_token), self.cap_tiles, codes.data_ptr(), _ptr(sign),
+                  scale.data_ptr(), _ptr(zs if sign is None else None), stream_ptr(self.device))
+        return codes, scale, zs
+
+    def side_struct(self) -> _lib.Side:
+        s = _lib.Side()
+        s.codes = _ptr(self.codes) if self.n_q else None
+        s.scale = _ptr(self.scale) if self.n_q else None
+        s.zero = _ptr(self.zero) if self.n_q else None
+        s.cap_tiles = self.cap_tiles
+        if self.n_sink:
+            s.sink = self.sink.data_ptr()
+            s.sink_sb, s.sink_sh, s.sink_st = self.sink.stride()[:3]
+        if self._rn:
+            r = self.recent
+            s.recent = r.data_ptr()
+            s.rec_sb, s.rec_sh, s.rec_st = r.stride()[:3]
+        s.n_sink, s.n_q, s.n_recent = self.n_sink, self.n_q, self._rn
+        s.bits, s.group, s.mode, s.over_token = self.bits, self.group, self.mode, int(self.over_token)
+        return s

@@ -1,0 +1,175 @@
+"""GPU parity of the cache layer (append + materialised K/V) and of the fused
+decode attention kernel, against the reference fixtures and the oracle."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cache_ref as C
+from tests._util import (TDT, assert_close_rel, cfg, merge_np, oracle_layer, synth_kv, synth_q,
+                         to_np32)
+
+pytestmark = pytest.mark.gpu
+
+PRESET_KW = {
+    "innerq_base": C.PRESETS["innerq_base"],
+    "innerq_small": C.PRESETS["innerq_small"],
+    "default4": dict(k_bits=4, v_bits=4),
+    "asym4_norm": dict(k_bits=4, v_bits=4, key_quantize_mode="asymmetric",
+                       value_quantize_mode="asymmetric", key_normalize=True,
+                       key_w_sink=4, value_w_sink=4, value_group_size=64,
+                       value_flush_size=64),
+}
+
+
+def _from_golden(arr, dtype):
+    if dtype == "bf16":
+        return torch.from_numpy(arr.view(np.int16).copy()).view(torch.bfloat16).cuda()
+    return torch.from_numpy(arr.copy()).cuda()
+
+
+@pytest.mark.parametrize("name", list(PRESET_KW))
+def test_layer_matches_reference_fixture(cache_golden, name):
+    from innerq_b200.cache import InnerqDynamicLayer
+    g = cache_golden
+    p = f"cache/{name}"
+    dtype = str(g[p + "/dtype"])
+    kin = _from_golden(g[p + "/k_in"], dtype)
+    vin = _from_golden(g[p + "/v_in"], dtype)
+    layer = InnerqDynamicLayer(cfg(**PRESET_KW[name]), 0)
+    T0 = kin.shape[2] - 40
+    k0, v0 = layer.update(kin[:, :, :T0], vin[:, :, :T0])
+    assert k0.data_ptr() == kin.data_ptr()  # prefill returns the raw states (cache.py:390-392)
+    trace = []
+    for t in range(T0, kin.shape[2]):
+        K, V = layer.update(kin[:, :, t:t + 1], vin[:, :, t:t + 1])
+        ks, vs = layer.key_side, layer.value_side
+        trace.append([ks.n_sink, ks.n_q, ks.n_recent, vs.n_sink, vs.n_q, vs.n_recent])
+    np.testing.assert_array_equal(np.array(trace), g[p + "/trace"])
+    # materialised K/V bit-exact with the reference's get_deq_tensors
+    np.testing.assert_array_equal(to_np32(K), to_np32(_from_golden(g[p + "/K"], dtype)))
+    np.testing.assert_array_equal(to_np32(V), to_np32(_from_golden(g[p + "/V"], dtype)))
+    if p + "/kf" in g:
+        np.testing.assert_array_equal(to_np32(layer.key_normalization_factor),
+                                      to_np32(_from_golden(g[p + "/kf"], dtype)))
+    # fused attention over the packed store vs the reference's sdpa on those K/V
+    q = _from_golden(g[p + "/q"], dtype)
+    out = layer.attend(q)
+    assert_close_rel(to_np32(out), g[p + "/o"][:, :, 0], 1e-3, name)
+    assert layer.get_seq_length() == kin.shape[2]
+    assert layer.get_mask_sizes(1) == (kin.shape[2] + 1, 0)
+
+
+def test_kivi_layout_is_refused():
+    from innerq_b200.cache import InnerqDynamicLayer
+    layer = InnerqDynamicLayer(cfg(**C.PRESETS["kivi"]), 0)
+    k, v = synth_kv(1, 2, 200, seed=3)
+    with pytest.raises(NotImplementedError):
+        layer.update(k, v)
+
+
+def _oracle_kv32(ol):
+    """[sink | fp32 dequant (not cast) | recent] of the oracle layer."""
+    out = []
+    for side in (ol.k, ol.v):
+        parts = [side.sink]
+        d = side.dequant_fp32()
+        if d is not None:
+            parts.append(d)
+        parts.append(side.recent)
+        out.append(np.concatenate(parts, axis=-2))
+    return out
+
+
+CASES = [
+    # (k_bits, v_bits, kmode, vmode, R, dtype, gk, gv, sink, recent, normalize, T0, steps)
+    (4, 4, "symmetric", "symmetric", 4, "fp16", 32, 32, 0, 32, False, 1000, 5),
+    (3, 3, "symmetric", "symmetric", 4, "fp16", 32, 32, 32, 96, True, 700, 40),
+    (3, 2, "symmetric", "symmetric", 4, "bf16", 32, 32, 32, 96, True, 517, 33),
+    (2, 2, "symmetric", "symmetric", 8, "fp16", 32, 32, 0, 32, False, 2048, 3),
+    (4, 4, "asymmetric", "asymmetric", 4, "fp16", 32, 32, 4, 32, True, 900, 7),
+    (2, 3, "asymmetric", "symmetric", 1, "bf16", 64, 64, 0, 32, False, 640, 2),
+    (4, 2, "symmetric", "asymmetric", 2, "fp16", 128, 128, 0, 128, False, 1100, 2),
+    (4, 4, "symmetric", "symmetric", 4, "fp16", 32, 32, 0, 32, False, 20, 3),   # all dense
+    (4, 4, "symmetric", "symmetric", 4, "fp16", 32, 32, 0, 32, False, 33, 40),  # tiny middle
+    (3, 3, "symmetric", "symmetric", 8, "bf16", 32, 32, 5, 7, True, 95, 31),    # odd sink
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
+def test_decode_attention_vs_oracle(case):
+    from innerq_b200.attention import decode_attention, decode_attention_partials
+    from innerq_b200.cache import InnerqDynamicLayer
+    bk, bv, km, vm, R, dtype, gk, gv, sink, recent, norm, T0, steps = case
+    kw = dict(k_bits=bk, v_bits=bv, key_quantize_mode=km, value_quantize_mode=vm,
+              key_group_size=gk, value_group_size=gv, key_w_sink=sink, value_w_sink=sink,
+              key_w_recent=recent, value_w_recent=recent, key_flush_size=1,
+              value_flush_size=gv, key_normalize=norm)
+    Hkv, B = 2, 2
+    k, v = synth_kv(B, Hkv, T0 + steps, dtype=dtype, seed=T0)
+    layer = InnerqDynamicLayer(cfg(**kw), 0)
+    ol = oracle_layer(kw, dtype)
+    layer.update(k[:, :, :T0], v[:, :, :T0])
+    ol.update(to_np32(k[:, :, :T0]), to_np32(v[:, :, :T0]))
+    for t in range(T0, T0 + steps):
+        layer.update(k[:, :, t:t + 1], v[:, :, t:t + 1])
+        Kr, Vr = ol.update(to_np32(k[:, :, t:t + 1]), to_np32(v[:, :, t:t + 1]))
+    q = synth_q(B, Hkv * R, dtype=dtype, seed=T0 + 1)
+    qn = to_np32(q)
+    # (1) the 1e-3 bar against the reference's dequantize-then-matmul
+    ref, _ = C.attention(qn, Kr, Vr)
+    out = decode_attention(q, layer.key_side, layer.value_side)
+    assert_close_rel(to_np32(out), ref[:, :, 0], 1e-3, "vs reference path")
+    # (2) tight: fp64 merge of the partials vs the fp32 dequant (no cast)
+    K32, V32 = _oracle_kv32(ol)
+    ref32, logits = C.attention(qn, K32, V32)
+    for ns in (0, 1, 7):
+        po, pm, pl = decode_attention_partials(q, layer.key_side, layer.value_side, n_splits=ns)
+        o64, lse2 = merge_np(po.cpu().numpy(), pm.cpu().numpy(), pl.cpu().numpy())
+        assert_close_rel(o64, ref32[:, :, 0], 2e-5, f"tight n_splits={ns}")
+        lse_ref = np.log2(np.exp(logits - logits.max(-1, keepdims=True)).sum(-1)) \
+            + logits.max(-1) / math.log(2)
+        np.testing.assert_allclose(lse2, lse_ref[:, :, 0], rtol=0, atol=2e-4)
+
+
+def test_lse_merge_kernel_and_tile_ranges():
+    """Partials of two disjoint tile ranges merged by the CUDA merge kernel equal
+    the full pass (the context-sharding path)."""
+    from innerq_b200.attention import (build_args, decode_attention, decode_attention_partials,
+                                       lse_merge, plan)
+    from innerq_b200.cache import InnerqDynamicLayer
+    kw = dict(k_bits=4, v_bits=4, key_w_sink=32, value_w_sink=32, key_flush_size=1)
+    layer = InnerqDynamicLayer(cfg(**kw), 0)
+    k, v = synth_kv(2, 8, 5000, seed=11)
+    layer.update(k, v)
+    q = synth_q(2, 32, seed=12)
+    full = decode_attention(q, layer.key_side, layer.value_side)
+    n_tiles, _ = plan(build_args(q, layer.key_side, layer.value_side))
+    cut = n_tiles // 3
+    parts = [decode_attention_partials(q, layer.key_side, layer.value_side, tile_range=r)
+             for r in ((0, cut), (cut, n_tiles))]
+    po = torch.cat([p[0] for p in parts], dim=2)
+    pm = torch.cat([p[1] for p in parts], dim=2)
+    pl = torch.cat([p[2] for p in parts], dim=2)
+    merged = lse_merge(po, pm, pl, torch.float16)
+    assert_close_rel(to_np32(merged), to_np32(full), 2e-3, "sharded merge")
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_full_size_context_32k(B):
+    """C1 shape (S = 32768, Hq 32 / Hkv 8, 4-bit G32) against an fp32
+    dequantize-then-matmul done on the GPU from the materialised cache."""
+    from innerq_b200.cache import InnerqDynamicLayer
+    kw = dict(k_bits=4, v_bits=4, key_flush_size=1, key_normalize=True)
+    layer = InnerqDynamicLayer(cfg(**kw), 0)
+    k, v = synth_kv(B, 8, 32768, seed=5)
+    layer.update(k, v)
+    layer.update(*synth_kv(B, 8, 1, seed=6))
+    q = synth_q(B, 32, seed=7)
+    out = layer.attend(q)
+    K, V = layer.get_deq_tensors()  # reference-exact materialisation
+    kk = K.float().repeat_interleave(4, dim=1)
+    vv = V.float().repeat_interleave(4, dim=1)
+    ref = torch.softmax((q.float() @ kk.transpose(-1, -2)) / math.sqrt(128), dim=-1) @ vv
+    assert_close_rel(to_np32(out), to_np32(ref[:, :, 0]), 1e-3, "32k")
