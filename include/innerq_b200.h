@@ -181,6 +181,26 @@ int innerq_lse_merge(const float* part_o, const float* part_m, const float* part
                      int rows_per_b, int n_splits, int D, int dtype, void* out, int64_t o_sb,
                      int64_t o_sh, float* lse, void* stream);
 
+/*
+ * innerq_decode_attn without a caller workspace, for callers that cannot
+ * allocate device memory at decode time (a fixed memory arena, or a serving
+ * loop that forbids allocation after warm-up).  No counterpart in the
+ * reference, which has no native entry points.
+ *
+ * The split-KV partials live in a file-scope device array of
+ * INNERQ_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit.  The first call on a device looks up that array's device address
+ * (cudaGetSymbolAddress) with the device current; make that first call
+ * before any stream capture.  Calls whose partials would not fit are rejected
+ * with INNERQ_ERR_ARG (pass a smaller n_splits or batch).  All calls share the
+ * one array: calls that overlap on the GPU (two streams, two threads) race.
+ * Nothing in it needs to start at zero.  Allocates nothing; arguments and
+ * results as innerq_decode_attn.
+ */
+#define INNERQ_NOALLOC_SCRATCH_BYTES (64ll << 20)
+int innerq_decode_attn_noalloc(const innerq_attn_args* args, void* out, int64_t o_sb,
+                               int64_t o_sh, float* lse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,7 +21,7 @@ EXPORTS = (
     "innerq_abi_version", "innerq_last_error", "innerq_tile_bytes", "innerq_norm_factor",
     "innerq_quant_pack", "innerq_unpack_ref", "innerq_dequant", "innerq_attn_plan",
     "innerq_decode_attn_workspace", "innerq_decode_attn", "innerq_decode_attn_partials",
-    "innerq_lse_merge", "innerq_dequant_ref",
+    "innerq_lse_merge", "innerq_dequant_ref", "innerq_decode_attn_noalloc",
 )
 
 
@@ -86,6 +86,7 @@ def load() -> C.CDLL:
         "innerq_decode_attn_workspace": (i64, [C.POINTER(AttnArgs)]),
         "innerq_decode_attn": (i32, [C.POINTER(AttnArgs), vp, i64, vp, i64, i64, vp, vp]),
         "innerq_decode_attn_partials": (i32, [C.POINTER(AttnArgs), vp, vp, vp, vp]),
+        "innerq_decode_attn_noalloc": (i32, [C.POINTER(AttnArgs), vp, i64, i64, vp, vp]),
         "innerq_lse_merge": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp, i64, i64, vp, vp]),
     }
     for name, (res, args) in sig.items():
@@ -102,7 +103,7 @@ def load() -> C.CDLL:
 KERNELS_PER_CALL = {
     "innerq_norm_factor": 1, "innerq_quant_pack": 1, "innerq_unpack_ref": 1, "innerq_dequant": 1,
     "innerq_dequant_ref": 1, "innerq_decode_attn": 2, "innerq_decode_attn_partials": 1,
-    "innerq_lse_merge": 1,
+    "innerq_lse_merge": 1, "innerq_decode_attn_noalloc": 2,
 }
 launch_count = [0]
 

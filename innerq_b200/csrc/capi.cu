@@ -169,6 +169,14 @@ int64_t ws_bytes(const innerq_attn_args* a, const Plan& p) {
 
 }  // namespace
 
+int innerq::set_last_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 extern "C" {
 
 int innerq_abi_version(void) { return INNERQ_ABI_VERSION; }

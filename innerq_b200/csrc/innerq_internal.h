@@ -27,6 +27,8 @@ cudaError_t launch_lse_merge(const float* po, const float* pm, const float* pl, 
 cudaError_t launch_dequant_ref(const int32_t* c, const void* s, const void* zs, int dt, int64_t n_outer,
                                int T, int D, int group, int asym, int over_token, float* out,
                                cudaStream_t st);
+// record the message innerq_last_error() returns on this thread; returns code
+int set_last_error(int code, const char* fmt, ...);
 // decode attention, one translation unit per K bit width
 cudaError_t launch_attn_k2(const DevArgs& a, int bv, int R, int dt, dim3 grid, cudaStream_t s);
 cudaError_t launch_attn_k3(const DevArgs& a, int bv, int R, int dt, dim3 grid, cudaStream_t s);
