@@ -152,12 +152,16 @@ int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm,
   d.tiles_per_split = p.tps; d.n_splits = p.n_splits;
   d.scale_log2 = a->softmax_scale * 1.4426950408889634f;
   d.po = po; d.pm = pm; d.pl = pl;
+  d.R = p.R;
   dim3 grid(p.n_splits, a->Hkv, a->B);
+  const int rp = p.R <= 4 ? 4 : 8;
+  const int ng = a->k.n_q > 0 ? kD / a->k.group : 4;
+  const bool bf = a->dtype == INNERQ_DT_BF16;
   cudaError_t e;
   switch (p.bk) {
-    case 2: e = launch_attn_k2(d, p.bv, p.R, a->dtype, grid, st); break;
-    case 3: e = launch_attn_k3(d, p.bv, p.R, a->dtype, grid, st); break;
-    default: e = launch_attn_k4(d, p.bv, p.R, a->dtype, grid, st); break;
+    case 2: e = bf ? launch_attn_k2_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k2_f16(d, p.bv, rp, ng, grid, st); break;
+    case 3: e = bf ? launch_attn_k3_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k3_f16(d, p.bv, rp, ng, grid, st); break;
+    default: e = bf ? launch_attn_k4_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k4_f16(d, p.bv, rp, ng, grid, st); break;
   }
   return cuda_status(e, "decode_attn");
 }

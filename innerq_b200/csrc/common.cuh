@@ -1,27 +1,29 @@
 // Shared device helpers for the InnerQ B200 kernels: dtype rounding, the packed
-// tile layouts, code extraction into fp16 pairs, and mma.sync wrappers.
+// tile layouts, code extraction into integer-MMA fragments, mma.sync wrappers.
 //
-// Packed layouts (D = 128, tiles of 32 tokens, b = bits per code):
+// Packed layouts (D = 128, tiles of 32 tokens, b = bits per code).  Both
+// layouts hand each lane of the consuming warp exactly the bytes of its
+// m16n8k32 integer-MMA A fragments (a0: row gid, k 4tq..4tq+3; a1: row gid+8;
+// a2: row gid, k 16+4tq..; a3: row gid+8, k 16+4tq..), so a 4-bit word
+// expands to two fragment registers with one shift and two LOP3s.
 //
-// "row" layout (K, channel groups; the A operand is K[token][dim]):
-//   tile = 32 tokens = 512*b bytes.  Lane L = 4*gid + tq of the consuming warp
-//   owns the 32 codes of tokens r = gid + 8*j (j = 0..3) at dims
-//   kb*16 + {2tq, 2tq+1, 2tq+8, 2tq+9} (kb = 0..7), i.e. exactly the
-//   m16n8k16 A-fragment elements.  Row-local code index c = kb*4 + hi8*2 + e.
-//     b=4: lane chunk 64 B = 4 rows x 16 B; word w = kb>>1, nibble (kb&1)*2+hi8 + 4e
-//     b=2: lane chunk 32 B = 4 rows x  8 B; word w = kb>>2, crumb  (kb&3)*2+hi8 + 8e
-//     b=3: low 2 bits as b=2 in plane L (1024 B / tile), bit 2 in plane H
-//          (512 B / tile, 4 B per row): bit (kb*2+hi8) + 16e
-//   Scales / zero points (channel groups, ng = D/G per token) per tile:
-//     [gid 8][j 4][ng] 16-bit values.
+// "row" layout (K, channel groups; A = K[token][dim]):
+//   Lane L = 4*gid + tq owns tokens r = gid + 8*j (j = 0..3) at dims
+//   d = kb*32 + half*16 + 4*tq + i (kb = 0..3, half = 0..1, i = 0..3).
+//     b=4: lane chunk 64 B = 4 rows x 4 words; word kb, nibble 2i + half
+//     b=2: lane chunk 32 B = 4 rows x 2 words; word kb>>1,
+//          crumb 4i + (kb&1)*2 + half
+//     b=3: low 2 bits as b=2 in plane L (1024 B / tile); bit 2 in plane H
+//          (512 B / tile, 1 word per row): bit 8i + kb*2 + half
+//   Scales / zero points (ng = D/G per token) per tile: [gid 8][j 4][ng].
 //
-// "col" layout (V, token groups; the A operand is V^T[dim][token]):
+// "col" layout (V, token groups; A = V^T[dim][token]):
 //   Lane L = 4*gid + tq owns dims d = mt*16 + h*8 + gid (mt = 0..7, h = 0..1)
-//   at tokens kb*16 + {2tq, 2tq+1, 2tq+8, 2tq+9} (kb = 0..1).
-//     b=4: 16 words; word mt*2+h, nibble (kb*2+hi8) + 4e
-//     b=2:  8 words; word mt,     crumb  (h*4+kb*2+hi8) + 8e
-//     b=3: plane L as b=2; plane H 4 words: word mt>>1, bit ((mt&1)*8+h*4+kb*2+hi8) + 16e
-//   Scales / zero points (token groups, one per (group, dim)): [gid 8][mt 8][h 2].
+//   at tokens r = half*16 + 4*tq + i.
+//     b=4: 16 words; word mt*2 + h, nibble 2i + half
+//     b=2:  8 words; word mt, crumb 4i + h*2 + half
+//     b=3: plane L as b=2; plane H 4 words: word mt>>1, bit 8i + (mt&1)*4 + h*2 + half
+//   Scales / zero points (one per (group, dim)): [gid 8][mt 8][h 2].
 //
 // Symmetric codes are stored offset-binary: u = sign*code + 2^(b-1) (1..2^b-1);
 // asymmetric codes are stored as is (0..2^b-1).
@@ -57,8 +59,7 @@ template <> __device__ __forceinline__ uint16_t from_f<BF16>(float v) {
 // one torch op in the input dtype: fp32 result rounded to the dtype (RNE)
 template <int DT> __device__ __forceinline__ float rnd(float v) { return to_f<DT>(from_f<DT>(v)); }
 
-// hi/lo split of an fp32 value into two 16-bit values of dtype DT packed as
-// the low (first) element of a pair
+// hi/lo split of an fp32 value into two 16-bit values of dtype DT
 template <int DT> __device__ __forceinline__ void split_hilo(float v, uint16_t& hi, uint16_t& lo) {
   hi = from_f<DT>(v);
   lo = from_f<DT>(v - to_f<DT>(hi));
@@ -87,89 +88,106 @@ template <int DT> __device__ __forceinline__ void mma_dt(float c[4], const uint3
 template <> __device__ __forceinline__ void mma_dt<F16>(float c[4], const uint32_t a[4], const uint32_t b[2]) { mma_f16(c, a, b); }
 template <> __device__ __forceinline__ void mma_dt<BF16>(float c[4], const uint32_t a[4], const uint32_t b[2]) { mma_bf16(c, a, b); }
 
-// ------------------------------------------------------ code extraction ---
-// fp16 pair (1024 + x, 1024 + y) from the two fields of a word selected by
-// mask at shift s; then subtract the 1024 + offset bias exactly in fp16.
-__device__ __forceinline__ uint32_t magic_pair(uint32_t w, int shift, uint32_t mask) {
-  return ((w >> shift) & mask) | 0x64006400u;
+// integer MMA: u8 codes x s8 / u8 digits, exact int32 accumulation
+__device__ __forceinline__ void mma_u8s8(int c[4], const uint32_t a[4], const uint32_t b[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
-__device__ __forceinline__ uint32_t hsub_u32(uint32_t a, uint32_t b) {
-  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ uint32_t hfma_u32(uint32_t a, uint32_t b, uint32_t c) {
-  __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b),
-                      *reinterpret_cast<__half2*>(&c));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-// bias constant (1024 + off) as an fp16 pair; off <= 8 so the sum is exact
-__host__ __device__ constexpr uint32_t bias_pair(int off) {
-  // fp16 of 1024 + k for 0 <= k < 1024 is 0x6400 + k
-  return (uint32_t)(0x6400 + off) | ((uint32_t)(0x6400 + off) << 16);
+__device__ __forceinline__ void mma_u8u8(int c[4], const uint32_t a[4], const uint32_t b[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// Decode pair p (elements at field p and p + fields/2) of a b-bit word as
-// signed fp16 values (u - off).  For b = 3 the caller supplies the L word
-// (2-bit pair index pl) and the H word (1-bit pair index ph).
-template <int BITS> struct Dec;
-template <> struct Dec<4> {
-  static __device__ __forceinline__ uint32_t pair(uint32_t w, int p, uint32_t bias) {
-    return hsub_u32(magic_pair(w, 4 * p, 0x000F000Fu), bias);
+// same, with a separate accumulator input c (d = a*b + c); passing literal
+// zeros or per-thread constants for c avoids materialising zeroed registers
+__device__ __forceinline__ void imma_u8s8(int d[4], const uint32_t a[4], const uint32_t b[2], int c0,
+                                          int c1, int c2, int c3) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(c0), "r"(c1), "r"(c2),
+        "r"(c3));
+}
+__device__ __forceinline__ void imma_u8u8(int d[4], const uint32_t a[4], const uint32_t b[2], int c0,
+                                          int c1, int c2, int c3) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(c0), "r"(c1), "r"(c2),
+        "r"(c3));
+}
+
+// ------------------------------------------------------ code extraction ---
+// One m16n8k32 A-fragment register (4 codes as bytes) from packed words.
+// Row layout (K): w = the words of one token row (b=3: L0, L1, H).
+template <int BITS>
+__device__ __forceinline__ uint32_t row_frag(const uint32_t* w, int kb, int half) {
+  if constexpr (BITS == 4) {
+    return (w[kb] >> (4 * half)) & 0x0F0F0F0Fu;
+  } else {
+    const uint32_t l = (w[kb >> 1] >> (2 * ((kb & 1) * 2 + half))) & 0x03030303u;
+    if constexpr (BITS == 2) return l;
+    return l | (((w[2] >> (kb * 2 + half)) & 0x01010101u) << 2);
   }
-};
-template <> struct Dec<2> {
-  static __device__ __forceinline__ uint32_t pair(uint32_t w, int p, uint32_t bias) {
-    return hsub_u32(magic_pair(w, 2 * p, 0x00030003u), bias);
+}
+// Col layout (V): the lane's chunk words (b=3: 8 L words then 4 H words).
+template <int BITS>
+__device__ __forceinline__ uint32_t col_frag(const uint32_t* w, int mt, int h, int half) {
+  if constexpr (BITS == 4) {
+    return (w[mt * 2 + h] >> (4 * half)) & 0x0F0F0F0Fu;
+  } else {
+    const uint32_t l = (w[mt] >> (2 * (h * 2 + half))) & 0x03030303u;
+    if constexpr (BITS == 2) return l;
+    return l | (((w[8 + (mt >> 1)] >> ((mt & 1) * 4 + h * 2 + half)) & 0x01010101u) << 2);
   }
-};
-struct Dec3 {
-  static __device__ __forceinline__ uint32_t pair(uint32_t wl, int pl, uint32_t wh, int ph,
-                                                  uint32_t bias) {
-    uint32_t lo = hsub_u32(magic_pair(wl, 2 * pl, 0x00030003u), bias);       // l - off
-    uint32_t hi = hsub_u32(magic_pair(wh, ph, 0x00010001u), 0x64006400u);    // h in {0,1}
-    return hfma_u32(hi, 0x44004400u /* 4.0 */, lo);                            // 4h + l - off
-  }
-};
+}
 
 // --------------------------------------------------- layout index helpers ---
-// Byte offset + bit shift of the code of token-in-tile r, dim d, row layout.
+// Byte offset (of a 32-bit word) + bit shift of the code of token-in-tile r,
+// dim d; hoff / hshift locate bit 2 of a 3-bit code in plane H.
 struct BitPos { int off; int shift; int hoff; int hshift; };
 
 __host__ __device__ inline BitPos row_pos(int bits, int r, int d) {
-  int gid = r & 7, j = r >> 3;
-  int kb = d >> 4, dd = d & 15, tq = (dd & 7) >> 1, e = dd & 1, hi8 = dd >> 3;
-  int lane = gid * 4 + tq;
+  const int gid = r & 7, j = r >> 3;
+  const int kb = d >> 5, half = (d >> 4) & 1, tq = (d >> 2) & 3, i = d & 3;
+  const int lane = gid * 4 + tq;
   BitPos p{0, 0, 0, 0};
   if (bits == 4) {
-    int w = kb >> 1, nib = (kb & 1) * 2 + hi8 + 4 * e;
-    p.off = lane * 64 + j * 16 + w * 4;
-    p.shift = 4 * nib;
-  } else {  // 2-bit, or the L plane of 3-bit
-    int w = kb >> 2, cr = (kb & 3) * 2 + hi8 + 8 * e;
-    p.off = lane * 32 + j * 8 + w * 4;
-    p.shift = 2 * cr;
+    p.off = lane * 64 + j * 16 + kb * 4;
+    p.shift = 4 * (2 * i + half);
+  } else {
+    p.off = lane * 32 + j * 8 + (kb >> 1) * 4;
+    p.shift = 2 * (4 * i + (kb & 1) * 2 + half);
     if (bits == 3) {
       p.hoff = 1024 + lane * 16 + j * 4;
-      p.hshift = kb * 2 + hi8 + 16 * e;
+      p.hshift = 8 * i + kb * 2 + half;
     }
   }
   return p;
 }
 
 __host__ __device__ inline BitPos col_pos(int bits, int r, int d) {
-  int mt = d >> 4, h = (d >> 3) & 1, gid = d & 7;
-  int kb = r >> 4, rr = r & 15, tq = (rr & 7) >> 1, e = rr & 1, hi8 = rr >> 3;
-  int lane = gid * 4 + tq;
+  const int mt = d >> 4, h = (d >> 3) & 1, gid = d & 7;
+  const int half = r >> 4, tq = (r >> 2) & 3, i = r & 3;
+  const int lane = gid * 4 + tq;
   BitPos p{0, 0, 0, 0};
   if (bits == 4) {
     p.off = lane * 64 + (mt * 2 + h) * 4;
-    p.shift = 4 * (kb * 2 + hi8 + 4 * e);
+    p.shift = 4 * (2 * i + half);
   } else {
     p.off = lane * 32 + mt * 4;
-    p.shift = 2 * (h * 4 + kb * 2 + hi8 + 8 * e);
+    p.shift = 2 * (4 * i + h * 2 + half);
     if (bits == 3) {
       p.hoff = 1024 + lane * 16 + (mt >> 1) * 4;
-      p.hshift = (mt & 1) * 8 + h * 4 + kb * 2 + hi8 + 16 * e;
+      p.hshift = 8 * i + (mt & 1) * 4 + h * 2 + half;
     }
   }
   return p;

@@ -5,21 +5,33 @@
 //   HF sdpa           softmax(q K^T * scale) V   (GQA via repeat_kv)
 // with one pass that reads the packed codes once and dequantizes in registers.
 //
-// Work decomposition: grid (split, kv_head, batch), 4 warps per CTA.  The
-// token axis is cut into 32-token tiles aligned to the V packed grid; each CTA
-// owns a contiguous range of tiles (a split) and each warp takes every 4th
-// tile of that range with its own online-softmax state.  The CTA writes an
-// unnormalised partial (O, m, l) per query head; lse_merge() combines splits
-// (and GPUs when context chunks are sharded).
+// Work decomposition: grid (split, kv_head, batch), 4 warps per CTA.  The token
+// axis is cut into 32-token tiles aligned to the V packed grid; each CTA owns a
+// contiguous range of tiles (a split) and each warp takes every 4th tile of that
+// range with its own online-softmax state.  The CTA writes an unnormalised
+// partial (O, m, l) per query head; lse_merge combines splits (and GPUs when
+// context chunks are sharded).
 //
-// Inner products use mma.sync m16n8k16 with register-resident A fragments:
-//   QK^T: A = K tile [token][dim] decoded from the row layout, B = q*f split
-//         into fp16 hi+lo columns (8 columns = 4 query heads x {hi,lo}), one
-//         accumulator per channel group, scaled by the group scale in fp32.
-//   PV:   A = V^T tile [dim][token] decoded from the col layout, B = P split
-//         into hi+lo, scaled by the (token-group, dim) scale in fp32.
-// The hi/lo split keeps ~22 mantissa bits, so results match an fp32
-// dequantize-then-matmul to ~1e-6 relative.
+// Staging: tiles whose K and V are both packed ("fast" tiles, the whole middle
+// of the cache) are fetched by the TMA engine with cp.async.bulk into a
+// per-warp ring of kStages shared-memory slots, completion tracked by one
+// mbarrier per slot (no multicast).  Boundary tiles (sink, recent, the K/V
+// packed/dense seams) load directly from global memory.
+//
+// Arithmetic: packed codes are multiplied on the tensor cores with
+// mma.sync m16n8k32 u8 x s8/u8 -> s32, so every partial dot product is exact:
+//   QK^T: A = K codes [token][dim] (u8), B = q*f*2^e rounded to a 22-bit
+//         integer (21 / 20 bits for groups of 64 / 128, so one group's sum
+//         fits int32) and split into three balanced int8 digits.
+//         logit = 2^-e * sum_g s_g * (sum_{d in g} u_d q_d - off * sum_{d in g} q_d)
+//   PV:   A = V codes [dim][token] (u8), B = exp2(x - tile max) as a 16-bit
+//         fixed-point value split into two u8 digits; scaled per tile by
+//         exp2(tile max - running max) / 65535 and by the (group, dim) scale.
+// B columns (d2, d1) and (d0, 0) per head; the offset-binary correction
+// off * sum q enters as the accumulator input of the d0 column.  The logits
+// carry ~2^-21 of max|q| rounding; the probabilities 2^-17 of each tile's
+// largest weight.
+// Dense (fp16 / bf16) rows use m16n8k16 with hi/lo-split B operands.
 #pragma once
 #include "common.cuh"
 
@@ -44,7 +56,7 @@ struct DevArgs {
   const uint16_t* q;
   int64_t q_b, q_h;
   const uint16_t* kf;  // key normalisation factor [B][Hkv][D] or null
-  int B, Hq, Hkv, S;
+  int B, Hq, Hkv, S, R;
   int t_first;         // token index of tile 0 (<= 0)
   int tile_lo, tile_hi;
   int tiles_per_split, n_splits;
@@ -55,20 +67,60 @@ struct DevArgs {
 };
 
 constexpr int kWarps = 4;
+constexpr int kStages = 3;
+constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier wait (iterations)
 
-template <int R>
-struct AttnSmem {
-  static constexpr int NT = (R + 3) / 4;
-  float q_s[R][kD];     // q * f * 2^e_p
-  float qd_s[R][kD];    // q * 2^e_d
-  float qsum_s[R][8];   // asym K: per channel group sum of q_s
-  uint2 bd_s[NT][8][32];
-  float p_s[kWarps][R][kTile];
-  float red_s[2][kWarps];
-  float cm_s[kWarps][R];
-  float cl_s[kWarps][R];
-  float co_s[kWarps][R][kD];
-};
+// bytes of one staged tile (K codes, K scales [, K zeros], V codes, V scales [, V zeros])
+__host__ __device__ inline int stage_bytes(int bk, int bv, int ng, int kasym, int vasym) {
+  return tile_bytes(bk) + 64 * ng * (1 + kasym) + tile_bytes(bv) + 256 * (1 + vasym);
+}
+__host__ __device__ inline int attn_dyn_smem(int bk, int bv, int ng, int kasym, int vasym) {
+  return kWarps * kStages * stage_bytes(bk, bv, ng, kasym, vasym);
+}
+
+// ------------------------------------------------------------ PTX helpers ---
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
+  for (uint32_t it = 0; it < limit; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+// plain (non-multicast) bulk copy global -> this CTA's shared memory
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -88,186 +140,387 @@ __device__ __forceinline__ float gid_sum(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 16);
   return v;
 }
+__device__ __forceinline__ int gid_isum(int v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  v += __shfl_xor_sync(0xffffffffu, v, 16);
+  return v;
+}
 
-// per-row K words of one packed token row (row layout)
+// words of one packed K token row (row layout): b=4: 4, b=2: 2, b=3: L0 L1 H
 template <int BITS> struct KRow { uint32_t w[BITS == 4 ? 4 : 3]; };
 
 template <int BITS>
-__device__ __forceinline__ void load_krow(KRow<BITS>& r, const uint8_t* tilebase, int lane2, int j) {
+__device__ __forceinline__ void load_krows(KRow<BITS> rw[4], const uint8_t* tb, int lane) {
+  // the lane's four rows of one fully packed tile (shared or global memory)
   if constexpr (BITS == 4) {
-    uint4 v = *reinterpret_cast<const uint4*>(tilebase + lane2 * 64 + j * 16);
-    r.w[0] = v.x; r.w[1] = v.y; r.w[2] = v.z; r.w[3] = v.w;
-  } else if constexpr (BITS == 2) {
-    uint2 v = *reinterpret_cast<const uint2*>(tilebase + lane2 * 32 + j * 8);
-    r.w[0] = v.x; r.w[1] = v.y; r.w[2] = 0;
+    const uint4* p = reinterpret_cast<const uint4*>(tb + lane * 64);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = p[j];
+      rw[j].w[0] = v.x; rw[j].w[1] = v.y; rw[j].w[2] = v.z; rw[j].w[3] = v.w;
+    }
   } else {
-    uint2 v = *reinterpret_cast<const uint2*>(tilebase + lane2 * 32 + j * 8);
-    r.w[0] = v.x; r.w[1] = v.y;
-    r.w[2] = *reinterpret_cast<const uint32_t*>(tilebase + 1024 + lane2 * 16 + j * 4);
+    const uint4* p = reinterpret_cast<const uint4*>(tb + lane * 32);
+    const uint4 v0 = p[0], v1 = p[1];
+    rw[0].w[0] = v0.x; rw[0].w[1] = v0.y; rw[1].w[0] = v0.z; rw[1].w[1] = v0.w;
+    rw[2].w[0] = v1.x; rw[2].w[1] = v1.y; rw[3].w[0] = v1.z; rw[3].w[1] = v1.w;
+    if constexpr (BITS == 3) {
+      const uint4 h = *reinterpret_cast<const uint4*>(tb + 1024 + lane * 16);
+      rw[0].w[2] = h.x; rw[1].w[2] = h.y; rw[2].w[2] = h.z; rw[3].w[2] = h.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) rw[j].w[2] = 0;
+    }
   }
 }
 
-// fp16 pair for (kb, hi8) of a packed K row
 template <int BITS>
-__device__ __forceinline__ uint32_t krow_pair(const KRow<BITS>& r, int kb, int hi8, uint32_t bias) {
+__device__ __forceinline__ void load_krow(KRow<BITS>& r, const uint8_t* tb, int lane2, int j) {
+  // one row of a tile, for tiles whose rows come from different places
   if constexpr (BITS == 4) {
-    return Dec<4>::pair(r.w[kb >> 1], (kb & 1) * 2 + hi8, bias);
-  } else if constexpr (BITS == 2) {
-    return Dec<2>::pair(r.w[kb >> 2], (kb & 3) * 2 + hi8, bias);
+    const uint4 v = *reinterpret_cast<const uint4*>(tb + lane2 * 64 + j * 16);
+    r.w[0] = v.x; r.w[1] = v.y; r.w[2] = v.z; r.w[3] = v.w;
   } else {
-    return Dec3::pair(r.w[kb >> 2], (kb & 3) * 2 + hi8, r.w[2], kb * 2 + hi8, bias);
+    const uint2 v = *reinterpret_cast<const uint2*>(tb + lane2 * 32 + j * 8);
+    r.w[0] = v.x; r.w[1] = v.y;
+    r.w[2] = BITS == 3 ? *reinterpret_cast<const uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) : 0u;
   }
 }
 
-// per-lane V chunk (col layout)
 template <int BITS> struct VChunk { uint32_t w[BITS == 4 ? 16 : (BITS == 2 ? 8 : 12)]; };
 
 template <int BITS>
-__device__ __forceinline__ void load_vchunk(VChunk<BITS>& c, const uint8_t* tilebase, int lane) {
+__device__ __forceinline__ void load_vchunk(VChunk<BITS>& c, const uint8_t* tb, int lane) {
   if constexpr (BITS == 4) {
-    const uint4* p = reinterpret_cast<const uint4*>(tilebase + lane * 64);
+    const uint4* p = reinterpret_cast<const uint4*>(tb + lane * 64);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      uint4 v = p[i];
+      const uint4 v = p[i];
       c.w[4 * i] = v.x; c.w[4 * i + 1] = v.y; c.w[4 * i + 2] = v.z; c.w[4 * i + 3] = v.w;
     }
   } else {
-    const uint4* p = reinterpret_cast<const uint4*>(tilebase + lane * 32);
+    const uint4* p = reinterpret_cast<const uint4*>(tb + lane * 32);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      uint4 v = p[i];
+      const uint4 v = p[i];
       c.w[4 * i] = v.x; c.w[4 * i + 1] = v.y; c.w[4 * i + 2] = v.z; c.w[4 * i + 3] = v.w;
     }
     if constexpr (BITS == 3) {
-      uint4 v = *reinterpret_cast<const uint4*>(tilebase + 1024 + lane * 16);
+      const uint4 v = *reinterpret_cast<const uint4*>(tb + 1024 + lane * 16);
       c.w[8] = v.x; c.w[9] = v.y; c.w[10] = v.z; c.w[11] = v.w;
     }
   }
 }
 
-template <int BITS>
-__device__ __forceinline__ uint32_t vchunk_pair(const VChunk<BITS>& c, int mt, int h, int kb,
-                                                int hi8, uint32_t bias) {
-  if constexpr (BITS == 4) {
-    return Dec<4>::pair(c.w[mt * 2 + h], kb * 2 + hi8, bias);
-  } else if constexpr (BITS == 2) {
-    return Dec<2>::pair(c.w[mt], h * 4 + kb * 2 + hi8, bias);
-  } else {
-    return Dec3::pair(c.w[mt], h * 4 + kb * 2 + hi8, c.w[8 + (mt >> 1)],
-                      (mt & 1) * 8 + h * 4 + kb * 2 + hi8, bias);
+// 16 16-bit values (32 B) as floats
+template <int DT>
+__device__ __forceinline__ void load16(float out[16], const uint16_t* p) {
+  const uint4 a = reinterpret_cast<const uint4*>(p)[0], b = reinterpret_cast<const uint4*>(p)[1];
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    out[2 * u] = to_f<DT>((uint16_t)(w[u] & 0xffffu));
+    out[2 * u + 1] = to_f<DT>((uint16_t)(w[u] >> 16));
   }
 }
 
-// Dense (fp16/bf16) K row pointer for token t, or null when t is not a dense
-// token of this side.
+// dense (fp16 / bf16) row pointer for token t of a side, or null
 __device__ __forceinline__ const uint16_t* dense_row(const DevSide& s, int b, int h, int t, int S) {
   if (t < 0 || t >= S) return nullptr;
   if (t < s.n_sink) return s.sink + b * s.sk_b + h * s.sk_h + (int64_t)t * s.sk_t;
-  int r = t - s.n_sink - s.n_q;
+  const int r = t - s.n_sink - s.n_q;
   if (r >= 0) return s.rec + b * s.rc_b + h * s.rc_h + (int64_t)r * s.rc_t;
   return nullptr;
 }
 
-template <int BK, int BV, int R, int DT>
-__global__ void __launch_bounds__(kWarps * 32)
+
+template <int RP>
+struct AttnStatic {
+  static constexpr int NT = RP / 4;
+  uint64_t bars[kWarps][kStages];
+  int ctot_s[RP][4];          // K offset correction per channel group: off * sum q
+  float qsum_s[RP][4];        // sum of q over each K channel group (asymmetric zero term)
+  uint2 bk_s[2 * NT][4][32];  // packed-K B fragments (three int8 digits of q)
+  uint2 bd_s[NT][8][32];      // dense-K B fragments (dtype hi/lo)
+  float p_s[kWarps][RP][kTile];
+  uint8_t pd_s[kWarps][RP][2][kTile];
+  float red_s[2][kWarps];
+  float cm_s[kWarps][RP];
+  float cl_s[kWarps][RP];
+};
+
+// balanced base-256 digits of an integer |v| < 2^23: v = d2*65536 + d1*256 + d0
+__device__ __forceinline__ void digits3(int v, int& d0, int& d1, int& d2) {
+  d0 = ((v + 128) & 255) - 128;
+  const int v1 = (v - d0) >> 8;
+  d1 = ((v1 + 128) & 255) - 128;
+  d2 = (v1 - d1) >> 8;
+}
+
+// Logits (before the softmax scale) of the lane's 4 token rows for its
+// head(s) from packed K words: lp[nt][j] += sum_g s[j][g] * (sum_d u q - off*sum_d q)
+// (+ z[j][g] * sum_d q for asymmetric keys).  All partial sums are exact int32.
+template <int BK, int NT, int NG>
+__device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const float sc[4][NG],
+                                                const float zc[4][NG], const uint2 (*bks)[4][32],
+                                                const int ctot[NT][NG], const float qsf[NT][NG],
+                                                int kasym, int lane, float lp[NT][4]) {
+  constexpr int KPG = 4 / NG;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    int acc[2][2][4];  // [mt][digit n-tile: (d2,d1) / (d0,-)][c]
+#pragma unroll
+    for (int kb = 0; kb < 4; ++kb) {
+      const int g = kb / KPG;
+      const bool first = kb % KPG == 0;
+      const uint2 b0 = bks[2 * nt][kb][lane], b1 = bks[2 * nt + 1][kb][lane];
+      const uint32_t bf0[2] = {b0.x, b0.y}, bf1[2] = {b1.x, b1.y};
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const uint32_t af[4] = {row_frag<BK>(rw[2 * mt].w, kb, 0), row_frag<BK>(rw[2 * mt + 1].w, kb, 0),
+                                row_frag<BK>(rw[2 * mt].w, kb, 1), row_frag<BK>(rw[2 * mt + 1].w, kb, 1)};
+        if (first) {
+          imma_u8s8(acc[mt][0], af, bf0, 0, 0, 0, 0);
+          imma_u8s8(acc[mt][1], af, bf1, -ctot[nt][g], 0, -ctot[nt][g], 0);
+        } else {
+          imma_u8s8(acc[mt][0], af, bf0, acc[mt][0][0], acc[mt][0][1], acc[mt][0][2], acc[mt][0][3]);
+          imma_u8s8(acc[mt][1], af, bf1, acc[mt][1][0], acc[mt][1][1], acc[mt][1][2], acc[mt][1][3]);
+        }
+      }
+      if (kb % KPG == KPG - 1) {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const int j = 2 * mt + rr;
+            // the exact sum fits int32; intermediate terms wrap modulo 2^32
+            const uint32_t t = (uint32_t)acc[mt][0][2 * rr] * 65536u +
+                               (uint32_t)acc[mt][0][2 * rr + 1] * 256u + (uint32_t)acc[mt][1][2 * rr];
+            lp[nt][j] = fmaf(sc[j][g], (float)(int)t, lp[nt][j]);
+            if (kasym) lp[nt][j] = fmaf(zc[j][g], qsf[nt][g], lp[nt][j]);
+          }
+      }
+    }
+  }
+}
+
+// O[nt][mt][h] += fv * (s * (sum_t u p - off * sum_t p) [+ z * sum_t p]) for one
+// packed V tile (integer MMA, probabilities as two u8 digits)
+template <int BV, int NT, int DT>
+__device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const float sv[16],
+                                                    const float zv[16], const uint32_t pb[NT][2],
+                                                    const int offp[NT], const float fv[NT],
+                                                    const float zf[NT], int vasym, float o[NT][8][2]) {
+  float svf[NT][16];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int u = 0; u < 16; ++u) svf[nt][u] = sv[u] * fv[nt];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const uint32_t af[4] = {col_frag<BV>(vc.w, mt, 0, 0), col_frag<BV>(vc.w, mt, 1, 0),
+                            col_frag<BV>(vc.w, mt, 0, 1), col_frag<BV>(vc.w, mt, 1, 1)};
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      int acc[4];
+      imma_u8u8(acc, af, pb[nt], 0, -offp[nt], 0, -offp[nt]);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = acc[2 * hh] * 256 + acc[2 * hh + 1];
+        o[nt][mt][hh] = fmaf(svf[nt][mt * 2 + hh], (float)t, o[nt][mt][hh]);
+        if (vasym) o[nt][mt][hh] = fmaf(zv[mt * 2 + hh], zf[nt], o[nt][mt][hh]);
+      }
+    }
+  }
+}
+
+// scales / zero points of the lane's 4 rows (row layout), 8*NG bytes at p
+template <int DT, int NG>
+__device__ __forceinline__ void load_kscales(float out[4][NG], const uint16_t* p) {
+  uint32_t w[2 * NG];
+  if constexpr (NG == 4) {
+    const uint4 a = reinterpret_cast<const uint4*>(p)[0], b = reinterpret_cast<const uint4*>(p)[1];
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+  } else if constexpr (NG == 2) {
+    const uint4 a = reinterpret_cast<const uint4*>(p)[0];
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  } else {
+    const uint2 a = reinterpret_cast<const uint2*>(p)[0];
+    w[0] = a.x; w[1] = a.y;
+  }
+#pragma unroll
+  for (int i = 0; i < 4 * NG; ++i) {
+    const uint16_t h = (uint16_t)((w[i >> 1] >> (16 * (i & 1))) & 0xffffu);
+    out[i / NG][i % NG] = to_f<DT>(h);
+  }
+}
+
+// BK/BV: code bits; RP: query heads per KV head padded to 4 or 8; DT: dtype;
+// NG: K channel groups per token (4, 2, 1 for groups of 32, 64, 128)
+template <int BK, int BV, int RP, int DT, int NG>
+__global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 3 : 2)
 decode_attn_kernel(const DevArgs a) {
-  constexpr int NT = (R + 3) / 4;
-  __shared__ AttnSmem<R> sm;
+  constexpr int NT = RP / 4;
+  constexpr int KPG = 4 / NG;           // 32-dim k-blocks per channel group
+  constexpr int QBITS = NG == 4 ? 22 : (NG == 2 ? 21 : 20);  // |q int| < 2^QBITS
+  extern __shared__ __align__(128) uint8_t dyn[];
+  __shared__ AttnStatic<RP> sm;
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
+  const int R = a.R;
   const int tile_beg = a.tile_lo + split * a.tiles_per_split;
   const int tile_end = min(tile_beg + a.tiles_per_split, a.tile_hi);
   const int S = a.S;
+  const int ks = a.k.n_sink, nqk = a.k.n_q;
+  const int vs = a.v.n_sink, nqv = a.v.n_q;
+  const int kasym = a.k.asym, vasym = a.v.asym;
+  const int SB = stage_bytes(BK, BV, NG, kasym, vasym);
+  const int koff = kasym ? 0 : (1 << (BK - 1));
+  const int voff = vasym ? 0 : (1 << (BV - 1));
 
   // ---------------------------------------------------------------- prologue
+  float* q_s = reinterpret_cast<float*>(dyn);          // [RP][128] q*f   (prologue only)
+  float* qd_s = q_s + RP * kD;                         // [RP][128] q
+  int* qi_s = reinterpret_cast<int*>(qd_s + RP * kD);  // [RP][128] integer q*f*2^e
   float amax_p = 0.f, amax_d = 0.f;
-  for (int i = threadIdx.x; i < R * kD; i += kWarps * 32) {
-    int h = i / kD, d = i % kD;
-    float qv = to_f<DT>(a.q[b * a.q_b + (int64_t)(hk * R + h) * a.q_h + d]);
-    float f = a.kf ? to_f<DT>(a.kf[((int64_t)b * a.Hkv + hk) * kD + d]) : 1.f;
-    float qp = qv * f;
-    sm.q_s[h][d] = qp;
-    sm.qd_s[h][d] = qv;
+  for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
+    const int h = i / kD, d = i % kD;
+    float qv = 0.f, f = 1.f;
+    if (h < R) {
+      qv = to_f<DT>(a.q[b * a.q_b + (int64_t)(hk * R + h) * a.q_h + d]);
+      if (a.kf) f = to_f<DT>(a.kf[((int64_t)b * a.Hkv + hk) * kD + d]);
+    }
+    const float qp = qv * f;
+    q_s[i] = qp;
+    qd_s[i] = qv;
     amax_p = fmaxf(amax_p, fabsf(qp));
     amax_d = fmaxf(amax_d, fabsf(qv));
   }
   amax_p = warp_max(amax_p);
   amax_d = warp_max(amax_d);
   if (lane == 0) { sm.red_s[0][warp] = amax_p; sm.red_s[1][warp] = amax_d; }
+  if (threadIdx.x < kWarps * kStages) mbar_init(&sm.bars[0][0] + threadIdx.x, 1);
+  mbar_fence_init();
   __syncthreads();
   amax_p = fmaxf(fmaxf(sm.red_s[0][0], sm.red_s[0][1]), fmaxf(sm.red_s[0][2], sm.red_s[0][3]));
   amax_d = fmaxf(fmaxf(sm.red_s[1][0], sm.red_s[1][1]), fmaxf(sm.red_s[1][2], sm.red_s[1][3]));
-  int ex;
-  int e_p = 0, e_d = 0;
-  if (amax_p > 0.f) { frexpf(amax_p, &ex); e_p = 15 - ex; }
+  int ex, e_p = 0, e_d = 0;
+  if (amax_p > 0.f) { frexpf(amax_p, &ex); e_p = QBITS - ex; }
   if (amax_d > 0.f) { frexpf(amax_d, &ex); e_d = 15 - ex; }
-  for (int i = threadIdx.x; i < R * kD; i += kWarps * 32) {
-    int h = i / kD, d = i % kD;
-    sm.q_s[h][d] = ldexpf(sm.q_s[h][d], e_p);
-    sm.qd_s[h][d] = ldexpf(sm.qd_s[h][d], e_d);
+  for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
+    qi_s[i] = __float2int_rn(ldexpf(q_s[i], e_p));
+    qd_s[i] = ldexpf(qd_s[i], e_d);
   }
   __syncthreads();
-  const int ng = kD / a.k.group;  // channel groups per K token (valid for the packed K path)
-  if (a.k.asym) {
-    for (int i = threadIdx.x; i < R * ng; i += kWarps * 32) {
-      int h = i / ng, g = i % ng;
-      float s = 0.f;
-      for (int d = g * a.k.group; d < (g + 1) * a.k.group; ++d) s += sm.q_s[h][d];
-      sm.qsum_s[h][g] = s;
+  // per (head, channel group) sums of q: one warp per head, lanes over dims
+  for (int h = warp; h < RP; h += kWarps) {
+    int s[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s[c] = qi_s[h * kD + c * 32 + lane];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s[c] += __shfl_xor_sync(0xffffffffu, s[c], o);
+    if (lane < 4) {
+      int t = 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) t += (c / KPG == lane) ? s[c] : 0;
+      sm.ctot_s[h][lane] = koff * t;
+      sm.qsum_s[h][lane] = (float)t;
     }
   }
-  // dense-K B fragments (dtype hi/lo)
+  // packed-K B fragments (m16n8k32): n-tile 2*quad holds digits (d2, d1) and
+  // 2*quad+1 holds (d0, 0) of each of the quad's 4 heads
+  for (int i = threadIdx.x; i < 2 * NT * 4 * 32; i += kWarps * 32) {
+    const int ntk = i / 128, kb = (i / 32) % 4, ln = i % 32;
+    const int g2 = ln >> 2, t2 = ln & 3;
+    const int head = (ntk >> 1) * 4 + (g2 >> 1), which = g2 & 1;
+    uint32_t wrd[2] = {0u, 0u};
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        int d0, d1, d2;
+        digits3(qi_s[head * kD + kb * 32 + hf * 16 + 4 * t2 + u], d0, d1, d2);
+        const int dg = (ntk & 1) ? (which ? 0 : d0) : (which ? d1 : d2);
+        wrd[hf] |= (uint32_t)(dg & 255) << (8 * u);
+      }
+    sm.bk_s[ntk][kb][ln] = make_uint2(wrd[0], wrd[1]);
+  }
+  // dense-K B fragments (m16n8k16, dtype hi/lo of q * 2^e_d)
   for (int i = threadIdx.x; i < NT * 8 * 32; i += kWarps * 32) {
-    int nt = i / 256, kb = (i / 32) % 8, ln = i % 32;
-    int g2 = ln >> 2, t2 = ln & 3;
-    int head = nt * 4 + (g2 >> 1), part = g2 & 1;
-    uint16_t v[4];
+    const int nt = i / 256, kb = (i / 32) % 8, ln = i % 32;
+    const int g2 = ln >> 2, t2 = ln & 3;
+    const int head = nt * 4 + (g2 >> 1), part = g2 & 1;
     const int dd[4] = {kb * 16 + 2 * t2, kb * 16 + 2 * t2 + 1, kb * 16 + 2 * t2 + 8, kb * 16 + 2 * t2 + 9};
+    uint16_t v[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      float x = head < R ? sm.qd_s[head][dd[u]] : 0.f;
       uint16_t hi, lo;
-      split_hilo<DT>(x, hi, lo);
+      split_hilo<DT>(qd_s[head * kD + dd[u]], hi, lo);
       v[u] = part ? lo : hi;
     }
     sm.bd_s[nt][kb][ln] = make_uint2(pack2(v[0], v[1]), pack2(v[2], v[3]));
   }
-  // packed-K B fragments in registers (fp16 hi/lo of q*f*2^e_p)
-  uint32_t bk[NT][8][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    int head = nt * 4 + (gid >> 1), part = gid & 1;
-#pragma unroll
-    for (int kb = 0; kb < 8; ++kb) {
-      uint16_t v[4];
-      const int dd[4] = {kb * 16 + 2 * tq, kb * 16 + 2 * tq + 1, kb * 16 + 2 * tq + 8, kb * 16 + 2 * tq + 9};
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float x = head < R ? sm.q_s[head][dd[u]] : 0.f;
-        uint16_t hi, lo;
-        split_hilo<F16>(x, hi, lo);
-        v[u] = part ? lo : hi;
-      }
-      bk[nt][kb][0] = pack2(v[0], v[1]);
-      bk[nt][kb][1] = pack2(v[2], v[3]);
-    }
-  }
-  __syncthreads();
+  __syncthreads();  // prologue scratch in `dyn` is dead from here on
 
+  int ctot[NT][NG];
+  float qsf[NT][NG];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      ctot[nt][g] = sm.ctot_s[nt * 4 + tq][g];
+      qsf[nt][g] = sm.qsum_s[nt * 4 + tq][g];
+    }
   const float cp = ldexpf(a.scale_log2, -e_p);
   const float cd = ldexpf(a.scale_log2, -e_d);
-  const int ks = a.k.n_sink, nqk = a.k.n_q;
-  const int vs = a.v.n_sink, nqv = a.v.n_q;
-  const uint32_t kbias = bias_pair(a.k.asym ? 0 : (1 << (BK - 1)));
-  const uint32_t vbias = bias_pair(a.v.asym ? 0 : (1 << (BV - 1)));
   const int64_t kbh = (int64_t)b * a.Hkv + hk;
   const uint8_t* kcodes = a.k.codes ? a.k.codes + kbh * a.k.cap_tiles * tile_bytes(BK) : nullptr;
-  const uint16_t* kscale = a.k.scale ? a.k.scale + kbh * a.k.cap_tiles * 32 * ng : nullptr;
-  const uint16_t* kzero = a.k.zero ? a.k.zero + kbh * a.k.cap_tiles * 32 * ng : nullptr;
+  const uint16_t* kscale = a.k.scale ? a.k.scale + kbh * a.k.cap_tiles * 32 * NG : nullptr;
+  const uint16_t* kzero = a.k.zero ? a.k.zero + kbh * a.k.cap_tiles * 32 * NG : nullptr;
   const uint8_t* vcodes = a.v.codes ? a.v.codes + kbh * a.v.cap_tiles * tile_bytes(BV) : nullptr;
   const int64_t vgroups_cap = a.v.codes ? a.v.cap_tiles * 32 / a.v.group : 0;
   const uint16_t* vscale = a.v.scale ? a.v.scale + kbh * vgroups_cap * kD : nullptr;
   const uint16_t* vzero = a.v.zero ? a.v.zero + kbh * vgroups_cap * kD : nullptr;
+
+  // stage offsets
+  const int o_ks = tile_bytes(BK);
+  const int o_kz = o_ks + 64 * NG;
+  const int o_vc = o_kz + (kasym ? 64 * NG : 0);
+  const int o_vs = o_vc + tile_bytes(BV);
+  const int o_vz = o_vs + 256;
+  uint8_t* ring = dyn + (size_t)warp * kStages * SB;
+
+  auto is_fast = [&](int tile) -> bool {
+    const int t0 = a.t_first + tile * kTile;
+    return nqk > 0 && t0 >= ks && t0 + kTile <= ks + nqk && ((t0 - ks) & 31) == 0 && nqv > 0 &&
+           t0 >= vs && t0 + kTile <= vs + nqv;
+  };
+  const int n_my = tile_end - tile_beg - warp > 0 ? (tile_end - tile_beg - warp + kWarps - 1) / kWarps : 0;
+  auto issue = [&](int i) {
+    if (i >= n_my || lane != 0) return;
+    const int slot = i % kStages;
+    uint64_t* bar = &sm.bars[warp][slot];
+    const int tile = tile_beg + warp + kWarps * i;
+    if (!is_fast(tile)) {
+      mbar_arrive(bar);
+      return;
+    }
+    const int t0 = a.t_first + tile * kTile;
+    const int64_t tk = (t0 - ks) >> 5, tv = (t0 - vs) >> 5;
+    const int64_t gv = (t0 - vs) / a.v.group;
+    uint8_t* st = ring + slot * SB;
+    fence_proxy_async();
+    mbar_arrive_tx(bar, (uint32_t)SB);
+    bulk_g2s(st, kcodes + tk * tile_bytes(BK), tile_bytes(BK), bar);
+    bulk_g2s(st + o_ks, kscale + tk * 32 * NG, 64 * NG, bar);
+    if (kasym) bulk_g2s(st + o_kz, kzero + tk * 32 * NG, 64 * NG, bar);
+    bulk_g2s(st + o_vc, vcodes + tv * tile_bytes(BV), tile_bytes(BV), bar);
+    bulk_g2s(st + o_vs, vscale + gv * kD, 256, bar);
+    if (vasym) bulk_g2s(st + o_vz, vzero + gv * kD, 256, bar);
+  };
 
   float m_run[NT], l_run[NT], o[NT][8][2];
 #pragma unroll
@@ -278,255 +531,200 @@ decode_attn_kernel(const DevArgs a) {
     for (int mt = 0; mt < 8; ++mt) o[nt][mt][0] = o[nt][mt][1] = 0.f;
   }
 
+#pragma unroll 1
+  for (int s = 0; s < kStages; ++s) issue(s);
+  bool failed = false;
+  int i_done = 0;
+
   // ---------------------------------------------------------------- tiles
-  for (int tile = tile_beg + warp; tile < tile_end; tile += kWarps) {
-    const int t0 = a.t_first + tile * kTile;
-    float x[NT][4];
-    // row sources: 1 packed, 2 dense, 0 masked
-    int src[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      int t = t0 + gid + 8 * j;
-      src[j] = (t < 0 || t >= S) ? 0 : ((t >= ks && t < ks + nqk) ? 1 : 2);
+#pragma unroll 1
+  for (int i = 0; i < n_my; ++i) {
+    const int slot = i % kStages;
+    if (!mbar_wait_bounded(&sm.bars[warp][slot], (uint32_t)((i / kStages) & 1), kWaitLimit)) {
+      failed = true;
+      break;
     }
-    const int lo_t = max(t0, 0), hi_t = min(t0 + kTile, S);
-    const bool kp_any = nqk > 0 && lo_t < ks + nqk && hi_t > ks;
-    const bool kd_any = (lo_t < min(ks, hi_t)) || (hi_t > max(ks + nqk, lo_t));
+    i_done = i + 1;
+    const int tile = tile_beg + warp + kWarps * i;
+    const int t0 = a.t_first + tile * kTile;
+    const bool fast = is_fast(tile);
+    const uint8_t* st = ring + slot * SB;
+    float x[NT][4];
 
-    float lp[NT][4], ld[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) lp[nt][j] = ld[nt][j] = 0.f;
-
-    if (kp_any) {
+    // ----------------------------------------------------------- QK^T
+    if (fast) {
       KRow<BK> rw[4];
-      float sc[4][4], zc[4][4];
+      float sc[4][NG], zc[4][NG];
+      load_krows<BK>(rw, st, lane);
+      load_kscales<DT, NG>(sc, reinterpret_cast<const uint16_t*>(st + o_ks) + gid * 4 * NG);
+      if (kasym) load_kscales<DT, NG>(zc, reinterpret_cast<const uint16_t*>(st + o_kz) + gid * 4 * NG);
+      float lp[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) lp[nt][j] = 0.f;
+      k_packed_logits<BK, NT, NG>(rw, sc, zc, sm.bk_s, ctot, qsf, kasym, lane, lp);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const bool head_ok = nt * 4 + tq < R;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[nt][j] = head_ok ? lp[nt][j] * cp : -INFINITY;
+      }
+    } else {
+      int src[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int p = t0 + gid + 8 * j - ks;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) { sc[j][g] = 0.f; zc[j][g] = 0.f; }
-        if (src[j] == 1) {
-          const int ti = p >> 5, r = p & 31;
-          load_krow<BK>(rw[j], kcodes + (int64_t)ti * tile_bytes(BK), (r & 7) * 4 + tq, r >> 3);
-          const int64_t so = (int64_t)ti * 32 * ng + ((r & 7) * 4 + (r >> 3)) * ng;
-#pragma unroll
-          for (int g = 0; g < 4; ++g)
-            if (g < ng) sc[j][g] = to_f<DT>(kscale[so + g]);
-          if (a.k.asym) {
-#pragma unroll
-            for (int g = 0; g < 4; ++g)
-              if (g < ng) zc[j][g] = to_f<DT>(kzero[so + g]);
-          }
-        } else {
-#pragma unroll
-          for (int u = 0; u < (BK == 4 ? 4 : 3); ++u) rw[j].w[u] = 0;
-        }
+        const int t = t0 + gid + 8 * j;
+        src[j] = (t < 0 || t >= S) ? 0 : ((t >= ks && t < ks + nqk) ? 1 : 2);
       }
-      // k-blocks per channel group: 2 (G=32), 4 (G=64), 8 (G=128)
-      const int kpg_shift = a.k.group == 32 ? 1 : (a.k.group == 64 ? 2 : 3);
-      const int kpg_mask = (1 << kpg_shift) - 1;
-      float acc[2][NT][4];
+      const int lo_t = max(t0, 0), hi_t = min(t0 + kTile, S);
+      const bool kp_any = nqk > 0 && lo_t < ks + nqk && hi_t > ks;
+      const bool kd_any = (lo_t < min(ks, hi_t)) || (hi_t > max(ks + nqk, lo_t));
+      float lp[NT][4], ld[NT][4];
 #pragma unroll
-      for (int kb = 0; kb < 8; ++kb) {
-        if ((kb & kpg_mask) == 0) {
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int mt = 0; mt < 2; ++mt)
+        for (int j = 0; j < 4; ++j) lp[nt][j] = ld[nt][j] = 0.f;
+      if (kp_any) {
+        KRow<BK> rw[4];
+        float sc[4][NG], zc[4][NG];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-              acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
-        }
+        for (int j = 0; j < 4; ++j) {
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          uint32_t af[4];
-          af[0] = krow_pair<BK>(rw[2 * mt], kb, 0, kbias);
-          af[1] = krow_pair<BK>(rw[2 * mt + 1], kb, 0, kbias);
-          af[2] = krow_pair<BK>(rw[2 * mt], kb, 1, kbias);
-          af[3] = krow_pair<BK>(rw[2 * mt + 1], kb, 1, kbias);
+          for (int g = 0; g < NG; ++g) sc[j][g] = zc[j][g] = 0.f;
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_f16(acc[mt][nt], af, bk[nt][kb]);
-        }
-        if ((kb & kpg_mask) == kpg_mask) {
-          const int g = kb >> kpg_shift;
-          float s[4], z[4];
+          for (int u = 0; u < (BK == 4 ? 4 : 3); ++u) rw[j].w[u] = 0u;
+          if (src[j] == 1) {
+            const int p = t0 + gid + 8 * j - ks;
+            const int ti = p >> 5, r = p & 31;
+            load_krow<BK>(rw[j], kcodes + (int64_t)ti * tile_bytes(BK), (r & 7) * 4 + tq, r >> 3);
+            const int64_t so = (int64_t)ti * 32 * NG + ((r & 7) * 4 + (r >> 3)) * NG;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            s[j] = g == 0 ? sc[j][0] : g == 1 ? sc[j][1] : g == 2 ? sc[j][2] : sc[j][3];
-            z[j] = g == 0 ? zc[j][0] : g == 1 ? zc[j][1] : g == 2 ? zc[j][2] : zc[j][3];
-          }
-#pragma unroll
-          for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              lp[nt][2 * mt] += s[2 * mt] * (acc[mt][nt][0] + acc[mt][nt][1]);
-              lp[nt][2 * mt + 1] += s[2 * mt + 1] * (acc[mt][nt][2] + acc[mt][nt][3]);
-            }
-          if (a.k.asym) {
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              const int head = nt * 4 + tq;
-              const float qs = head < R ? sm.qsum_s[head][g] : 0.f;
-#pragma unroll
-              for (int j = 0; j < 4; ++j) lp[nt][j] += z[j] * qs;
+            for (int g = 0; g < NG; ++g) {
+              sc[j][g] = to_f<DT>(kscale[so + g]);
+              zc[j][g] = kasym ? to_f<DT>(kzero[so + g]) : 0.f;
             }
           }
         }
+        k_packed_logits<BK, NT, NG>(rw, sc, zc, sm.bk_s, ctot, qsf, kasym, lane, lp);
       }
-    }
-    if (kd_any) {
-      const uint16_t* rp[4];
+      if (kd_any) {
+        const uint16_t* rp[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        rp[j] = src[j] == 2 ? dense_row(a.k, b, hk, t0 + gid + 8 * j, S) : nullptr;
+        for (int j = 0; j < 4; ++j) rp[j] = src[j] == 2 ? dense_row(a.k, b, hk, t0 + gid + 8 * j, S) : nullptr;
 #pragma unroll
-      for (int kb = 0; kb < 8; ++kb) {
+        for (int kb = 0; kb < 8; ++kb)
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          uint32_t af[4];
-          const uint16_t* r0 = rp[2 * mt];
-          const uint16_t* r1 = rp[2 * mt + 1];
-          int c0 = kb * 16 + 2 * tq;
-          af[0] = r0 ? *reinterpret_cast<const uint32_t*>(r0 + c0) : 0u;
-          af[1] = r1 ? *reinterpret_cast<const uint32_t*>(r1 + c0) : 0u;
-          af[2] = r0 ? *reinterpret_cast<const uint32_t*>(r0 + c0 + 8) : 0u;
-          af[3] = r1 ? *reinterpret_cast<const uint32_t*>(r1 + c0 + 8) : 0u;
+          for (int mt = 0; mt < 2; ++mt) {
+            const uint16_t* r0 = rp[2 * mt];
+            const uint16_t* r1 = rp[2 * mt + 1];
+            const int c0 = kb * 16 + 2 * tq;
+            const uint32_t af[4] = {r0 ? *reinterpret_cast<const uint32_t*>(r0 + c0) : 0u,
+                                    r1 ? *reinterpret_cast<const uint32_t*>(r1 + c0) : 0u,
+                                    r0 ? *reinterpret_cast<const uint32_t*>(r0 + c0 + 8) : 0u,
+                                    r1 ? *reinterpret_cast<const uint32_t*>(r1 + c0 + 8) : 0u};
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            uint2 bb = sm.bd_s[nt][kb][lane];
-            uint32_t bf[2] = {bb.x, bb.y};
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
-            mma_dt<DT>(c, af, bf);
-            ld[nt][2 * mt] += c[0] + c[1];
-            ld[nt][2 * mt + 1] += c[2] + c[3];
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint2 bb = sm.bd_s[nt][kb][lane];
+              const uint32_t bf[2] = {bb.x, bb.y};
+              float c[4] = {0.f, 0.f, 0.f, 0.f};
+              mma_dt<DT>(c, af, bf);
+              ld[nt][2 * mt] += c[0] + c[1];
+              ld[nt][2 * mt + 1] += c[2] + c[3];
+            }
           }
-        }
       }
-    }
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const bool head_ok = nt * 4 + tq < R;
+      for (int nt = 0; nt < NT; ++nt) {
+        const bool head_ok = nt * 4 + tq < R;
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        x[nt][j] = (!head_ok || src[j] == 0) ? -INFINITY
-                   : (src[j] == 1 ? lp[nt][j] * cp : ld[nt][j] * cd);
+        for (int j = 0; j < 4; ++j)
+          x[nt][j] = (!head_ok || src[j] == 0) ? -INFINITY : (src[j] == 1 ? lp[nt][j] * cp : ld[nt][j] * cd);
+      }
     }
 
     // ------------------------------------------------------------ softmax
-    float psum[NT];
+    const bool vpacked = nqv > 0 && t0 >= vs && t0 + kTile <= vs + nqv;
+    float fv[NT];
+    int psum[NT];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      float mx = fmaxf(fmaxf(x[nt][0], x[nt][1]), fmaxf(x[nt][2], x[nt][3]));
-      mx = gid_max(mx);
+      const float mx = gid_max(fmaxf(fmaxf(x[nt][0], x[nt][1]), fmaxf(x[nt][2], x[nt][3])));
       const float m_new = fmaxf(m_run[nt], mx);
-      float alpha = 1.f, ps = 0.f;
-      float p[4];
-      if (m_new == -INFINITY) {
-        p[0] = p[1] = p[2] = p[3] = 0.f;
-      } else {
+      float pt[4] = {0.f, 0.f, 0.f, 0.f};
+      float alpha = 1.f, wt = 0.f;
+      if (mx != -INFINITY) {
         alpha = exp2f(m_run[nt] - m_new);
+        wt = exp2f(mx - m_new);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) { p[j] = exp2f(x[nt][j] - m_new); ps += p[j]; }
+        for (int j = 0; j < 4; ++j) pt[j] = exp2f(x[nt][j] - mx);
       }
       m_run[nt] = m_new;
-      l_run[nt] = l_run[nt] * alpha + ps;
+      l_run[nt] = l_run[nt] * alpha + wt * ((pt[0] + pt[1]) + (pt[2] + pt[3]));
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) { o[nt][mt][0] *= alpha; o[nt][mt][1] *= alpha; }
-      psum[nt] = ps;
+        for (int mt = 0; mt < 8; ++mt) { o[nt][mt][0] *= alpha; o[nt][mt][1] *= alpha; }
+      }
       const int head = nt * 4 + tq;
-      if (head < R) {
+      if (vpacked) {
+        int ps = 0;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) sm.p_s[warp][head][gid + 8 * j] = p[j];
+        for (int j = 0; j < 4; ++j) {
+          const int v = __float2int_rn(pt[j] * 65535.f);
+          ps += v;
+          sm.pd_s[warp][head][0][gid + 8 * j] = (uint8_t)(v >> 8);
+          sm.pd_s[warp][head][1][gid + 8 * j] = (uint8_t)(v & 255);
+        }
+        psum[nt] = gid_isum(ps);
+        fv[nt] = wt * (1.f / 65535.f);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sm.p_s[warp][head][gid + 8 * j] = pt[j] * wt;
       }
     }
     __syncwarp();
 
     // ------------------------------------------------------------------ PV
-    const bool vpacked = nqv > 0 && t0 >= vs && t0 + kTile <= vs + nqv;
     if (vpacked) {
-      if (a.v.asym) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) psum[nt] = gid_sum(psum[nt]);
-      }
-      uint32_t pb[NT][2][2];
+      uint32_t pb[NT][2];
+      int offp[NT];
+      float zf[NT];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const int head = nt * 4 + (gid >> 1), part = gid & 1;
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-          uint16_t v[4];
-          const int rr[4] = {kb * 16 + 2 * tq, kb * 16 + 2 * tq + 1, kb * 16 + 2 * tq + 8, kb * 16 + 2 * tq + 9};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float pv = head < R ? sm.p_s[warp][head][rr[u]] : 0.f;
-            uint16_t hi, lo;
-            split_hilo<F16>(pv, hi, lo);
-            v[u] = part ? lo : hi;
-          }
-          pb[nt][kb][0] = pack2(v[0], v[1]);
-          pb[nt][kb][1] = pack2(v[2], v[3]);
-        }
+        const int head = nt * 4 + (gid >> 1), digit = gid & 1;
+        pb[nt][0] = *reinterpret_cast<const uint32_t*>(&sm.pd_s[warp][head][digit][4 * tq]);
+        pb[nt][1] = *reinterpret_cast<const uint32_t*>(&sm.pd_s[warp][head][digit][16 + 4 * tq]);
+        offp[nt] = voff * psum[nt];
+        zf[nt] = (float)psum[nt] * fv[nt];
       }
-      const int pv_tok = t0 - vs;
       VChunk<BV> vc;
-      load_vchunk<BV>(vc, vcodes + (int64_t)(pv_tok >> 5) * tile_bytes(BV), lane);
-      const int gg = pv_tok / a.v.group;
-      uint16_t sv[16], zv[16];
-      {
-        const uint4* sp = reinterpret_cast<const uint4*>(vscale + (int64_t)gg * kD + gid * 16);
-        uint4 s0 = sp[0], s1 = sp[1];
-        const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-        for (int u = 0; u < 8; ++u) { sv[2 * u] = sw[u] & 0xffff; sv[2 * u + 1] = sw[u] >> 16; }
-        if (a.v.asym) {
-          const uint4* zp = reinterpret_cast<const uint4*>(vzero + (int64_t)gg * kD + gid * 16);
-          uint4 z0 = zp[0], z1 = zp[1];
-          const uint32_t zw[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
-#pragma unroll
-          for (int u = 0; u < 8; ++u) { zv[2 * u] = zw[u] & 0xffff; zv[2 * u + 1] = zw[u] >> 16; }
-        }
+      float sv[16], zv[16];
+      if (fast) {
+        load_vchunk<BV>(vc, st + o_vc, lane);
+        load16<DT>(sv, reinterpret_cast<const uint16_t*>(st + o_vs) + gid * 16);
+        if (vasym) load16<DT>(zv, reinterpret_cast<const uint16_t*>(st + o_vz) + gid * 16);
+      } else {
+        const int pv = t0 - vs;
+        load_vchunk<BV>(vc, vcodes + (int64_t)(pv >> 5) * tile_bytes(BV), lane);
+        const int64_t gg = pv / a.v.group;
+        load16<DT>(sv, vscale + gg * kD + gid * 16);
+        if (vasym) load16<DT>(zv, vzero + gg * kD + gid * 16);
       }
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        float acc[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-          uint32_t af[4];
-          af[0] = vchunk_pair<BV>(vc, mt, 0, kb, 0, vbias);
-          af[1] = vchunk_pair<BV>(vc, mt, 1, kb, 0, vbias);
-          af[2] = vchunk_pair<BV>(vc, mt, 0, kb, 1, vbias);
-          af[3] = vchunk_pair<BV>(vc, mt, 1, kb, 1, vbias);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_f16(acc[nt], af, pb[nt][kb]);
-        }
-        const float s0 = to_f<DT>(sv[mt * 2]), s1 = to_f<DT>(sv[mt * 2 + 1]);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          o[nt][mt][0] += s0 * (acc[nt][0] + acc[nt][1]);
-          o[nt][mt][1] += s1 * (acc[nt][2] + acc[nt][3]);
-          if (a.v.asym) {
-            o[nt][mt][0] += to_f<DT>(zv[mt * 2]) * psum[nt];
-            o[nt][mt][1] += to_f<DT>(zv[mt * 2 + 1]) * psum[nt];
-          }
-        }
-      }
+      v_packed_accumulate<BV, NT, DT>(vc, sv, zv, pb, offp, fv, zf, vasym, o);
     } else {
-      // dense V tile (sink / recent / masked rows)
+      // dense V tile (sink / recent / masked rows), probabilities as dtype hi/lo
       uint32_t pb[NT][2][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int head = nt * 4 + (gid >> 1), part = gid & 1;
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) {
-          uint16_t v[4];
           const int rr[4] = {kb * 16 + 2 * tq, kb * 16 + 2 * tq + 1, kb * 16 + 2 * tq + 8, kb * 16 + 2 * tq + 9};
+          uint16_t v[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            float pv = head < R ? sm.p_s[warp][head][rr[u]] : 0.f;
             uint16_t hi, lo;
-            split_hilo<DT>(pv, hi, lo);
+            split_hilo<DT>(sm.p_s[warp][head][rr[u]], hi, lo);
             v[u] = part ? lo : hi;
           }
           pb[nt][kb][0] = pack2(v[0], v[1]);
@@ -539,8 +737,8 @@ decode_attn_kernel(const DevArgs a) {
         const int rr[4] = {kb * 16 + 2 * tq, kb * 16 + 2 * tq + 1, kb * 16 + 2 * tq + 8, kb * 16 + 2 * tq + 9};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          int t = t0 + rr[u];
-          bool dense = t >= 0 && t < S && !(t >= vs && t < vs + nqv);
+          const int t = t0 + rr[u];
+          const bool dense = t >= 0 && t < S && !(t >= vs && t < vs + nqv);
           vp[kb][u] = dense ? dense_row(a.v, b, hk, t, S) : nullptr;
         }
       }
@@ -558,11 +756,8 @@ decode_attn_kernel(const DevArgs a) {
             e[u][0] = vp[kb][u] ? vp[kb][u][d0] : (uint16_t)0;
             e[u][1] = vp[kb][u] ? vp[kb][u][d0 + 8] : (uint16_t)0;
           }
-          uint32_t af[4];
-          af[0] = pack2(e[0][0], e[1][0]);
-          af[1] = pack2(e[0][1], e[1][1]);
-          af[2] = pack2(e[2][0], e[3][0]);
-          af[3] = pack2(e[2][1], e[3][1]);
+          const uint32_t af[4] = {pack2(e[0][0], e[1][0]), pack2(e[0][1], e[1][1]),
+                                  pack2(e[2][0], e[3][0]), pack2(e[2][1], e[3][1])};
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) mma_dt<DT>(acc[nt], af, pb[nt][kb]);
         }
@@ -574,20 +769,31 @@ decode_attn_kernel(const DevArgs a) {
       }
     }
     __syncwarp();
+    issue(i + kStages);
+  }
+
+  if (failed) {
+    // a staged tile never arrived: wait (bounded) for this warp's copies still
+    // in flight, then publish NaN so the caller sees the failure
+#pragma unroll 1
+    for (int i = i_done; i < min(n_my, i_done + kStages); ++i)
+      mbar_wait_bounded(&sm.bars[warp][i % kStages], (uint32_t)((i / kStages) & 1), kWaitLimit);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) { m_run[nt] = NAN; l_run[nt] = NAN; }
   }
 
   // ------------------------------------------------------- combine warps
+  __syncthreads();  // the ring is idle; reuse it for the per-warp outputs
+  float* co_s = reinterpret_cast<float*>(dyn);  // [kWarps][RP][128]
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const float l = gid_sum(l_run[nt]);
     const int head = nt * 4 + tq;
-    if (head < R) {
-      if (gid == 0) { sm.cm_s[warp][head] = m_run[nt]; sm.cl_s[warp][head] = l; }
+    if (gid == 0) { sm.cm_s[warp][head] = m_run[nt]; sm.cl_s[warp][head] = l; }
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        sm.co_s[warp][head][mt * 16 + gid] = o[nt][mt][0];
-        sm.co_s[warp][head][mt * 16 + 8 + gid] = o[nt][mt][1];
-      }
+    for (int mt = 0; mt < 8; ++mt) {
+      co_s[(warp * RP + head) * kD + mt * 16 + gid] = o[nt][mt][0];
+      co_s[(warp * RP + head) * kD + mt * 16 + 8 + gid] = o[nt][mt][1];
     }
   }
   __syncthreads();
@@ -602,7 +808,7 @@ decode_attn_kernel(const DevArgs a) {
       for (int w = 0; w < kWarps; ++w) {
         const float mw = sm.cm_s[w][head];
         const float wt = mw == -INFINITY ? 0.f : exp2f(mw - M);
-        ov += wt * sm.co_s[w][head][d];
+        ov += wt * co_s[(w * RP + head) * kD + d];
         lv += wt * sm.cl_s[w][head];
       }
     }

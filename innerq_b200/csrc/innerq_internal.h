@@ -29,8 +29,15 @@ cudaError_t launch_dequant_ref(const int32_t* c, const void* s, const void* zs, 
                                cudaStream_t st);
 // record the message innerq_last_error() returns on this thread; returns code
 int set_last_error(int code, const char* fmt, ...);
-// decode attention, one translation unit per K bit width
-cudaError_t launch_attn_k2(const DevArgs& a, int bv, int R, int dt, dim3 grid, cudaStream_t s);
-cudaError_t launch_attn_k3(const DevArgs& a, int bv, int R, int dt, dim3 grid, cudaStream_t s);
-cudaError_t launch_attn_k4(const DevArgs& a, int bv, int R, int dt, dim3 grid, cudaStream_t s);
+// decode attention, one translation unit per (K bits, dtype); rp = query heads
+// per KV head padded to 4 or 8, ng = K channel groups per token (4, 2, 1)
+#define INNERQ_DECL_ATTN(name) \
+  cudaError_t name(const DevArgs& a, int bv, int rp, int ng, dim3 grid, cudaStream_t s);
+INNERQ_DECL_ATTN(launch_attn_k2_f16)
+INNERQ_DECL_ATTN(launch_attn_k2_bf16)
+INNERQ_DECL_ATTN(launch_attn_k3_f16)
+INNERQ_DECL_ATTN(launch_attn_k3_bf16)
+INNERQ_DECL_ATTN(launch_attn_k4_f16)
+INNERQ_DECL_ATTN(launch_attn_k4_bf16)
+#undef INNERQ_DECL_ATTN
 }  // namespace innerq

@@ -51,7 +51,7 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
                         uint8_t* __restrict__ codes, uint16_t* __restrict__ scale,
                         uint16_t* __restrict__ zero, int64_t cap_tiles, int64_t t_off,
                         int64_t n_rows) {
-  __shared__ uint8_t cbuf[4][kD];
+  __shared__ uint32_t wbuf[4][16];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 4 + warp;
   if (row >= n_rows) return;
@@ -102,30 +102,36 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
     scale[si] = from_f<DT>(s);
     if (asym) zero[si] = from_f<DT>(z);
   }
+  // assemble the row's four lane segments (one per tq) with the layout map
+  uint32_t* seg = wbuf[warp];
+  constexpr int kWordsPerSeg = BITS == 4 ? 4 : (BITS == 2 ? 2 : 3);  // b=3: L0, L1, H
+  if (lane < 4 * kWordsPerSeg) seg[lane] = 0u;
+  __syncwarp();
 #pragma unroll
-  for (int i = 0; i < 4; ++i) cbuf[warp][4 * lane + i] = (uint8_t)u[i];
+  for (int i = 0; i < 4; ++i) {
+    const int d = 4 * lane + i;
+    const BitPos bp = row_pos(BITS, r, d);
+    const int tq = (d >> 2) & 3;
+    const uint32_t uc = (uint32_t)u[i];
+    if (BITS == 4) {
+      atomicOr(&seg[tq * 4 + ((bp.off & 15) >> 2)], uc << bp.shift);
+    } else {
+      atomicOr(&seg[tq * kWordsPerSeg + ((bp.off & 7) >> 2)], (uc & 3u) << bp.shift);
+      if (BITS == 3) atomicOr(&seg[tq * 3 + 2], (uc >> 2) << bp.hshift);
+    }
+  }
   __syncwarp();
   if (lane < 4) {
     const int tq = lane;
-    uint32_t w[4] = {0, 0, 0, 0};
-    uint32_t wh = 0;
-    for (int c = 0; c < 32; ++c) {
-      const int kb = c >> 2, hi8 = (c >> 1) & 1, e = c & 1;
-      const uint32_t uc = cbuf[warp][kb * 16 + hi8 * 8 + 2 * tq + e];
-      if (BITS == 4) {
-        w[kb >> 1] |= uc << (4 * ((kb & 1) * 2 + hi8 + 4 * e));
-      } else {
-        w[kb >> 2] |= (uc & 3u) << (2 * ((kb & 3) * 2 + hi8 + 8 * e));
-        if (BITS == 3) wh |= (uc >> 2) << (kb * 2 + hi8 + 16 * e);
-      }
-    }
     uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
     const int lane2 = (r & 7) * 4 + tq, j = r >> 3;
     if (BITS == 4) {
-      *reinterpret_cast<uint4*>(tb + lane2 * 64 + j * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(tb + lane2 * 64 + j * 16) =
+          make_uint4(seg[tq * 4], seg[tq * 4 + 1], seg[tq * 4 + 2], seg[tq * 4 + 3]);
     } else {
-      *reinterpret_cast<uint2*>(tb + lane2 * 32 + j * 8) = make_uint2(w[0], w[1]);
-      if (BITS == 3) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = wh;
+      *reinterpret_cast<uint2*>(tb + lane2 * 32 + j * 8) =
+          make_uint2(seg[tq * kWordsPerSeg], seg[tq * kWordsPerSeg + 1]);
+      if (BITS == 3) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = seg[tq * 3 + 2];
     }
   }
 }
@@ -141,6 +147,7 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
                       uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
                       int64_t cap_tiles, int64_t t_off) {
   __shared__ uint8_t cb[128][kD];
+  __shared__ __align__(16) uint32_t tw[4 * tile_bytes(4) / 4];
   const int gi = blockIdx.x, h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
   const int64_t bh = (int64_t)b * H + h;
   const int d = threadIdx.x;
@@ -177,47 +184,27 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
   scale[si] = from_f<DT>(s);
   if (asym) zero[si] = from_f<DT>(z);
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
-  for (int tile = warp; tile < group / 32; tile += 4) {
-    uint32_t w[16];
-    uint32_t wh[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int i = 0; i < 16; ++i) w[i] = 0;
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int hi8 = 0; hi8 < 2; ++hi8)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int dd = mt * 16 + hh * 8 + gid;
-              const int r = kb * 16 + hi8 * 8 + 2 * tq + e;
-              const uint32_t uc = cb[tile * 32 + r][dd];
-              if (BITS == 4) {
-                w[mt * 2 + hh] |= uc << (4 * (kb * 2 + hi8 + 4 * e));
-              } else {
-                w[mt] |= (uc & 3u) << (2 * (hh * 4 + kb * 2 + hi8 + 8 * e));
-                if (BITS == 3)
-                  wh[mt >> 1] |= (uc >> 2) << ((mt & 1) * 8 + hh * 4 + kb * 2 + hi8 + 16 * e);
-              }
-            }
-    const int64_t ti = (t_off + (int64_t)gi * group) / 32 + tile;
-    uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
+  // assemble each 32-token tile of the group in shared memory with the layout map
+  const int n_tiles = group / 32;
+  constexpr int TW = tile_bytes(BITS) / 4;
+  for (int i = threadIdx.x; i < n_tiles * TW; i += blockDim.x) tw[i] = 0u;
+  __syncthreads();
+  for (int t = 0; t < group; ++t) {
+    const uint32_t uc = cb[t][d];
+    const BitPos bp = col_pos(BITS, t & 31, d);
+    uint32_t* w = tw + (t >> 5) * TW;
     if (BITS == 4) {
-      uint4* o = reinterpret_cast<uint4*>(tb + lane * 64);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      atomicOr(&w[bp.off >> 2], uc << bp.shift);
     } else {
-      uint4* o = reinterpret_cast<uint4*>(tb + lane * 32);
-      o[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      o[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      if (BITS == 3)
-        *reinterpret_cast<uint4*>(tb + 1024 + lane * 16) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+      atomicOr(&w[bp.off >> 2], (uc & 3u) << bp.shift);
+      if (BITS == 3) atomicOr(&w[bp.hoff >> 2], (uc >> 2) << bp.hshift);
     }
   }
+  __syncthreads();
+  const int64_t ti0 = (t_off + (int64_t)gi * group) / 32;
+  uint4* dst = reinterpret_cast<uint4*>(codes + (bh * cap_tiles + ti0) * tile_bytes(BITS));
+  const uint4* src = reinterpret_cast<const uint4*>(tw);
+  for (int i = threadIdx.x; i < n_tiles * TW / 4; i += blockDim.x) dst[i] = src[i];
 }
 
 // --------------------------------------------------------------------------

@@ -140,7 +140,7 @@ def test_decode_attention_vs_oracle(case):
     for ns in (0, 1, 7):
         po, pm, pl = decode_attention_partials(q, layer.key_side, layer.value_side, n_splits=ns)
         o64, lse2 = merge_np(po.cpu().numpy(), pm.cpu().numpy(), pl.cpu().numpy())
-        assert_close_rel(o64, ref32[:, :, 0], 2e-5, f"tight n_splits={ns}")
+        assert_close_rel(o64, ref32[:, :, 0], 1e-4, f"tight n_splits={ns}")
         lse_ref = np.log2(np.exp(logits - logits.max(-1, keepdims=True)).sum(-1)) \
             + logits.max(-1) / math.log(2)
         np.testing.assert_allclose(lse2, lse_ref[:, :, 0], rtol=0, atol=2e-4)
