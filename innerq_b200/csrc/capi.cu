@@ -106,12 +106,19 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   const int ntr = p.tile_hi - p.tile_lo;
   int splits = a->n_splits;
   if (splits <= 0) {
-    const int bh = a->B * a->Hkv;
-    const int slots = sm_count() * (p.R == 8 ? 2 : 3);
-    splits = (8 * slots + bh - 1) / bh;
-    splits = splits < 1 ? 1 : splits;
-    const int max_by_work = ntr / 8 > 1 ? ntr / 8 : 1;
-    if (splits > max_by_work) splits = max_by_work;
+    // cost model: waves of resident CTAs x (tiles per CTA + per-CTA overhead
+    // worth ~12 tiles); the best split count balances wave quantisation
+    // against the fixed prologue/epilogue of each CTA
+    const int64_t bh = (int64_t)a->B * a->Hkv;
+    const int64_t slots = (int64_t)sm_count() * (p.R <= 4 ? 4 : 2);
+    int64_t best = -1;
+    splits = 1;
+    for (int s = 1; s <= 256 && s <= (ntr > 0 ? ntr : 1); ++s) {
+      const int64_t tpc = (ntr + s - 1) / s;
+      const int64_t waves = (bh * s + slots - 1) / slots;
+      const int64_t cost = waves * (tpc + 12);
+      if (best < 0 || cost < best) { best = cost; splits = s; }
+    }
   }
   if (splits > 65535) splits = 65535;
   p.tps = ntr > 0 ? (ntr + splits - 1) / splits : 1;

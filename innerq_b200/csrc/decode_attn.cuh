@@ -12,11 +12,13 @@
 // partial (O, m, l) per query head; lse_merge combines splits (and GPUs when
 // context chunks are sharded).
 //
-// Staging: tiles whose K and V are both packed ("fast" tiles, the whole middle
-// of the cache) are fetched by the TMA engine with cp.async.bulk into a
-// per-warp ring of kStages shared-memory slots, completion tracked by one
-// mbarrier per slot (no multicast).  Boundary tiles (sink, recent, the K/V
-// packed/dense seams) load directly from global memory.
+// Staging: the 4 warps take 4 consecutive tiles at a time (a stage).  Stages
+// whose K and V are all packed (the whole middle of the cache) are fetched by
+// the TMA engine with a handful of cp.async.bulk copies into a CTA ring of
+// stages_for(RP) slots, completion tracked by one mbarrier per slot (no
+// multicast); the last warp to finish with a slot issues its refill.
+// Boundary tiles (sink, recent, the K/V packed/dense seams) load directly
+// from global memory.
 //
 // Arithmetic: packed codes are multiplied on the tensor cores with
 // mma.sync m16n8k32 u8 x s8/u8 -> s32, so every partial dot product is exact:
@@ -67,15 +69,19 @@ struct DevArgs {
 };
 
 constexpr int kWarps = 4;
-constexpr int kStages = 3;
-constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier wait (iterations)
+// staging slots per warp: 2 where 4 CTAs share an SM (<= 4 query heads per
+// KV head), 3 where 2 CTAs do
+__host__ __device__ constexpr int stages_for(int rp) { return rp <= 4 ? 2 : 3; }
+// bounded mbarrier wait: each try suspends the warp for up to ~100 us (hint,
+// in ns) instead of spinning; 1 << 16 tries bound the wait to seconds
+constexpr uint32_t kWaitLimit = 1u << 16;
 
 // bytes of one staged tile (K codes, K scales [, K zeros], V codes, V scales [, V zeros])
 __host__ __device__ inline int stage_bytes(int bk, int bv, int ng, int kasym, int vasym) {
   return tile_bytes(bk) + 64 * ng * (1 + kasym) + tile_bytes(bv) + 256 * (1 + vasym);
 }
-__host__ __device__ inline int attn_dyn_smem(int bk, int bv, int ng, int kasym, int vasym) {
-  return kWarps * kStages * stage_bytes(bk, bv, ng, kasym, vasym);
+__host__ __device__ inline int attn_dyn_smem(int bk, int bv, int ng, int kasym, int vasym, int rp) {
+  return kWarps * stages_for(rp) * stage_bytes(bk, bv, ng, kasym, vasym);
 }
 
 // ------------------------------------------------------------ PTX helpers ---
@@ -98,7 +104,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -120,6 +126,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 2^x with the MUFU approximation (ex2.approx.ftz.f32: ~2 ulp; 2^-inf = 0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -235,10 +248,21 @@ __device__ __forceinline__ const uint16_t* dense_row(const DevSide& s, int b, in
 }
 
 
+// a tile whose 32 K rows and 32 V rows all sit in the packed stores, both
+// tile-aligned: it is staged by the bulk-copy ring
+__device__ __forceinline__ bool is_fast_tile(const DevArgs& a, int tile) {
+  const int t0 = a.t_first + tile * kTile;
+  const int ks = a.k.n_sink, nqk = a.k.n_q, vs = a.v.n_sink, nqv = a.v.n_q;
+  return nqk > 0 && t0 >= ks && t0 + kTile <= ks + nqk && ((t0 - ks) & 31) == 0 && nqv > 0 &&
+         t0 >= vs && t0 + kTile <= vs + nqv;
+}
+
 template <int RP>
 struct AttnStatic {
   static constexpr int NT = RP / 4;
-  uint64_t bars[kWarps][kStages];
+  static constexpr int kStages = stages_for(RP);
+  uint64_t bars[kStages];     // "stage full" barriers of the CTA's staging ring
+  int cnt[kStages];           // warps done with each stage
   int ctot_s[RP][4];          // K offset correction per channel group: off * sum q
   float qsum_s[RP][4];        // sum of q over each K channel group (asymmetric zero term)
   uint2 bk_s[2 * NT][4][32];  // packed-K B fragments (three int8 digits of q)
@@ -261,11 +285,11 @@ __device__ __forceinline__ void digits3(int v, int& d0, int& d1, int& d2) {
 // Logits (before the softmax scale) of the lane's 4 token rows for its
 // head(s) from packed K words: lp[nt][j] += sum_g s[j][g] * (sum_d u q - off*sum_d q)
 // (+ z[j][g] * sum_d q for asymmetric keys).  All partial sums are exact int32.
-template <int BK, int NT, int NG>
+template <int BK, int NT, int NG, bool KASYM>
 __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const float sc[4][NG],
                                                 const float zc[4][NG], const uint2 (*bks)[4][32],
                                                 const int ctot[NT][NG], const float qsf[NT][NG],
-                                                int kasym, int lane, float lp[NT][4]) {
+                                                int lane, float lp[NT][4]) {
   constexpr int KPG = 4 / NG;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -298,7 +322,7 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
             const uint32_t t = (uint32_t)acc[mt][0][2 * rr] * 65536u +
                                (uint32_t)acc[mt][0][2 * rr + 1] * 256u + (uint32_t)acc[mt][1][2 * rr];
             lp[nt][j] = fmaf(sc[j][g], (float)(int)t, lp[nt][j]);
-            if (kasym) lp[nt][j] = fmaf(zc[j][g], qsf[nt][g], lp[nt][j]);
+            if constexpr (KASYM) lp[nt][j] = fmaf(zc[j][g], qsf[nt][g], lp[nt][j]);
           }
       }
     }
@@ -307,11 +331,11 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
 
 // O[nt][mt][h] += fv * (s * (sum_t u p - off * sum_t p) [+ z * sum_t p]) for one
 // packed V tile (integer MMA, probabilities as two u8 digits)
-template <int BV, int NT, int DT>
+template <int BV, int NT, bool VASYM>
 __device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const float sv[16],
                                                     const float zv[16], const uint32_t pb[NT][2],
                                                     const int offp[NT], const float fv[NT],
-                                                    const float zf[NT], int vasym, float o[NT][8][2]) {
+                                                    const float zf[NT], float o[NT][8][2]) {
   float svf[NT][16];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -329,7 +353,7 @@ __device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const 
       for (int hh = 0; hh < 2; ++hh) {
         const int t = acc[2 * hh] * 256 + acc[2 * hh + 1];
         o[nt][mt][hh] = fmaf(svf[nt][mt * 2 + hh], (float)t, o[nt][mt][hh]);
-        if (vasym) o[nt][mt][hh] = fmaf(zv[mt * 2 + hh], zf[nt], o[nt][mt][hh]);
+        if constexpr (VASYM) o[nt][mt][hh] = fmaf(zv[mt * 2 + hh], zf[nt], o[nt][mt][hh]);
       }
     }
   }
@@ -359,9 +383,10 @@ __device__ __forceinline__ void load_kscales(float out[4][NG], const uint16_t* p
 // BK/BV: code bits; RP: query heads per KV head padded to 4 or 8; DT: dtype;
 // NG: K channel groups per token (4, 2, 1 for groups of 32, 64, 128)
 template <int BK, int BV, int RP, int DT, int NG>
-__global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 3 : 2)
+__global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 2)
 decode_attn_kernel(const DevArgs a) {
   constexpr int NT = RP / 4;
+  constexpr int kStages = stages_for(RP);
   constexpr int KPG = 4 / NG;           // 32-dim k-blocks per channel group
   constexpr int QBITS = NG == 4 ? 22 : (NG == 2 ? 21 : 20);  // |q int| < 2^QBITS
   extern __shared__ __align__(128) uint8_t dyn[];
@@ -400,7 +425,10 @@ decode_attn_kernel(const DevArgs a) {
   amax_p = warp_max(amax_p);
   amax_d = warp_max(amax_d);
   if (lane == 0) { sm.red_s[0][warp] = amax_p; sm.red_s[1][warp] = amax_d; }
-  if (threadIdx.x < kWarps * kStages) mbar_init(&sm.bars[0][0] + threadIdx.x, 1);
+  if (threadIdx.x < kStages) {
+    mbar_init(&sm.bars[threadIdx.x], 1);
+    sm.cnt[threadIdx.x] = 0;
+  }
   mbar_fence_init();
   __syncthreads();
   amax_p = fmaxf(fmaxf(sm.red_s[0][0], sm.red_s[0][1]), fmaxf(sm.red_s[0][2], sm.red_s[0][3]));
@@ -448,8 +476,10 @@ decode_attn_kernel(const DevArgs a) {
       }
     sm.bk_s[ntk][kb][ln] = make_uint2(wrd[0], wrd[1]);
   }
-  // dense-K B fragments (m16n8k16, dtype hi/lo of q * 2^e_d)
-  for (int i = threadIdx.x; i < NT * 8 * 32; i += kWarps * 32) {
+  // dense-K B fragments (m16n8k16, dtype hi/lo of q * 2^e_d), only for CTAs
+  // that meet a sink / recent / seam tile (packed tiles form one contiguous run)
+  const bool any_dense = tile_end > tile_beg && !(is_fast_tile(a, tile_beg) && is_fast_tile(a, tile_end - 1));
+  for (int i = threadIdx.x; any_dense && i < NT * 8 * 32; i += kWarps * 32) {
     const int nt = i / 256, kb = (i / 32) % 8, ln = i % 32;
     const int g2 = ln >> 2, t2 = ln & 3;
     const int head = nt * 4 + (g2 >> 1), part = g2 & 1;
@@ -485,41 +515,54 @@ decode_attn_kernel(const DevArgs a) {
   const uint16_t* vscale = a.v.scale ? a.v.scale + kbh * vgroups_cap * kD : nullptr;
   const uint16_t* vzero = a.v.zero ? a.v.zero + kbh * vgroups_cap * kD : nullptr;
 
-  // stage offsets
-  const int o_ks = tile_bytes(BK);
-  const int o_kz = o_ks + 64 * NG;
-  const int o_vc = o_kz + (kasym ? 64 * NG : 0);
-  const int o_vs = o_vc + tile_bytes(BV);
-  const int o_vz = o_vs + 256;
-  uint8_t* ring = dyn + (size_t)warp * kStages * SB;
+  // One ring per CTA: stage i holds the kWarps consecutive tiles
+  // tile_beg + kWarps*i + w (warp w takes tile w).  Layout of a stage:
+  // [K codes x4 | K scales x4 | K zeros x4 | V codes x4 | V scales | V zeros]
+  const int TBK = tile_bytes(BK), TBV = tile_bytes(BV);
+  const int o_ks = kWarps * TBK;
+  const int o_kz = o_ks + kWarps * 64 * NG;
+  const int o_vc = o_kz + (kasym ? kWarps * 64 * NG : 0);
+  const int o_vs = o_vc + kWarps * TBV;
+  const int o_vz = o_vs + kWarps * 256;
+  const int SBC = kWarps * SB;  // bytes of a stage (same total as kWarps per-tile slots)
+  uint8_t* ring = dyn;
 
-  auto is_fast = [&](int tile) -> bool {
-    const int t0 = a.t_first + tile * kTile;
-    return nqk > 0 && t0 >= ks && t0 + kTile <= ks + nqk && ((t0 - ks) & 31) == 0 && nqv > 0 &&
-           t0 >= vs && t0 + kTile <= vs + nqv;
+  // packed tiles form one contiguous run [fast_lo, fast_hi) of tile indices
+  int fast_lo = 0, fast_hi = 0;
+  if (nqk > 0 && nqv > 0 && ((vs - ks) & 31) == 0) {
+    const int lo_tok = max(ks, vs), hi_tok = min(ks + nqk, vs + nqv);
+    fast_lo = (lo_tok - a.t_first + 31) >> 5;
+    fast_hi = (hi_tok - a.t_first) >> 5;  // floor: the tile must end inside
+  }
+  const int n_st = (tile_end - tile_beg + kWarps - 1) / kWarps;
+  auto stage_fast = [&](int i) -> bool {
+    const int ta = tile_beg + kWarps * i, tb = min(ta + kWarps, tile_end) - 1;
+    return ta >= fast_lo && tb < fast_hi;
   };
-  const int n_my = tile_end - tile_beg - warp > 0 ? (tile_end - tile_beg - warp + kWarps - 1) / kWarps : 0;
+  // issued by one thread: the last warp to release the slot (or thread 0 at start)
   auto issue = [&](int i) {
-    if (i >= n_my || lane != 0) return;
+    if (i >= n_st) return;
     const int slot = i % kStages;
-    uint64_t* bar = &sm.bars[warp][slot];
-    const int tile = tile_beg + warp + kWarps * i;
-    if (!is_fast(tile)) {
+    uint64_t* bar = &sm.bars[slot];
+    if (!stage_fast(i)) {
       mbar_arrive(bar);
       return;
     }
-    const int t0 = a.t_first + tile * kTile;
+    const int ta = tile_beg + kWarps * i, n_in = min(kWarps, tile_end - ta);
+    const int t0 = a.t_first + ta * kTile;
     const int64_t tk = (t0 - ks) >> 5, tv = (t0 - vs) >> 5;
-    const int64_t gv = (t0 - vs) / a.v.group;
-    uint8_t* st = ring + slot * SB;
+    const int64_t g0 = (t0 - vs) / a.v.group, g1 = (t0 + n_in * kTile - 1 - vs) / a.v.group;
+    const uint32_t nvg = (uint32_t)(g1 - g0 + 1);
+    uint8_t* st = ring + slot * SBC;
+    const uint32_t kb = n_in * (TBK + 64 * NG * (1 + kasym)), vb = n_in * TBV + nvg * 256 * (1 + vasym);
     fence_proxy_async();
-    mbar_arrive_tx(bar, (uint32_t)SB);
-    bulk_g2s(st, kcodes + tk * tile_bytes(BK), tile_bytes(BK), bar);
-    bulk_g2s(st + o_ks, kscale + tk * 32 * NG, 64 * NG, bar);
-    if (kasym) bulk_g2s(st + o_kz, kzero + tk * 32 * NG, 64 * NG, bar);
-    bulk_g2s(st + o_vc, vcodes + tv * tile_bytes(BV), tile_bytes(BV), bar);
-    bulk_g2s(st + o_vs, vscale + gv * kD, 256, bar);
-    if (vasym) bulk_g2s(st + o_vz, vzero + gv * kD, 256, bar);
+    mbar_arrive_tx(bar, kb + vb);
+    bulk_g2s(st, kcodes + tk * TBK, n_in * TBK, bar);
+    bulk_g2s(st + o_ks, kscale + tk * 32 * NG, n_in * 64 * NG, bar);
+    if (kasym) bulk_g2s(st + o_kz, kzero + tk * 32 * NG, n_in * 64 * NG, bar);
+    bulk_g2s(st + o_vc, vcodes + tv * TBV, n_in * TBV, bar);
+    bulk_g2s(st + o_vs, vscale + g0 * kD, nvg * 256, bar);
+    if (vasym) bulk_g2s(st + o_vz, vzero + g0 * kD, nvg * 256, bar);
   };
 
   float m_run[NT], l_run[NT], o[NT][8][2];
@@ -531,39 +574,44 @@ decode_attn_kernel(const DevArgs a) {
     for (int mt = 0; mt < 8; ++mt) o[nt][mt][0] = o[nt][mt][1] = 0.f;
   }
 
+  if (threadIdx.x == 0) {
 #pragma unroll 1
-  for (int s = 0; s < kStages; ++s) issue(s);
+    for (int s = 0; s < kStages; ++s) issue(s);
+  }
   bool failed = false;
   int i_done = 0;
 
   // ---------------------------------------------------------------- tiles
 #pragma unroll 1
-  for (int i = 0; i < n_my; ++i) {
+  for (int i = 0; i < n_st; ++i) {
     const int slot = i % kStages;
-    if (!mbar_wait_bounded(&sm.bars[warp][slot], (uint32_t)((i / kStages) & 1), kWaitLimit)) {
+    if (!mbar_wait_bounded(&sm.bars[slot], (uint32_t)((i / kStages) & 1), kWaitLimit)) {
       failed = true;
       break;
     }
     i_done = i + 1;
-    const int tile = tile_beg + warp + kWarps * i;
+    const int tile = tile_beg + kWarps * i + warp;
     const int t0 = a.t_first + tile * kTile;
-    const bool fast = is_fast(tile);
-    const uint8_t* st = ring + slot * SB;
+    const bool fast = stage_fast(i);
+    const uint8_t* sg = ring + slot * SBC;
+    if (tile < tile_end) {
     float x[NT][4];
 
     // ----------------------------------------------------------- QK^T
     if (fast) {
       KRow<BK> rw[4];
       float sc[4][NG], zc[4][NG];
-      load_krows<BK>(rw, st, lane);
-      load_kscales<DT, NG>(sc, reinterpret_cast<const uint16_t*>(st + o_ks) + gid * 4 * NG);
-      if (kasym) load_kscales<DT, NG>(zc, reinterpret_cast<const uint16_t*>(st + o_kz) + gid * 4 * NG);
+      load_krows<BK>(rw, sg + warp * TBK, lane);
+      load_kscales<DT, NG>(sc, reinterpret_cast<const uint16_t*>(sg + o_ks + warp * 64 * NG) + gid * 4 * NG);
+      if (kasym)
+        load_kscales<DT, NG>(zc, reinterpret_cast<const uint16_t*>(sg + o_kz + warp * 64 * NG) + gid * 4 * NG);
       float lp[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int j = 0; j < 4; ++j) lp[nt][j] = 0.f;
-      k_packed_logits<BK, NT, NG>(rw, sc, zc, sm.bk_s, ctot, qsf, kasym, lane, lp);
+      if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.bk_s, ctot, qsf, lane, lp);
+      else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.bk_s, ctot, qsf, lane, lp);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const bool head_ok = nt * 4 + tq < R;
@@ -606,7 +654,8 @@ decode_attn_kernel(const DevArgs a) {
             }
           }
         }
-        k_packed_logits<BK, NT, NG>(rw, sc, zc, sm.bk_s, ctot, qsf, kasym, lane, lp);
+        if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.bk_s, ctot, qsf, lane, lp);
+      else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.bk_s, ctot, qsf, lane, lp);
       }
       if (kd_any) {
         const uint16_t* rp[4];
@@ -654,10 +703,10 @@ decode_attn_kernel(const DevArgs a) {
       float pt[4] = {0.f, 0.f, 0.f, 0.f};
       float alpha = 1.f, wt = 0.f;
       if (mx != -INFINITY) {
-        alpha = exp2f(m_run[nt] - m_new);
-        wt = exp2f(mx - m_new);
+        alpha = ex2(m_run[nt] - m_new);
+        wt = ex2(mx - m_new);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) pt[j] = exp2f(x[nt][j] - mx);
+        for (int j = 0; j < 4; ++j) pt[j] = ex2(x[nt][j] - mx);
       }
       m_run[nt] = m_new;
       l_run[nt] = l_run[nt] * alpha + wt * ((pt[0] + pt[1]) + (pt[2] + pt[3]));
@@ -700,9 +749,10 @@ decode_attn_kernel(const DevArgs a) {
       VChunk<BV> vc;
       float sv[16], zv[16];
       if (fast) {
-        load_vchunk<BV>(vc, st + o_vc, lane);
-        load16<DT>(sv, reinterpret_cast<const uint16_t*>(st + o_vs) + gid * 16);
-        if (vasym) load16<DT>(zv, reinterpret_cast<const uint16_t*>(st + o_vz) + gid * 16);
+        const int gofs = ((t0 - vs) / a.v.group - (a.t_first + (tile - warp) * kTile - vs) / a.v.group) * 256;
+        load_vchunk<BV>(vc, sg + o_vc + warp * TBV, lane);
+        load16<DT>(sv, reinterpret_cast<const uint16_t*>(sg + o_vs + gofs) + gid * 16);
+        if (vasym) load16<DT>(zv, reinterpret_cast<const uint16_t*>(sg + o_vz + gofs) + gid * 16);
       } else {
         const int pv = t0 - vs;
         load_vchunk<BV>(vc, vcodes + (int64_t)(pv >> 5) * tile_bytes(BV), lane);
@@ -710,7 +760,8 @@ decode_attn_kernel(const DevArgs a) {
         load16<DT>(sv, vscale + gg * kD + gid * 16);
         if (vasym) load16<DT>(zv, vzero + gg * kD + gid * 16);
       }
-      v_packed_accumulate<BV, NT, DT>(vc, sv, zv, pb, offp, fv, zf, vasym, o);
+      if (vasym) v_packed_accumulate<BV, NT, true>(vc, sv, zv, pb, offp, fv, zf, o);
+      else v_packed_accumulate<BV, NT, false>(vc, sv, zv, pb, offp, fv, zf, o);
     } else {
       // dense V tile (sink / recent / masked rows), probabilities as dtype hi/lo
       uint32_t pb[NT][2][2];
@@ -768,16 +819,23 @@ decode_attn_kernel(const DevArgs a) {
         }
       }
     }
+    }  // tile < tile_end
     __syncwarp();
-    issue(i + kStages);
+    if (lane == 0) {
+      // the last warp to finish with this slot refills it
+      if (atomicAdd(&sm.cnt[slot], 1) == kWarps - 1) {
+        sm.cnt[slot] = 0;
+        issue(i + kStages);
+      }
+    }
   }
 
   if (failed) {
     // a staged tile never arrived: wait (bounded) for this warp's copies still
     // in flight, then publish NaN so the caller sees the failure
 #pragma unroll 1
-    for (int i = i_done; i < min(n_my, i_done + kStages); ++i)
-      mbar_wait_bounded(&sm.bars[warp][i % kStages], (uint32_t)((i / kStages) & 1), kWaitLimit);
+    for (int i = i_done; i < min(n_st, i_done + kStages); ++i)
+      mbar_wait_bounded(&sm.bars[i % kStages], (uint32_t)((i / kStages) & 1), kWaitLimit / 16);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) { m_run[nt] = NAN; l_run[nt] = NAN; }
   }

@@ -10,7 +10,7 @@ namespace {
 template <int BV, int RP, int NG>
 cudaError_t go(const DevArgs& a, dim3 grid, cudaStream_t s) {
   auto kern = decode_attn_kernel<2, BV, RP, F16, NG>;
-  const int smem = attn_dyn_smem(2, BV, NG, a.k.asym, a.v.asym);
+  const int smem = attn_dyn_smem(2, BV, NG, a.k.asym, a.v.asym, RP);
   int dev = 0;
   cudaGetDevice(&dev);
   static int set_bytes[64] = {0};
