@@ -240,8 +240,9 @@ def run_ours(a):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-    assert a.hkv % world == 0, "KV heads must divide across GPUs"
-    hkv, hq = a.hkv // world, a.hq // world
+    from innerq_b200.sharding import gather_heads, head_shard
+    h_lo, h_hi = head_shard(a.hkv, world, rank)
+    hkv, hq = h_hi - h_lo, (h_hi - h_lo) * (a.hq // a.hkv)
     B, L = a.batch, a.layers
     kw = cache_kw(a)
     conf = types.SimpleNamespace(_attn_implementation="innerq", **kw)
@@ -267,7 +268,6 @@ def run_ours(a):
     ks = torch.randn((NPOOL, L, B, hkv, 1, D), device=dev, generator=g).half()
     vs = torch.randn((NPOOL, L, B, hkv, 1, D), device=dev, generator=g).half()
     out = torch.empty((L, B, hq, D), device=dev, dtype=torch.float16)
-    gathered = torch.empty((world, L, B, hq, D), device=dev, dtype=torch.float16) if world > 1 else None
 
     def step(i, q=None, k=None, v=None):
         q = qs[i % NPOOL] if q is None else q
@@ -277,7 +277,7 @@ def run_ours(a):
             layer.update(k[li], v[li])
             layer.attend(q[li], out=out[li])
         if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+            gather_heads(out)  # [L, B, Hq, D] across the KV-head shards
 
     def bytes_now():
         return sum(layer_bytes(l, B, hkv, hq) for l in layers)

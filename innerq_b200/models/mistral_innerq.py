@@ -1,0 +1,20 @@
+"""InnerqMistralForCausalLM: ``src/innerq/models/mistral_innerq.py:6-18``.
+
+Installs the InnerQ ``DynamicCache`` for ``generate`` exactly as the reference
+does, and additionally routes attention through the ``"innerq"`` function so
+decode steps read the packed cache directly.
+"""
+from transformers.models.mistral.modeling_mistral import MistralForCausalLM
+
+from ..cache import DynamicCache
+from .attention_hook import use_innerq_attention
+
+
+class InnerqMistralForCausalLM(MistralForCausalLM):
+    def __init__(self, config):
+        super().__init__(config)
+        use_innerq_attention(self)
+
+    def _prepare_cache_for_generation(self, generation_config, model_kwargs, generation_mode,
+                                      batch_size, max_cache_length):
+        model_kwargs["past_key_values"] = DynamicCache(config=self.config.get_text_config(decoder=True))
