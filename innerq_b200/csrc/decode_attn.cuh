@@ -511,7 +511,9 @@ decode_attn_kernel(const DevArgs a) {
   const uint16_t* kscale = a.k.scale ? a.k.scale + kbh * a.k.cap_tiles * 32 * NG : nullptr;
   const uint16_t* kzero = a.k.zero ? a.k.zero + kbh * a.k.cap_tiles * 32 * NG : nullptr;
   const uint8_t* vcodes = a.v.codes ? a.v.codes + kbh * a.v.cap_tiles * tile_bytes(BV) : nullptr;
-  const int64_t vgroups_cap = a.v.codes ? a.v.cap_tiles * 32 / a.v.group : 0;
+  // V token-group size is 32, 64 or 128: divide by shifting
+  const int vgs = a.v.group == 32 ? 5 : (a.v.group == 64 ? 6 : 7);
+  const int64_t vgroups_cap = a.v.codes ? (a.v.cap_tiles * 32) >> vgs : 0;
   const uint16_t* vscale = a.v.scale ? a.v.scale + kbh * vgroups_cap * kD : nullptr;
   const uint16_t* vzero = a.v.zero ? a.v.zero + kbh * vgroups_cap * kD : nullptr;
 
@@ -551,7 +553,7 @@ decode_attn_kernel(const DevArgs a) {
     const int ta = tile_beg + kWarps * i, n_in = min(kWarps, tile_end - ta);
     const int t0 = a.t_first + ta * kTile;
     const int64_t tk = (t0 - ks) >> 5, tv = (t0 - vs) >> 5;
-    const int64_t g0 = (t0 - vs) / a.v.group, g1 = (t0 + n_in * kTile - 1 - vs) / a.v.group;
+    const int64_t g0 = (t0 - vs) >> vgs, g1 = (t0 + n_in * kTile - 1 - vs) >> vgs;
     const uint32_t nvg = (uint32_t)(g1 - g0 + 1);
     uint8_t* st = ring + slot * SBC;
     const uint32_t kb = n_in * (TBK + 64 * NG * (1 + kasym)), vb = n_in * TBV + nvg * 256 * (1 + vasym);
@@ -703,7 +705,7 @@ decode_attn_kernel(const DevArgs a) {
       float pt[4] = {0.f, 0.f, 0.f, 0.f};
       float alpha = 1.f, wt = 0.f;
       if (mx != -INFINITY) {
-        alpha = ex2(m_run[nt] - m_new);
+        alpha = m_new == m_run[nt] ? 1.f : ex2(m_run[nt] - m_new);
         wt = ex2(mx - m_new);
 #pragma unroll
         for (int j = 0; j < 4; ++j) pt[j] = ex2(x[nt][j] - mx);
@@ -719,7 +721,9 @@ decode_attn_kernel(const DevArgs a) {
         int ps = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int v = __float2int_rn(pt[j] * 65535.f);
+          // round to nearest on the FMA pipe: adding 1.5*2^23 leaves the integer
+          // in the low mantissa bits (pt*65535 < 2^22)
+          const int v = __float_as_int(fmaf(pt[j], 65535.f, 12582912.f)) - 0x4B400000;
           ps += v;
           sm.pd_s[warp][head][0][gid + 8 * j] = (uint8_t)(v >> 8);
           sm.pd_s[warp][head][1][gid + 8 * j] = (uint8_t)(v & 255);
@@ -749,14 +753,14 @@ decode_attn_kernel(const DevArgs a) {
       VChunk<BV> vc;
       float sv[16], zv[16];
       if (fast) {
-        const int gofs = ((t0 - vs) / a.v.group - (a.t_first + (tile - warp) * kTile - vs) / a.v.group) * 256;
+        const int gofs = (((t0 - vs) >> vgs) - ((a.t_first + (tile - warp) * kTile - vs) >> vgs)) * 256;
         load_vchunk<BV>(vc, sg + o_vc + warp * TBV, lane);
         load16<DT>(sv, reinterpret_cast<const uint16_t*>(sg + o_vs + gofs) + gid * 16);
         if (vasym) load16<DT>(zv, reinterpret_cast<const uint16_t*>(sg + o_vz + gofs) + gid * 16);
       } else {
         const int pv = t0 - vs;
         load_vchunk<BV>(vc, vcodes + (int64_t)(pv >> 5) * tile_bytes(BV), lane);
-        const int64_t gg = pv / a.v.group;
+        const int64_t gg = pv >> vgs;
         load16<DT>(sv, vscale + gg * kD + gid * 16);
         if (vasym) load16<DT>(zv, vzero + gg * kD + gid * 16);
       }
