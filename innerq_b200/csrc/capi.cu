@@ -110,7 +110,7 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
     // worth ~12 tiles); the best split count balances wave quantisation
     // against the fixed prologue/epilogue of each CTA
     const int64_t bh = (int64_t)a->B * a->Hkv;
-    const int64_t slots = (int64_t)sm_count() * (p.R <= 4 ? 4 : 2);
+    const int64_t slots = (int64_t)sm_count() * (p.R <= 4 ? 4 : 3);
     int64_t best = -1;
     splits = 1;
     for (int s = 1; s <= 256 && s <= (ntr > 0 ? ntr : 1); ++s) {

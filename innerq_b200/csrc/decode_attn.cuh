@@ -71,7 +71,7 @@ struct DevArgs {
 constexpr int kWarps = 4;
 // staging slots per warp: 2 where 4 CTAs share an SM (<= 4 query heads per
 // KV head), 3 where 2 CTAs do
-__host__ __device__ constexpr int stages_for(int rp) { return rp <= 4 ? 2 : 3; }
+__host__ __device__ constexpr int stages_for(int rp) { return 2; }
 // bounded mbarrier wait: each try suspends the warp for up to ~100 us (hint,
 // in ns) instead of spinning; 1 << 16 tries bound the wait to seconds
 constexpr uint32_t kWaitLimit = 1u << 16;
@@ -226,6 +226,15 @@ __device__ __forceinline__ void load_vchunk(VChunk<BITS>& c, const uint8_t* tb, 
   }
 }
 
+// a pair of 16-bit dtype values packed in a word -> two floats
+template <int DT> __device__ __forceinline__ float2 pair_to_f2(uint32_t w);
+template <> __device__ __forceinline__ float2 pair_to_f2<F16>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <> __device__ __forceinline__ float2 pair_to_f2<BF16>(uint32_t w) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+
 // 16 16-bit values (32 B) as floats
 template <int DT>
 __device__ __forceinline__ void load16(float out[16], const uint16_t* p) {
@@ -233,8 +242,9 @@ __device__ __forceinline__ void load16(float out[16], const uint16_t* p) {
   const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
-    out[2 * u] = to_f<DT>((uint16_t)(w[u] & 0xffffu));
-    out[2 * u + 1] = to_f<DT>((uint16_t)(w[u] >> 16));
+    const float2 f = pair_to_f2<DT>(w[u]);
+    out[2 * u] = f.x;
+    out[2 * u + 1] = f.y;
   }
 }
 
@@ -374,16 +384,17 @@ __device__ __forceinline__ void load_kscales(float out[4][NG], const uint16_t* p
     w[0] = a.x; w[1] = a.y;
   }
 #pragma unroll
-  for (int i = 0; i < 4 * NG; ++i) {
-    const uint16_t h = (uint16_t)((w[i >> 1] >> (16 * (i & 1))) & 0xffffu);
-    out[i / NG][i % NG] = to_f<DT>(h);
+  for (int u = 0; u < 2 * NG; ++u) {
+    const float2 f = pair_to_f2<DT>(w[u]);
+    out[(2 * u) / NG][(2 * u) % NG] = f.x;
+    out[(2 * u + 1) / NG][(2 * u + 1) % NG] = f.y;
   }
 }
 
 // BK/BV: code bits; RP: query heads per KV head padded to 4 or 8; DT: dtype;
 // NG: K channel groups per token (4, 2, 1 for groups of 32, 64, 128)
 template <int BK, int BV, int RP, int DT, int NG>
-__global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 2)
+__global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 3)
 decode_attn_kernel(const DevArgs a) {
   constexpr int NT = RP / 4;
   constexpr int kStages = stages_for(RP);
