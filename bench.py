@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--group", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", default="c1", choices=["c1", "c3"],
+                    help="c1: decode attention over a 32-layer cache (default); "
+                         "c3: full decode step of a random-init Llama-3-8B-shaped model")
     return ap.parse_args()
 
 
@@ -404,8 +407,84 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+def run_c3(a):
+    """full decode step of a random-init Llama-3-8B-shaped
+    model (32 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, vocab
+    128256, bf16 weights N(0, 0.02)) with a 4-bit InnerQ cache, batch 16,
+    context 8192, token ids uniform over the vocabulary; reports tokens/s.
+    The cache is pre-filled synthetically (per-layer random K/V through the
+    cache's own prefill path) instead of running a prompt through the model."""
+    import torch
+    from transformers import LlamaConfig
+
+    from innerq_b200 import _lib
+    from innerq_b200.cache import DynamicCache
+    from innerq_b200.models import InnerqLlamaForCausalLM
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, S = a.batch if a.batch != 32 else 16, a.ctx if a.ctx != 32768 else 8192
+    qcfg = cache_kw(a)
+    cfg = LlamaConfig(num_hidden_layers=32, hidden_size=4096, intermediate_size=14336,
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                      vocab_size=128256, max_position_embeddings=S + 1024, rope_theta=500000.0,
+                      torch_dtype=torch.bfloat16, **qcfg)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = InnerqLlamaForCausalLM(cfg).to(torch.bfloat16)
+    with torch.no_grad():
+        for p in model.parameters():
+            p.normal_(0.0, 0.02)
+    model.eval()
+    cache = DynamicCache(config=model.config.get_text_config(decoder=True))
+    g = torch.Generator(device=dev).manual_seed(1)
+    for layer in cache.layers:
+        k = (torch.randn((B, 8, S - 1, 128), device=dev, generator=g)
+             * torch.exp(torch.randn(128, device=dev, generator=g))).bfloat16()
+        v = torch.randn((B, 8, S - 1, 128), device=dev, generator=g).bfloat16()
+        layer.update(k, v)
+        del k, v
+    ids = torch.randint(0, cfg.vocab_size, (a.steps + a.warmup + 8, B, 1), device=dev, generator=g)
+    pos0 = S - 1
+
+    def step(i):
+        pos = torch.full((B, 1), pos0 + i, device=dev, dtype=torch.long)
+        out = model(input_ids=ids[i], past_key_values=cache, position_ids=pos, use_cache=True)
+        return out.logits
+
+    with torch.no_grad():
+        for i in range(max(3, a.warmup)):
+            step(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sampler = ClockSampler(0)
+        sampler.start()
+        n0 = _lib.launch_count[0]
+        e0.record()
+        for i in range(a.steps):
+            step(max(3, a.warmup) + i)
+        e1.record()
+        torch.cuda.synchronize()
+        clocks = sampler.stop()
+        ours = _lib.launch_count[0] - n0
+    ms = e0.elapsed_time(e1) / a.steps
+    line = {
+        "metric": "decode tokens/s (Llama-3-8B-shaped, 4-bit InnerQ cache)", "value": round(B / (ms * 1e-3), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": a.steps, "warmup": max(3, a.warmup),
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02), uniform token ids, synthetic cache)",
+        "config": {"workload": "C3: full decode step, random-init Llama-3-8B shape", "batch": B,
+                   "context": S, "layers": 32, "k_bits": a.kbits, "v_bits": a.vbits},
+        "gpu_launches": ours, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
+    if a.workload == "c3" and a.impl != "reference":
+        run_c3(a)
+        return
     if a.impl == "reference":
         run_reference(a)
     else:
