@@ -22,10 +22,14 @@
  * V the col layout (dims are rows of the PV A operand); see
  * innerq_b200/csrc/common.cuh for the bit-level layout.
  *
- * Supported combinations: role K with channel groups (group 32/64/128),
- * role V with token groups (group 32/64/128); bits 2, 3, 4; symmetric or
- * asymmetric.  These are the InnerQ layouts (key_quantize_over_token=False,
- * value_quantize_over_token=True, the reference defaults, cache.py:87-88).
+ * Built: bits 2, 3, 4; group 32/64/128; symmetric or asymmetric; either
+ * group axis for either role (the store, pack, unpack and dequant entry
+ * points).  The fused decode attention reads the InnerQ layouts only: K with
+ * channel groups and V with token groups (key_quantize_over_token=False,
+ * value_quantize_over_token=True, the reference defaults, cache.py:87-88);
+ * other layouts (KIVI) are materialised with innerq_dequant.
+ * Values grouped over channels must be appended into a zero-filled store
+ * (their codes share words across tokens).
  */
 #ifndef INNERQ_B200_H
 #define INNERQ_B200_H

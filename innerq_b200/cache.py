@@ -169,7 +169,7 @@ class InnerqDynamicLayer(CacheLayerMixin):
             self.lazy_initialization(key_states, value_states)
             return key_states, value_states
         self.add_to_cache(key_states, value_states)
-        if self.fused and key_states.shape[-2] == 1:
+        if self.fused and key_states.shape[-2] == 1 and self._k.fusable and self._v.fusable:
             # the "innerq" attention function reads the packed store
             key_states._innerq_layer = self
             return key_states, value_states

@@ -39,10 +39,6 @@ int check_common(int dtype, int D, int bits, int group, int mode, int role, int 
   if (mode != INNERQ_SYM && mode != INNERQ_ASYM) return fail(INNERQ_ERR_ARG, "mode %d", mode);
   if (group != 32 && group != 64 && group != 128)
     return fail(INNERQ_ERR_UNSUPPORTED, "group size %d (32, 64, 128 are built)", group);
-  if (role == INNERQ_ROLE_K && over_token)
-    return fail(INNERQ_ERR_UNSUPPORTED, "keys grouped over tokens are not built");
-  if (role == INNERQ_ROLE_V && !over_token)
-    return fail(INNERQ_ERR_UNSUPPORTED, "values grouped over channels are not built");
   if (role != INNERQ_ROLE_K && role != INNERQ_ROLE_V) return fail(INNERQ_ERR_ARG, "role %d", role);
   return INNERQ_OK;
 }
@@ -62,6 +58,11 @@ int check_side(const innerq_side& s, int dtype, int role, const char* name) {
   if (s.n_q > 0) {
     int rc = check_common(dtype, kD, s.bits, s.group, s.mode, role, s.over_token);
     if (rc) return rc;
+    // the fused kernel reads the InnerQ layouts (cache.py:87-88 defaults)
+    if (role == INNERQ_ROLE_K && s.over_token)
+      return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens (use innerq_dequant)");
+    if (role == INNERQ_ROLE_V && !s.over_token)
+      return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: values grouped over channels (use innerq_dequant)");
     if (!s.codes || !s.scale || (s.mode == INNERQ_ASYM && !s.zero))
       return fail(INNERQ_ERR_ARG, "%s: missing store pointer", name);
     if (!aligned(s.codes, 16) || !aligned(s.scale, 16) || (s.zero && !aligned(s.zero, 16)))

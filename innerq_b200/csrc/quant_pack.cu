@@ -44,7 +44,7 @@ __global__ void norm_factor_kernel(const uint16_t* __restrict__ x, int64_t sb, i
 // --------------------------------------------------------------------------
 // Row layout, channel groups (K): one warp per token row.
 // --------------------------------------------------------------------------
-template <int DT, int BITS>
+template <int DT, int BITS, int ROLEV>
 __global__ void __launch_bounds__(128)
 pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st,
                         int H, int T, const uint16_t* __restrict__ nf, int group, int asym,
@@ -102,6 +102,24 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
     scale[si] = from_f<DT>(s);
     if (asym) zero[si] = from_f<DT>(z);
   }
+  if (ROLEV) {
+    // col layout (values grouped over channels): a token's codes are spread
+    // over every lane chunk of its tile, sharing words with other tokens, so
+    // OR them into the (zero-initialised) store word by word
+    uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const BitPos bp = col_pos(BITS, r, 4 * lane + i);
+      const uint32_t uc = (uint32_t)u[i];
+      if (BITS == 4) {
+        atomicOr(reinterpret_cast<uint32_t*>(tb + bp.off), uc << bp.shift);
+      } else {
+        atomicOr(reinterpret_cast<uint32_t*>(tb + bp.off), (uc & 3u) << bp.shift);
+        if (BITS == 3) atomicOr(reinterpret_cast<uint32_t*>(tb + bp.hoff), (uc >> 2) << bp.hshift);
+      }
+    }
+    return;
+  }
   // assemble the row's four lane segments (one per tq) with the layout map
   uint32_t* seg = wbuf[warp];
   constexpr int kWordsPerSeg = BITS == 4 ? 4 : (BITS == 2 ? 2 : 3);  // b=3: L0, L1, H
@@ -140,7 +158,7 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
 // Col layout, token groups (V): one CTA of 128 threads (one per dim) per
 // group of `group` tokens.
 // --------------------------------------------------------------------------
-template <int DT, int BITS>
+template <int DT, int BITS, int ROLEV>
 __global__ void __launch_bounds__(128)
 pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st,
                       int group, int asym, uint8_t* __restrict__ codes,
@@ -191,7 +209,7 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
   __syncthreads();
   for (int t = 0; t < group; ++t) {
     const uint32_t uc = cb[t][d];
-    const BitPos bp = col_pos(BITS, t & 31, d);
+    const BitPos bp = ROLEV ? col_pos(BITS, t & 31, d) : row_pos(BITS, t & 31, d);
     uint32_t* w = tw + (t >> 5) * TW;
     if (BITS == 4) {
       atomicOr(&w[bp.off >> 2], uc << bp.shift);
@@ -382,21 +400,33 @@ cudaError_t launch_pack(const void* x, int dt, int B, int H, int T, int64_t sb, 
                         int64_t st, int bits, int group, int asym, int role_v, int over_token,
                         const void* nf, void* codes, void* scale, void* zero, int64_t cap_tiles,
                         int64_t t_off, cudaStream_t s) {
-  if (!role_v && !over_token) {
+  if (!over_token) {
     const int64_t rows = (int64_t)B * H * T;
     const unsigned grid = (unsigned)((rows + 3) / 4);
-    DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC><<<grid, 128, 0, s>>>(
-                                            (const uint16_t*)x, sb, sh, st, H, T,
-                                            (const uint16_t*)nf, group, asym, (uint8_t*)codes,
-                                            (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off, rows)));
-  } else if (role_v && over_token) {
-    dim3 grid(T / group, H, B);
-    DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_col_token_kernel<DTC, BC><<<grid, 128, 0, s>>>(
-                                            (const uint16_t*)x, sb, sh, st, group, asym,
-                                            (uint8_t*)codes, (uint16_t*)scale, (uint16_t*)zero,
-                                            cap_tiles, t_off)));
+    if (role_v) {
+      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC, 1><<<grid, 128, 0, s>>>(
+                                              (const uint16_t*)x, sb, sh, st, H, T,
+                                              (const uint16_t*)nf, group, asym, (uint8_t*)codes,
+                                              (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off, rows)));
+    } else {
+      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC, 0><<<grid, 128, 0, s>>>(
+                                              (const uint16_t*)x, sb, sh, st, H, T,
+                                              (const uint16_t*)nf, group, asym, (uint8_t*)codes,
+                                              (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off, rows)));
+    }
   } else {
-    return cudaErrorNotSupported;
+    dim3 grid(T / group, H, B);
+    if (role_v) {
+      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_col_token_kernel<DTC, BC, 1><<<grid, 128, 0, s>>>(
+                                              (const uint16_t*)x, sb, sh, st, group, asym,
+                                              (uint8_t*)codes, (uint16_t*)scale, (uint16_t*)zero,
+                                              cap_tiles, t_off)));
+    } else {
+      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_col_token_kernel<DTC, BC, 0><<<grid, 128, 0, s>>>(
+                                              (const uint16_t*)x, sb, sh, st, group, asym,
+                                              (uint8_t*)codes, (uint16_t*)scale, (uint16_t*)zero,
+                                              cap_tiles, t_off)));
+    }
   }
   return cudaGetLastError();
 }

@@ -77,12 +77,16 @@ class PackedSide:
             raise NotImplementedError(f"{self.bits}-bit codes are not built (2, 3, 4 are)")
         if self.group not in (32, 64, 128):
             raise NotImplementedError(f"group size {self.group} is not built (32, 64, 128 are)")
-        if self.role == _lib.ROLE_K and self.over_token:
-            raise NotImplementedError("keys grouped over tokens (KIVI layout) are not built")
-        if self.role == _lib.ROLE_V and not self.over_token:
-            raise NotImplementedError("values grouped over channels are not built")
         if self.D != D_SUPPORTED:
             raise NotImplementedError(f"head_dim {self.D} is not built (128 is)")
+
+    @property
+    def fusable(self) -> bool:
+        """The fused decode attention reads this side's layout: keys grouped
+        over channels, values over tokens (the InnerQ defaults)."""
+        if not self.quantize:
+            return True
+        return self.over_token == (self.role == _lib.ROLE_V)
 
     @property
     def n_sink(self) -> int:
@@ -107,7 +111,9 @@ class PackedSide:
         if self.over_token:
             cap_tiles = (cap_tiles * 32 + self.group - 1) // self.group * self.group // 32
         B, H, D = self.B, self.H, self.D
-        codes = torch.empty((B, H, cap_tiles, tb), dtype=torch.uint8, device=self.device)
+        # values grouped over channels OR their codes into shared words: zero-fill
+        alloc = torch.zeros if (self.role == _lib.ROLE_V and not self.over_token) else torch.empty
+        codes = alloc((B, H, cap_tiles, tb), dtype=torch.uint8, device=self.device)
         if self.over_token:
             sshape = (B, H, cap_tiles * 32 // self.group, D)
         else:

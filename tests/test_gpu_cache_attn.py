@@ -14,6 +14,7 @@ pytestmark = pytest.mark.gpu
 
 PRESET_KW = {
     "innerq_base": C.PRESETS["innerq_base"],
+    "kivi": C.PRESETS["kivi"],
     "innerq_small": C.PRESETS["innerq_small"],
     "default4": dict(k_bits=4, v_bits=4),
     "asym4_norm": dict(k_bits=4, v_bits=4, key_quantize_mode="asymmetric",
@@ -58,19 +59,34 @@ def test_layer_matches_reference_fixture(cache_golden, name):
     # itself moves the output by up to a few 1e-3 at 3 bits (1e-2 in bf16); the
     # 1e-3 bar is checked against the fp32 dequantize-then-matmul in
     # test_decode_attention_vs_oracle.
-    q = _from_golden(g[p + "/q"], dtype)
-    out = layer.attend(q)
-    assert_close_rel(to_np32(out), g[p + "/o"][:, :, 0], 3e-2 if dtype == "bf16" else 1e-2, name)
+    if layer.key_side.fusable and layer.value_side.fusable:
+        q = _from_golden(g[p + "/q"], dtype)
+        out = layer.attend(q)
+        assert_close_rel(to_np32(out), g[p + "/o"][:, :, 0], 3e-2 if dtype == "bf16" else 1e-2, name)
     assert layer.get_seq_length() == kin.shape[2]
     assert layer.get_mask_sizes(1) == (kin.shape[2] + 1, 0)
 
 
-def test_kivi_layout_is_refused():
+def test_kivi_layout_materialised_and_not_fused():
+    """KIVI (keys grouped over tokens, values over channels, asymmetric) runs
+    through the packed store and the dequant kernel, bit-exact with the
+    reference; the fused kernel refuses that layout."""
+    from innerq_b200.attention import decode_attention
     from innerq_b200.cache import InnerqDynamicLayer
+    from innerq_b200._lib import InnerqError
     layer = InnerqDynamicLayer(cfg(**C.PRESETS["kivi"]), 0)
-    k, v = synth_kv(1, 2, 200, seed=3)
-    with pytest.raises(NotImplementedError):
-        layer.update(k, v)
+    k, v = synth_kv(1, 2, 240, seed=3)
+    ol = oracle_layer(C.PRESETS["kivi"], "fp16")
+    layer.update(k[:, :, :200], v[:, :, :200])
+    ol.update(to_np32(k[:, :, :200]), to_np32(v[:, :, :200]))
+    for t in range(200, 240):
+        K, V = layer.update(k[:, :, t:t + 1], v[:, :, t:t + 1])
+        Kr, Vr = ol.update(to_np32(k[:, :, t:t + 1]), to_np32(v[:, :, t:t + 1]))
+    np.testing.assert_array_equal(to_np32(K), Kr)
+    np.testing.assert_array_equal(to_np32(V), Vr)
+    assert not layer.key_side.fusable and not layer.value_side.fusable
+    with pytest.raises(InnerqError):
+        decode_attention(synth_q(1, 8), layer.key_side, layer.value_side)
 
 
 def _oracle_kv32(ol):
