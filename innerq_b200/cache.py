@@ -32,7 +32,7 @@ from transformers.cache_utils import Cache, CacheLayerMixin
 
 from . import _lib
 from .quant import QMode
-from .store import PackedSide
+from .store import HybridSide, PackedSide
 
 
 class InnerqDynamicLayer(CacheLayerMixin):
@@ -69,20 +69,18 @@ class InnerqDynamicLayer(CacheLayerMixin):
         self.key_quantize_mode = QMode.from_str(getattr(config, 'key_quantize_mode', 'symmetric'))
         self.value_quantize_mode = QMode.from_str(getattr(config, 'value_quantize_mode', 'symmetric'))
 
-        for name, m, on in (("key", self.key_quantize_mode, self.key_quantize),
-                            ("value", self.value_quantize_mode, self.value_quantize)):
-            if on and m == QMode.HYBRID:
-                raise NotImplementedError(f"{name}_quantize_mode='hybrid' is not built in the packed store")
+        def side(role, qmode, bits, group, over_token, w_sink, w_recent, flush, normalize=False):
+            if qmode == QMode.HYBRID:  # quant.py:133-176
+                return HybridSide(role, bits, group, over_token, w_sink, w_recent, flush, normalize)
+            mode = _lib.ASYM if qmode == QMode.ASYM else _lib.SYM
+            return PackedSide(role, bits, group, mode, over_token, w_sink, w_recent, flush, normalize)
 
-        def mode(m):
-            return _lib.ASYM if m == QMode.ASYM else _lib.SYM
-
-        self._k = PackedSide(_lib.ROLE_K, self.key_bits, self.key_group_size, mode(self.key_quantize_mode),
-                             self.key_quantize_over_token, self.key_w_sink, self.key_w_recent,
-                             self.key_flush_size, normalize=bool(self.key_normalize) and self.key_quantize)
-        self._v = PackedSide(_lib.ROLE_V, self.value_bits, self.value_group_size,
-                             mode(self.value_quantize_mode), self.value_quantize_over_token,
-                             self.value_w_sink, self.value_w_recent, self.value_flush_size)
+        self._k = side(_lib.ROLE_K, self.key_quantize_mode, self.key_bits, self.key_group_size,
+                       self.key_quantize_over_token, self.key_w_sink, self.key_w_recent,
+                       self.key_flush_size, normalize=bool(self.key_normalize) and self.key_quantize)
+        self._v = side(_lib.ROLE_V, self.value_quantize_mode, self.value_bits, self.value_group_size,
+                       self.value_quantize_over_token, self.value_w_sink, self.value_w_recent,
+                       self.value_flush_size)
 
     # ----------------------------------------------- reference-format views
     @property

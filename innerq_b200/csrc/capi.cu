@@ -35,7 +35,7 @@ bool aligned(const void* p, int n) { return ((uintptr_t)p % n) == 0; }
 int check_common(int dtype, int D, int bits, int group, int mode, int role, int over_token) {
   if (dtype != INNERQ_DT_F16 && dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype %d", dtype);
   if (D != kD) return fail(INNERQ_ERR_UNSUPPORTED, "head_dim %d (only 128 is built)", D);
-  if (bits < 2 || bits > 4) return fail(INNERQ_ERR_UNSUPPORTED, "bits %d (2, 3, 4 are built)", bits);
+  if (bits < 1 || bits > 4) return fail(INNERQ_ERR_UNSUPPORTED, "bits %d (1 to 4 are built)", bits);
   if (mode != INNERQ_SYM && mode != INNERQ_ASYM) return fail(INNERQ_ERR_ARG, "mode %d", mode);
   if (group != 32 && group != 64 && group != 128)
     return fail(INNERQ_ERR_UNSUPPORTED, "group size %d (32, 64, 128 are built)", group);
@@ -58,6 +58,7 @@ int check_side(const innerq_side& s, int dtype, int role, const char* name) {
   if (s.n_q > 0) {
     int rc = check_common(dtype, kD, s.bits, s.group, s.mode, role, s.over_token);
     if (rc) return rc;
+    if (s.bits < 2) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: %s bits %d (2, 3, 4)", name, s.bits);
     // the fused kernel reads the InnerQ layouts (cache.py:87-88 defaults)
     if (role == INNERQ_ROLE_K && s.over_token)
       return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens (use innerq_dequant)");
@@ -193,7 +194,7 @@ extern "C" {
 
 int innerq_abi_version(void) { return INNERQ_ABI_VERSION; }
 const char* innerq_last_error(void) { return g_err; }
-int64_t innerq_tile_bytes(int bits) { return (bits >= 2 && bits <= 4) ? tile_bytes(bits) : -1; }
+int64_t innerq_tile_bytes(int bits) { return (bits >= 1 && bits <= 4) ? tile_bytes(bits) : -1; }
 
 int innerq_norm_factor(const void* x, int dtype, int B, int H, int T, int D, int64_t sb, int64_t sh,
                        int64_t st, void* out_f, void* stream) {

@@ -25,6 +25,9 @@
 //     b=3: plane L as b=2; plane H 4 words: word mt>>1, bit 8i + (mt&1)*4 + h*2 + half
 //   Scales / zero points (one per (group, dim)): [gid 8][mt 8][h 2].
 //
+// b=1 (the asymmetric half of hybrid mode) is a single plane laid out like
+// plane H of b=3.
+//
 // Symmetric codes are stored offset-binary: u = sign*code + 2^(b-1) (1..2^b-1);
 // asymmetric codes are stored as is (0..2^b-1).
 #pragma once
@@ -160,7 +163,10 @@ __host__ __device__ inline BitPos row_pos(int bits, int r, int d) {
   const int kb = d >> 5, half = (d >> 4) & 1, tq = (d >> 2) & 3, i = d & 3;
   const int lane = gid * 4 + tq;
   BitPos p{0, 0, 0, 0};
-  if (bits == 4) {
+  if (bits == 1) {  // a single bit plane laid out like plane H of b=3
+    p.off = lane * 16 + j * 4;
+    p.shift = 8 * i + kb * 2 + half;
+  } else if (bits == 4) {
     p.off = lane * 64 + j * 16 + kb * 4;
     p.shift = 4 * (2 * i + half);
   } else {
@@ -179,7 +185,10 @@ __host__ __device__ inline BitPos col_pos(int bits, int r, int d) {
   const int half = r >> 4, tq = (r >> 2) & 3, i = r & 3;
   const int lane = gid * 4 + tq;
   BitPos p{0, 0, 0, 0};
-  if (bits == 4) {
+  if (bits == 1) {
+    p.off = lane * 16 + (mt >> 1) * 4;
+    p.shift = 8 * i + (mt & 1) * 4 + h * 2 + half;
+  } else if (bits == 4) {
     p.off = lane * 64 + (mt * 2 + h) * 4;
     p.shift = 4 * (2 * i + half);
   } else {

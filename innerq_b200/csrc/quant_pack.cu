@@ -111,7 +111,7 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
     for (int i = 0; i < 4; ++i) {
       const BitPos bp = col_pos(BITS, r, 4 * lane + i);
       const uint32_t uc = (uint32_t)u[i];
-      if (BITS == 4) {
+      if (BITS == 4 || BITS == 1) {
         atomicOr(reinterpret_cast<uint32_t*>(tb + bp.off), uc << bp.shift);
       } else {
         atomicOr(reinterpret_cast<uint32_t*>(tb + bp.off), (uc & 3u) << bp.shift);
@@ -122,7 +122,7 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
   }
   // assemble the row's four lane segments (one per tq) with the layout map
   uint32_t* seg = wbuf[warp];
-  constexpr int kWordsPerSeg = BITS == 4 ? 4 : (BITS == 2 ? 2 : 3);  // b=3: L0, L1, H
+  constexpr int kWordsPerSeg = BITS == 4 ? 4 : (BITS == 2 ? 2 : (BITS == 3 ? 3 : 1));  // b=3: L0, L1, H
   if (lane < 4 * kWordsPerSeg) seg[lane] = 0u;
   __syncwarp();
 #pragma unroll
@@ -131,7 +131,9 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
     const BitPos bp = row_pos(BITS, r, d);
     const int tq = (d >> 2) & 3;
     const uint32_t uc = (uint32_t)u[i];
-    if (BITS == 4) {
+    if (BITS == 1) {
+      atomicOr(&seg[tq], uc << bp.shift);
+    } else if (BITS == 4) {
       atomicOr(&seg[tq * 4 + ((bp.off & 15) >> 2)], uc << bp.shift);
     } else {
       atomicOr(&seg[tq * kWordsPerSeg + ((bp.off & 7) >> 2)], (uc & 3u) << bp.shift);
@@ -143,7 +145,9 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
     const int tq = lane;
     uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
     const int lane2 = (r & 7) * 4 + tq, j = r >> 3;
-    if (BITS == 4) {
+    if (BITS == 1) {
+      *reinterpret_cast<uint32_t*>(tb + lane2 * 16 + j * 4) = seg[tq];
+    } else if (BITS == 4) {
       *reinterpret_cast<uint4*>(tb + lane2 * 64 + j * 16) =
           make_uint4(seg[tq * 4], seg[tq * 4 + 1], seg[tq * 4 + 2], seg[tq * 4 + 3]);
     } else {
@@ -211,7 +215,7 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
     const uint32_t uc = cb[t][d];
     const BitPos bp = ROLEV ? col_pos(BITS, t & 31, d) : row_pos(BITS, t & 31, d);
     uint32_t* w = tw + (t >> 5) * TW;
-    if (BITS == 4) {
+    if (BITS == 4 || BITS == 1) {
       atomicOr(&w[bp.off >> 2], uc << bp.shift);
     } else {
       atomicOr(&w[bp.off >> 2], (uc & 3u) << bp.shift);
@@ -236,6 +240,7 @@ __device__ __forceinline__ int extract_code(const uint8_t* store_bh, int bits, i
   const BitPos bp = role_v ? col_pos(bits, r, d) : row_pos(bits, r, d);
   const uint32_t w = *reinterpret_cast<const uint32_t*>(tb + bp.off);
   if (bits == 4) return (w >> bp.shift) & 15u;
+  if (bits == 1) return (w >> bp.shift) & 1u;
   int u = (w >> bp.shift) & 3u;
   if (bits == 3) {
     const uint32_t wh = *reinterpret_cast<const uint32_t*>(tb + bp.hoff);
@@ -378,7 +383,10 @@ __global__ void dequant_ref_kernel(const int32_t* __restrict__ c, const uint16_t
     __VA_ARGS__;                        \
   }
 #define BITS_DISPATCH(bits, ...)        \
-  if ((bits) == 2) {                    \
+  if ((bits) == 1) {                    \
+    constexpr int BC = 1;               \
+    __VA_ARGS__;                        \
+  } else if ((bits) == 2) {             \
     constexpr int BC = 2;               \
     __VA_ARGS__;                        \
   } else if ((bits) == 3) {             \

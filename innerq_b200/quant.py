@@ -16,7 +16,8 @@ Same names, signatures, return values and errors as the reference:
   reference does.
 
 Tensors must be CUDA float16 / bfloat16 with a last dimension of 128 and
-2/3/4-bit codes, group sizes 32/64/128 (what the kernels are built for);
+2/3/4-bit codes (1-bit asymmetric, the low half of hybrid mode), group sizes
+32/64/128 (what the kernels are built for);
 anything else raises.  There is no CPU path.
 """
 from __future__ import annotations
@@ -65,8 +66,8 @@ def _quantize(tensor: torch.Tensor, group_size: int, bit: int, expanded_dim: int
     T, D = shape[-2], shape[-1]
     if D != 128:
         raise NotImplementedError(f"last dim {D}: the packed kernels are built for 128")
-    if bit not in (2, 3, 4):
-        raise NotImplementedError(f"{bit}-bit codes are not built (2, 3, 4 are)")
+    if bit not in (1, 2, 3, 4) or (bit == 1 and mode == _lib.SYM):
+        raise NotImplementedError(f"{bit}-bit codes are not built (2, 3, 4; 1 for asymmetric)")
     if group_size not in (32, 64, 128):
         raise NotImplementedError(f"group size {group_size} is not built (32, 64, 128 are)")
     dt = dtype_code(tensor.dtype)

@@ -73,8 +73,8 @@ class PackedSide:
     def _check_supported(self):
         if not self.quantize:
             return
-        if self.bits not in (2, 3, 4):
-            raise NotImplementedError(f"{self.bits}-bit codes are not built (2, 3, 4 are)")
+        if self.bits not in (1, 2, 3, 4) or (self.bits == 1 and self.mode == _lib.SYM):
+            raise NotImplementedError(f"{self.bits}-bit codes are not built (2, 3, 4; 1 asymmetric)")
         if self.group not in (32, 64, 128):
             raise NotImplementedError(f"group size {self.group} is not built (32, 64, 128 are)")
         if self.D != D_SUPPORTED:
@@ -272,3 +272,86 @@ class PackedSide:
         s.n_sink, s.n_q, s.n_recent = self.n_sink, self.n_q, self._rn
         s.bits, s.group, s.mode, s.over_token = self.bits, self.group, self.mode, int(self.over_token)
         return s
+
+
+class HybridSide(PackedSide):
+    """Hybrid mode (``quant.py:133-176``): every group is quantized twice —
+    symmetric at ``bits`` (kept in this store) and asymmetric at ``bits - 1``
+    (kept in ``self.zp``) — and a per-group mask chooses the symmetric one
+    where its fp32 L1 error is lower.  Materialised through the dequant
+    kernels; the fused attention kernel does not read hybrid stores.
+
+    The mask is computed from the GPU dequantization with torch sums, so on an
+    exact tie of the two fp32 error sums (summation order differs from the
+    reference's CPU sum) the choice can differ; both choices are valid
+    reconstructions of that group."""
+
+    def __init__(self, role, bits, group, over_token, w_sink, w_recent, flush, normalize=False):
+        super().__init__(role, bits, group, _lib.SYM, over_token, w_sink, w_recent, flush, normalize)
+        self.zp = PackedSide(role, bits - 1, group, _lib.ASYM, over_token, 0, 0, flush)
+        self.masks = []
+
+    @property
+    def fusable(self) -> bool:
+        return not self.quantize
+
+    def _check_supported(self):
+        super()._check_supported()
+        for k in ("dtype", "device", "B", "H", "D"):
+            setattr(self.zp, k, getattr(self, k))
+        self.zp._check_supported()
+
+    def _quantize(self, x: torch.Tensor):
+        if x.shape[2] == 0:
+            return
+        from . import quant as Q
+        xs = x
+        if self.normalize:
+            raise NotImplementedError("hybrid mode with key normalisation")
+        axis = 2 if self.over_token else 3
+        qa = Q.quantize_asym(xs, self.group, self.bits - 1, axis)
+        qs = Q.quantize_sym(xs, self.group, self.bits, axis)
+        if self.over_token:
+            da = Q.dequantize_tokendim_asym(*qa, self.group)
+            ds = Q.dequantize_tokendim_sym(*qs, self.group)
+            shp = (x.shape[0], x.shape[1], x.shape[2] // self.group, self.group, x.shape[3])
+            red = 3
+        else:
+            da = Q.dequantize_channeldim_asym(*qa, self.group)
+            ds = Q.dequantize_channeldim_sym(*qs, self.group)
+            shp = (x.shape[0], x.shape[1], x.shape[2], x.shape[3] // self.group, self.group)
+            red = 4
+        xf = x.float()
+        err_a = (da - xf).view(shp).abs().sum(red)
+        err_s = (ds - xf).view(shp).abs().sum(red)
+        self.masks.append(err_a > err_s)
+        self.zp._quantize(x)
+        PackedSide._quantize(self, x)
+
+    def mask(self):
+        return torch.cat(self.masks, dim=2) if self.masks else None
+
+    def materialize(self) -> torch.Tensor:
+        out = super().materialize()
+        if self.n_q == 0:
+            return out
+        ns, nq = self.n_sink, self.n_q
+        zp_mid = torch.empty((self.B, self.H, nq, self.D), dtype=self.dtype, device=self.device)
+        _lib.call("innerq_dequant", self.zp.codes.data_ptr(), self.zp.scale.data_ptr(),
+                  self.zp.zero.data_ptr(), dtype_code(self.dtype), self.B, self.H, 0, nq, self.D,
+                  self.zp.bits, self.group, _lib.ASYM, self.role, int(self.over_token),
+                  self.zp.cap_tiles, None, zp_mid.data_ptr(), zp_mid.stride(0), zp_mid.stride(1),
+                  zp_mid.stride(2), stream_ptr(self.device))
+        m = self.mask()
+        m = m.repeat_interleave(self.group, dim=2 if self.over_token else 3)
+        mid = out[:, :, ns:ns + nq]
+        mid.copy_(torch.where(m, mid, zp_mid))
+        return out
+
+    def ref_views(self):
+        if self.n_q == 0:
+            return None, None, None
+        cs, ss, sg = super().ref_views()
+        ca, sa, za = self.zp.ref_views()
+        return ({'zp': ca, 'nozp': cs}, {'zp': sa, 'nozp': ss, 'mask': self.mask()},
+                {'zp': za, 'nozp': sg})

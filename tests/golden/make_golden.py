@@ -141,6 +141,12 @@ PRESETS = {
                        value_quantize_mode="asymmetric", key_normalize=True,
                        key_w_sink=4, value_w_sink=4, value_group_size=64,
                        value_flush_size=64),
+    "innerq_hybrid": dict(k_bits=3, v_bits=2, key_flush_size=1, value_flush_size=32,
+                          key_group_size=32, value_group_size=32, key_w_recent=96,
+                          value_w_recent=96, key_w_sink=32, value_w_sink=32,
+                          key_normalize=True, key_quantize_over_token=False,
+                          value_quantize_over_token=True, key_quantize_mode="symmetric",
+                          value_quantize_mode="hybrid"),
 }
 
 
@@ -162,8 +168,11 @@ def cache_cases(innerq):
             ks.append(k1)
             vs.append(v1)
             K, V = layer.update(k1, v1)
-            nqk = 0 if layer.keys_q is None else layer.keys_q.shape[2]
-            nqv = 0 if layer.values_q is None else layer.values_q.shape[2]
+            def nq(c):
+                if c is None:
+                    return 0
+                return (c["nozp"] if isinstance(c, dict) else c).shape[2]
+            nqk, nqv = nq(layer.keys_q), nq(layer.values_q)
             trace.append([layer.keys_sink.shape[2], nqk, layer.keys_recent.shape[2],
                           layer.values_sink.shape[2], nqv, layer.values_recent.shape[2]])
         q = torch.randn((B, 4 * H, 1, D), generator=gen).to(TDT[dtype])

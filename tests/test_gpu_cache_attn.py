@@ -15,6 +15,8 @@ pytestmark = pytest.mark.gpu
 PRESET_KW = {
     "innerq_base": C.PRESETS["innerq_base"],
     "kivi": C.PRESETS["kivi"],
+    # scripts/run_lmeval.sh:134-153; V hybrid (quant.py:133-176), materialised
+    "innerq_hybrid": dict(C.PRESETS["innerq_small"], value_quantize_mode="hybrid"),
     "innerq_small": C.PRESETS["innerq_small"],
     "default4": dict(k_bits=4, v_bits=4),
     "asym4_norm": dict(k_bits=4, v_bits=4, key_quantize_mode="asymmetric",
