@@ -470,21 +470,30 @@ decode_attn_kernel(const DevArgs a) {
     }
   }
   // packed-K B fragments (m16n8k32): n-tile 2*quad holds digits (d2, d1) and
-  // 2*quad+1 holds (d0, 0) of each of the quad's 4 heads
+  // 2*quad+1 holds (d0, 0) of each of the quad's 4 heads.  First split every
+  // q into its three digit bytes (in place of q_s, dead by now), then each
+  // fragment word is one 32-bit read of 4 consecutive digit bytes.
+  int8_t* dg_s = reinterpret_cast<int8_t*>(q_s);  // [3][RP][128]
+  for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
+    int d0, d1, d2;
+    digits3(qi_s[i], d0, d1, d2);
+    dg_s[i] = (int8_t)d0;
+    dg_s[RP * kD + i] = (int8_t)d1;
+    dg_s[2 * RP * kD + i] = (int8_t)d2;
+  }
+  __syncthreads();
   for (int i = threadIdx.x; i < 2 * NT * 4 * 32; i += kWarps * 32) {
     const int ntk = i / 128, kb = (i / 32) % 4, ln = i % 32;
     const int g2 = ln >> 2, t2 = ln & 3;
     const int head = (ntk >> 1) * 4 + (g2 >> 1), which = g2 & 1;
+    // digit plane: n-tile 2q -> (d2, d1), n-tile 2q+1 -> (d0, none)
+    const int plane = (ntk & 1) ? (which ? -1 : 0) : (which ? 1 : 2);
     uint32_t wrd[2] = {0u, 0u};
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        int d0, d1, d2;
-        digits3(qi_s[head * kD + kb * 32 + hf * 16 + 4 * t2 + u], d0, d1, d2);
-        const int dg = (ntk & 1) ? (which ? 0 : d0) : (which ? d1 : d2);
-        wrd[hf] |= (uint32_t)(dg & 255) << (8 * u);
-      }
+    if (plane >= 0) {
+      const int8_t* src = dg_s + plane * RP * kD + head * kD + kb * 32 + 4 * t2;
+      wrd[0] = *reinterpret_cast<const uint32_t*>(src);
+      wrd[1] = *reinterpret_cast<const uint32_t*>(src + 16);
+    }
     sm.bk_s[ntk][kb][ln] = make_uint2(wrd[0], wrd[1]);
   }
   // dense-K B fragments (m16n8k16, dtype hi/lo of q * 2^e_d), only for CTAs
@@ -880,7 +889,7 @@ decode_attn_kernel(const DevArgs a) {
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
         const float mw = sm.cm_s[w][head];
-        const float wt = mw == -INFINITY ? 0.f : exp2f(mw - M);
+        const float wt = ex2(mw - M);  // 0 for an empty warp (mw = -inf)
         ov += wt * co_s[(w * RP + head) * kD + d];
         lv += wt * sm.cl_s[w][head];
       }
