@@ -217,6 +217,7 @@ int innerq_quant_pack(const void* x, int dtype, int B, int H, int T, int D, int6
   if (!aligned(codes, 16) || !aligned(scale, 2)) return fail(INNERQ_ERR_ARG, "store alignment");
   if (t_offset + T > cap_tiles * 32) return fail(INNERQ_ERR_ARG, "store capacity %lld tokens < %lld",
                                                 (long long)(cap_tiles * 32), (long long)(t_offset + T));
+  if (B > 65535 || H > 65535) return fail(INNERQ_ERR_ARG, "B and H must be <= 65535 (grid limits)");
   if (over_token) {
     if (T % group || t_offset % group)
       return fail(INNERQ_ERR_ARG, "token groups need T (%d) and t_offset (%lld) divisible by group %d", T,

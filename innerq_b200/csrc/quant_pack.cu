@@ -42,24 +42,14 @@ __global__ void norm_factor_kernel(const uint16_t* __restrict__ x, int64_t sb, i
 }
 
 // --------------------------------------------------------------------------
-// Row layout, channel groups (K): one warp per token row.
+// Channel groups (per-token groups along head_dim): one warp per token row.
 // --------------------------------------------------------------------------
 template <int DT, int BITS, int ROLEV>
-__global__ void __launch_bounds__(128)
-pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st,
-                        int H, int T, const uint16_t* __restrict__ nf, int group, int asym,
-                        uint8_t* __restrict__ codes, uint16_t* __restrict__ scale,
-                        uint16_t* __restrict__ zero, int64_t cap_tiles, int64_t t_off,
-                        int64_t n_rows) {
-  __shared__ uint32_t wbuf[4][16];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
-  if (row >= n_rows) return;
-  const int t = (int)(row % T);
-  const int64_t bh = row / T;
-  const int h = (int)(bh % H), b = (int)(bh / H);
-  const uint16_t* xr = x + b * sb + h * sh + (int64_t)t * st + 4 * lane;
-  const uint2 raw = *reinterpret_cast<const uint2*>(xr);
+__device__ __forceinline__ void pack_row_token(const uint2 raw, int t, int64_t bh, int lane,
+                                               uint32_t* seg, const uint16_t* __restrict__ nf,
+                                               int group, int asym, uint8_t* __restrict__ codes,
+                                               uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
+                                               int64_t cap_tiles, int64_t t_off) {
   float v[4] = {to_f<DT>(raw.x & 0xffff), to_f<DT>(raw.x >> 16), to_f<DT>(raw.y & 0xffff),
                 to_f<DT>(raw.y >> 16)};
   if (nf) {  // cache.py:125 key_states / factor, in the dtype
@@ -121,8 +111,8 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
     return;
   }
   // assemble the row's four lane segments (one per tq) with the layout map
-  uint32_t* seg = wbuf[warp];
   constexpr int kWordsPerSeg = BITS == 4 ? 4 : (BITS == 2 ? 2 : (BITS == 3 ? 3 : 1));  // b=3: L0, L1, H
+  __syncwarp();  // the previous token's segment reads are done
   if (lane < 4 * kWordsPerSeg) seg[lane] = 0u;
   __syncwarp();
 #pragma unroll
@@ -156,6 +146,32 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
       if (BITS == 3) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = seg[tq * 3 + 2];
     }
   }
+}
+
+
+template <int DT, int BITS, int ROLEV>
+__global__ void __launch_bounds__(256)
+pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st,
+                        int H, int T, const uint16_t* __restrict__ nf, int group, int asym,
+                        uint8_t* __restrict__ codes, uint16_t* __restrict__ scale,
+                        uint16_t* __restrict__ zero, int64_t cap_tiles, int64_t t_off) {
+  __shared__ uint32_t wbuf[8][16];
+  // grid (token blocks of 8 warps x 4 tokens, H, B); each warp loads its 4
+  // token rows before working on them, so the loads are in flight together
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = (blockIdx.x * 8 + warp) * 4;
+  if (t0 >= T) return;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int64_t bh = (int64_t)b * H + h;
+  uint2 raw[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (t0 + k < T)
+      raw[k] = *reinterpret_cast<const uint2*>(x + b * sb + h * sh + (int64_t)(t0 + k) * st + 4 * lane);
+#pragma unroll 1
+  for (int k = 0; k < 4 && t0 + k < T; ++k)
+    pack_row_token<DT, BITS, ROLEV>(raw[k], t0 + k, bh, lane, wbuf[warp], nf, group, asym, codes,
+                                    scale, zero, cap_tiles, t_off);
 }
 
 // --------------------------------------------------------------------------
@@ -409,18 +425,17 @@ cudaError_t launch_pack(const void* x, int dt, int B, int H, int T, int64_t sb, 
                         const void* nf, void* codes, void* scale, void* zero, int64_t cap_tiles,
                         int64_t t_off, cudaStream_t s) {
   if (!over_token) {
-    const int64_t rows = (int64_t)B * H * T;
-    const unsigned grid = (unsigned)((rows + 3) / 4);
+    const dim3 grid((unsigned)((T + 31) / 32), (unsigned)H, (unsigned)B);
     if (role_v) {
-      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC, 1><<<grid, 128, 0, s>>>(
+      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC, 1><<<grid, 256, 0, s>>>(
                                               (const uint16_t*)x, sb, sh, st, H, T,
                                               (const uint16_t*)nf, group, asym, (uint8_t*)codes,
-                                              (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off, rows)));
+                                              (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off)));
     } else {
-      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC, 0><<<grid, 128, 0, s>>>(
+      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC, 0><<<grid, 256, 0, s>>>(
                                               (const uint16_t*)x, sb, sh, st, H, T,
                                               (const uint16_t*)nf, group, asym, (uint8_t*)codes,
-                                              (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off, rows)));
+                                              (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off)));
     }
   } else {
     dim3 grid(T / group, H, B);
