@@ -64,6 +64,50 @@ def build_args(q: torch.Tensor, k: PackedSide, v: PackedSide, scale: float | Non
     return a
 
 
+class DecodeAttention:
+    """Per-layer launcher that keeps its C argument struct and output buffer
+    between decode steps and only refreshes what changes (query pointer,
+    token counts, recent-window pointer), to keep host time per layer low."""
+
+    def __init__(self):
+        self.args = _lib.AttnArgs()
+        self.args.struct_size = C.sizeof(_lib.AttnArgs)
+        self.out = None
+        self._lib = _lib.load()
+
+    def __call__(self, q: torch.Tensor, k: PackedSide, v: PackedSide, scale: float | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        if not q.is_cuda or q.dtype != k.dtype:
+            require_cuda(q, "query")
+            raise TypeError(f"query dtype {q.dtype} != cache dtype {k.dtype}")
+        if q.dim() == 4 and q.shape[2] != 1:
+            raise ValueError("decode attention takes one query token per sequence")
+        if q.stride(-1) != 1:
+            q = q.contiguous()
+        a = self.args
+        B, Hq, D = q.shape[0], q.shape[1], q.shape[-1]
+        a.dtype = dtype_code(q.dtype)
+        a.B, a.Hq, a.Hkv, a.D = B, Hq, k.H, D
+        a.q = q.data_ptr()
+        a.q_sb, a.q_sh = q.stride(0), q.stride(1)
+        a.key_norm = k.norm_f.data_ptr() if (k.normalize and k.norm_f is not None and k.n_q) else None
+        k.fill_side(a.k)
+        v.fill_side(a.v)
+        a.softmax_scale = float(scale if scale is not None else 1.0 / math.sqrt(D))
+        ref = C.byref(a)
+        ws_bytes = self._lib.innerq_decode_attn_workspace(ref)
+        if ws_bytes < 0:
+            raise _lib.InnerqError("innerq_decode_attn_workspace", -1, _lib.last_error())
+        ws = _workspace(q.device, ws_bytes)
+        if out is None:
+            if self.out is None or self.out.shape != (B, Hq, D) or self.out.dtype != q.dtype:
+                self.out = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
+            out = self.out
+        _lib.call("innerq_decode_attn", ref, ws.data_ptr(), ws.numel(), out.data_ptr(),
+                  out.stride(0), out.stride(1), None, stream_ptr(q.device))
+        return out
+
+
 def plan(args: _lib.AttnArgs) -> tuple[int, int]:
     nt, ns = C.c_int32(), C.c_int32()
     _lib.call("innerq_attn_plan", C.byref(args), C.byref(nt), C.byref(ns))

@@ -44,6 +44,7 @@ class InnerqDynamicLayer(CacheLayerMixin):
         self.layer_idx = layer_idx
         self.cumulative_length = 0
         self.fused = bool(getattr(config, "_attn_implementation", None) == "innerq")
+        self._attn = None
         super().__init__()
 
     # cache.py:70-119
@@ -174,10 +175,17 @@ class InnerqDynamicLayer(CacheLayerMixin):
         return self.get_deq_tensors()
 
     def attend(self, query: torch.Tensor, scaling: float | None = None,
-               out: torch.Tensor | None = None) -> torch.Tensor:
-        """Fused decode attention of query [B, Hq, 1, D] over this layer."""
-        from .attention import decode_attention
-        return decode_attention(query, self._k, self._v, scaling, out=out)
+               out: torch.Tensor | None = None, reuse: bool = False) -> torch.Tensor:
+        """Fused decode attention of query [B, Hq, 1, D] over this layer ->
+        [B, Hq, D].  With reuse=True the result lives in a per-layer buffer
+        that the next call overwrites (the model hook consumes it at once)."""
+        if self._attn is None:
+            from .attention import DecodeAttention
+            self._attn = DecodeAttention()
+        out_ = self._attn(query, self._k, self._v, scaling, out=out)
+        # the launcher reuses its buffer on the next step: hand out a copy-free
+        # view only when the caller gave the destination
+        return out_ if (out is not None or reuse) else out_.clone()
 
     def get_mask_sizes(self, cache_position) -> tuple[int, int]:
         """cache.py:398-402; also takes the int query_length of transformers >= 5.5."""

@@ -34,7 +34,7 @@ def innerq_attention_forward(module, query, key, value, attention_mask, dropout:
     if layer is not None:
         key._innerq_layer = None
         if query.shape[2] == 1 and _trivial_mask(attention_mask):
-            out = layer.attend(query, scaling)           # [B, Hq, D]
+            out = layer.attend(query, scaling, reuse=True)  # [B, Hq, D]
             return out.unsqueeze(1), None                # [B, q_len=1, Hq, D]
         key, value = layer.get_deq_tensors()
     return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,

@@ -34,7 +34,16 @@ def dtype_code(dt: torch.dtype) -> int:
     raise TypeError(f"innerq_b200 kernels take float16 or bfloat16 tensors, got {dt}")
 
 
+try:
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
 def stream_ptr(device: torch.device) -> int:
+    """cudaStream_t of the current torch stream on `device` (as an int)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -141,7 +150,8 @@ class PackedSide:
         need = self._rn + n_new
         if self._rbuf is not None and self._r0 + need <= self._rbuf.shape[2]:
             return
-        cap = max(need, self.w_recent + self.flush + 32, 2 * self._rn)
+        # slack so the FIFO compacts rarely (once per ~1000 appended tokens)
+        cap = max(need, self.w_recent + self.flush + 1024, 2 * self._rn)
         if self._rbuf is None or cap > self._rbuf.shape[2]:
             buf = torch.empty((self.B, self.H, cap, self.D), dtype=self.dtype, device=self.device)
         else:
@@ -256,22 +266,33 @@ class PackedSide:
                   scale.data_ptr(), _ptr(zs if sign is None else None), stream_ptr(self.device))
         return codes, scale, zs
 
-    def side_struct(self) -> _lib.Side:
-        s = _lib.Side()
-        s.codes = _ptr(self.codes) if self.n_q else None
-        s.scale = _ptr(self.scale) if self.n_q else None
-        s.zero = _ptr(self.zero) if self.n_q else None
+    def fill_side(self, s: _lib.Side) -> _lib.Side:
+        """Write this side's current geometry into a (reused) C struct; the
+        recent-window pointer is computed without building a tensor view."""
+        nq = self.n_q
+        s.codes = self.codes.data_ptr() if nq else None
+        s.scale = self.scale.data_ptr() if nq else None
+        s.zero = self.zero.data_ptr() if (nq and self.zero is not None) else None
         s.cap_tiles = self.cap_tiles
-        if self.n_sink:
+        if self.sink is not None and self.sink.shape[2]:
             s.sink = self.sink.data_ptr()
             s.sink_sb, s.sink_sh, s.sink_st = self.sink.stride()[:3]
+            s.n_sink = self.sink.shape[2]
+        else:
+            s.sink, s.n_sink = None, 0
         if self._rn:
-            r = self.recent
-            s.recent = r.data_ptr()
-            s.rec_sb, s.rec_sh, s.rec_st = r.stride()[:3]
-        s.n_sink, s.n_q, s.n_recent = self.n_sink, self.n_q, self._rn
+            rb = self._rbuf
+            sb, sh, st, _ = rb.stride()
+            s.recent = rb.data_ptr() + self._r0 * st * rb.element_size()
+            s.rec_sb, s.rec_sh, s.rec_st = sb, sh, st
+        else:
+            s.recent = None
+        s.n_q, s.n_recent = nq, self._rn
         s.bits, s.group, s.mode, s.over_token = self.bits, self.group, self.mode, int(self.over_token)
         return s
+
+    def side_struct(self) -> _lib.Side:
+        return self.fill_side(_lib.Side())
 
 
 class HybridSide(PackedSide):
