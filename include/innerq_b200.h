@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define INNERQ_ABI_VERSION 1
+#define INNERQ_ABI_VERSION 2
 
 enum {
   INNERQ_OK = 0,
@@ -155,7 +155,8 @@ typedef struct {
  * split count it will use (n_splits resolved). */
 int innerq_attn_plan(const innerq_attn_args* args, int32_t* n_tiles, int32_t* n_splits);
 
-/* Workspace bytes innerq_decode_attn needs (the split-KV partials). */
+/* Workspace bytes innerq_decode_attn needs: the split-KV partials and the
+ * per-(batch, KV head) query blocks the attention pass reads. */
 int64_t innerq_decode_attn_workspace(const innerq_attn_args* args);
 
 /*
@@ -164,7 +165,7 @@ int64_t innerq_decode_attn_workspace(const innerq_attn_args* args);
  * reading the packed K/V and fp16 sink / recent tokens directly.  Replaces
  * InnerqDynamicLayer.get_deq_tensors (cache.py:278-281) followed by the HF
  * sdpa consumer.  workspace (>= innerq_decode_attn_workspace bytes, 16-byte
- * aligned) holds the split partials.  out [B][Hq][D] dtype with strides
+ * aligned) holds the split partials and the query blocks.  out [B][Hq][D] dtype with strides
  * (o_sb, o_sh); lse (nullable, [B][Hq] fp32) receives log2-sum-exp2 of the
  * scaled logits.
  */
@@ -175,9 +176,12 @@ int innerq_decode_attn(const innerq_attn_args* args, void* workspace, int64_t wo
  * Partials only: part_o [B][Hq][n_splits][D] fp32 (unnormalised), part_m and
  * part_l [B][Hq][n_splits] (log2-domain running max and sum).  For context
  * sharding across GPUs: gather the partials, then innerq_lse_merge.
+ * workspace (>= innerq_decode_attn_workspace bytes, 16-byte aligned) holds the
+ * query blocks.
  */
 int innerq_decode_attn_partials(const innerq_attn_args* args, float* part_o, float* part_m,
-                                float* part_l, void* stream);
+                                float* part_l, void* workspace, int64_t workspace_bytes,
+                                void* stream);
 
 /* Merge split partials: out[row] = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s,
  * rows = B * rows_per_b, out row (b, h) at b*o_sb + h*o_sh. */

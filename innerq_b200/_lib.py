@@ -85,7 +85,7 @@ def load() -> C.CDLL:
         "innerq_attn_plan": (i32, [C.POINTER(AttnArgs), C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
         "innerq_decode_attn_workspace": (i64, [C.POINTER(AttnArgs)]),
         "innerq_decode_attn": (i32, [C.POINTER(AttnArgs), vp, i64, vp, i64, i64, vp, vp]),
-        "innerq_decode_attn_partials": (i32, [C.POINTER(AttnArgs), vp, vp, vp, vp]),
+        "innerq_decode_attn_partials": (i32, [C.POINTER(AttnArgs), vp, vp, vp, vp, i64, vp]),
         "innerq_decode_attn_noalloc": (i32, [C.POINTER(AttnArgs), vp, i64, i64, vp, vp]),
         "innerq_lse_merge": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp, i64, i64, vp, vp]),
     }
@@ -93,7 +93,7 @@ def load() -> C.CDLL:
         f = getattr(lib, name)
         f.restype = res
         f.argtypes = args
-    if lib.innerq_abi_version() != 1:
+    if lib.innerq_abi_version() != 2:
         raise ImportError("libinnerq_b200.so ABI version mismatch; rebuild it")
     _lib = lib
     return lib
@@ -102,8 +102,8 @@ def load() -> C.CDLL:
 # kernels each compute entry point launches (for launch accounting in bench.py)
 KERNELS_PER_CALL = {
     "innerq_norm_factor": 1, "innerq_quant_pack": 1, "innerq_unpack_ref": 1, "innerq_dequant": 1,
-    "innerq_dequant_ref": 1, "innerq_decode_attn": 2, "innerq_decode_attn_partials": 1,
-    "innerq_lse_merge": 1, "innerq_decode_attn_noalloc": 2,
+    "innerq_dequant_ref": 1, "innerq_decode_attn": 3, "innerq_decode_attn_partials": 2,
+    "innerq_lse_merge": 1, "innerq_decode_attn_noalloc": 3,
 }
 launch_count = [0]
 

@@ -141,8 +141,12 @@ def decode_attention_partials(q: torch.Tensor, k: PackedSide, v: PackedSide,
     po = torch.empty((B, Hq, ns, D), dtype=torch.float32, device=q.device)
     pm = torch.empty((B, Hq, ns), dtype=torch.float32, device=q.device)
     pl = torch.empty((B, Hq, ns), dtype=torch.float32, device=q.device)
+    ws_bytes = _lib.load().innerq_decode_attn_workspace(C.byref(args))
+    if ws_bytes < 0:
+        raise _lib.InnerqError("innerq_decode_attn_workspace", -1, _lib.last_error())
+    ws = _workspace(q.device, ws_bytes)
     _lib.call("innerq_decode_attn_partials", C.byref(args), po.data_ptr(), pm.data_ptr(),
-              pl.data_ptr(), stream_ptr(q.device))
+              pl.data_ptr(), ws.data_ptr(), ws.numel(), stream_ptr(q.device))
     return po, pm, pl
 
 

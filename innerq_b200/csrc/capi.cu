@@ -115,8 +115,8 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   int splits = a->n_splits;
   if (splits <= 0) {
     // cost model: waves of resident CTAs x (tiles per CTA + per-CTA overhead
-    // worth ~12 tiles); the best split count balances wave quantisation
-    // against the fixed prologue/epilogue of each CTA
+    // worth ~6 tiles: the query-block wait, the warp combine and the partial
+    // write); the best split count balances wave quantisation against it
     const int64_t bh = (int64_t)a->B * a->Hkv;
     const int64_t slots = (int64_t)sm_count() * (p.R <= 4 ? 4 : 3);
     int64_t best = -1;
@@ -124,7 +124,7 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
     for (int s = 1; s <= 256 && s <= (ntr > 0 ? ntr : 1); ++s) {
       const int64_t tpc = (ntr + s - 1) / s;
       const int64_t waves = (bh * s + slots - 1) / slots;
-      const int64_t cost = waves * (tpc + 12);
+      const int64_t cost = waves * (tpc + 6);
       if (best < 0 || cost < best) { best = cost; splits = s; }
     }
   }
@@ -152,8 +152,19 @@ DevSide dev_side(const innerq_side& s) {
   return d;
 }
 
+int64_t part_bytes(const innerq_attn_args* a, const Plan& p) {
+  const int64_t rows = (int64_t)a->B * a->Hq * p.n_splits;
+  return rows * kD * 4 + 2 * ((rows * 4 + 255) / 256 * 256);
+}
+
+int64_t ws_bytes(const innerq_attn_args* a, const Plan& p) {
+  const int rp = p.R <= 4 ? 4 : 8;
+  return part_bytes(a, p) + (int64_t)a->B * a->Hkv * qprep_bytes(rp);
+}
+
+// prep pass + attention pass; qprep: the query-block region of a workspace
 int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm, float* pl,
-                 cudaStream_t st) {
+                 void* qprep, cudaStream_t st) {
   DevArgs d;
   d.k = dev_side(a->k);
   d.v = dev_side(a->v);
@@ -167,23 +178,20 @@ int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm,
   d.tiles_per_split = p.tps; d.n_splits = p.n_splits;
   d.scale_log2 = a->softmax_scale * 1.4426950408889634f;
   d.po = po; d.pm = pm; d.pl = pl;
+  d.qprep = qprep;
   d.R = p.R;
   dim3 grid(p.n_splits, a->Hkv, a->B);
   const int rp = p.R <= 4 ? 4 : 8;
   const int ng = a->k.n_q > 0 ? kD / a->k.group : 4;
   const bool bf = a->dtype == INNERQ_DT_BF16;
-  cudaError_t e;
+  cudaError_t e = launch_qprep(d, rp, ng, bf, st);
+  if (e != cudaSuccess) return cuda_status(e, "qprep");
   switch (p.bk) {
     case 2: e = bf ? launch_attn_k2_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k2_f16(d, p.bv, rp, ng, grid, st); break;
     case 3: e = bf ? launch_attn_k3_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k3_f16(d, p.bv, rp, ng, grid, st); break;
     default: e = bf ? launch_attn_k4_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k4_f16(d, p.bv, rp, ng, grid, st); break;
   }
   return cuda_status(e, "decode_attn");
-}
-
-int64_t ws_bytes(const innerq_attn_args* a, const Plan& p) {
-  const int64_t rows = (int64_t)a->B * a->Hq * p.n_splits;
-  return rows * kD * 4 + 2 * ((rows * 4 + 255) / 256 * 256);
 }
 
 }  // namespace
@@ -302,12 +310,18 @@ int64_t innerq_decode_attn_workspace(const innerq_attn_args* args) {
 }
 
 int innerq_decode_attn_partials(const innerq_attn_args* args, float* part_o, float* part_m,
-                                float* part_l, void* stream) {
+                                float* part_l, void* workspace, int64_t workspace_bytes,
+                                void* stream) {
   Plan p;
   int rc = make_plan(args, p);
   if (rc) return rc;
   if (!part_o || !part_m || !part_l) return fail(INNERQ_ERR_ARG, "null partials");
-  return run_partials(args, p, part_o, part_m, part_l, (cudaStream_t)stream);
+  const int64_t need = ws_bytes(args, p);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
+    return fail(INNERQ_ERR_ARG, "workspace %lld bytes < %lld needed (or misaligned)",
+                (long long)workspace_bytes, (long long)need);
+  return run_partials(args, p, part_o, part_m, part_l, (char*)workspace + part_bytes(args, p),
+                      (cudaStream_t)stream);
 }
 
 int innerq_decode_attn(const innerq_attn_args* args, void* workspace, int64_t workspace_bytes,
@@ -324,7 +338,7 @@ int innerq_decode_attn(const innerq_attn_args* args, void* workspace, int64_t wo
   float* po = (float*)workspace;
   float* pm = po + rows * kD;
   float* pl = (float*)((char*)pm + (rows * 4 + 255) / 256 * 256);
-  rc = run_partials(args, p, po, pm, pl, (cudaStream_t)stream);
+  rc = run_partials(args, p, po, pm, pl, (char*)workspace + part_bytes(args, p), (cudaStream_t)stream);
   if (rc) return rc;
   return cuda_status(launch_lse_merge(po, pm, pl, args->B * args->Hq, args->Hq, p.n_splits,
                                       args->dtype, out, o_sb, o_sh, lse, (cudaStream_t)stream),

@@ -15,7 +15,8 @@
 //          crumb 4i + (kb&1)*2 + half
 //     b=3: low 2 bits as b=2 in plane L (1024 B / tile); bit 2 in plane H
 //          (512 B / tile, 1 word per row): bit 8i + kb*2 + half
-//   Scales / zero points (ng = D/G per token) per tile: [gid 8][j 4][ng].
+//   Scales / zero points (ng = D/G per token) per tile: [gid 8][g ng][j 4], so
+//   rows j = 2m, 2m+1 (the two rows of one MMA m-tile) share a 32-bit word.
 //
 // "col" layout (V, token groups; A = V^T[dim][token]):
 //   Lane L = 4*gid + tq owns dims d = mt*16 + h*8 + gid (mt = 0..7, h = 0..1)
@@ -204,7 +205,7 @@ __host__ __device__ inline BitPos col_pos(int bits, int r, int d) {
 
 // scale index inside a row-layout tile (channel groups)
 __host__ __device__ inline int row_scale_idx(int r, int g, int ng) {
-  return ((r & 7) * 4 + (r >> 3)) * ng + g;
+  return ((r & 7) * ng + g) * 4 + (r >> 3);
 }
 // scale index inside a col-layout group (token groups)
 __host__ __device__ inline int col_scale_idx(int d) {

@@ -20,6 +20,10 @@
 // Boundary tiles (sink, recent, the K/V packed/dense seams) load directly
 // from global memory.
 //
+// The query side (digits, B fragments, group sums) of each (batch, KV head)
+// is built once by qprep_kernel; each CTA bulk-copies that block while its
+// first KV stages are in flight (programmatic dependent launch).
+//
 // Arithmetic: packed codes are multiplied on the tensor cores with
 // mma.sync m16n8k32 u8 x s8/u8 -> s32, so every partial dot product is exact:
 //   QK^T: A = K codes [token][dim] (u8), B = q*f*2^e rounded to a 22-bit
@@ -63,14 +67,14 @@ struct DevArgs {
   int tile_lo, tile_hi;
   int tiles_per_split, n_splits;
   float scale_log2;    // softmax scale * log2(e)
+  const void* qprep;   // [B][Hkv] QPrep<RP> blocks written by qprep_kernel
   float* po;           // [B][Hq][n_splits][D]
   float* pm;           // [B][Hq][n_splits]
   float* pl;
 };
 
 constexpr int kWarps = 4;
-// staging slots per warp: 2 where 4 CTAs share an SM (<= 4 query heads per
-// KV head), 3 where 2 CTAs do
+// staging ring depth (stages of kWarps tiles); 2 keeps 4 CTAs per SM
 __host__ __device__ constexpr int stages_for(int rp) { return 2; }
 // bounded mbarrier wait: each try suspends the warp for up to ~100 us (hint,
 // in ns) instead of spinning; 1 << 16 tries bound the wait to seconds
@@ -118,6 +122,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+// programmatic dependent launch: the prep kernel lets the attention grid start
+// early; the attention grid waits for the prep grid (and its memory) here
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 // plain (non-multicast) bulk copy global -> this CTA's shared memory
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -235,18 +245,16 @@ template <> __device__ __forceinline__ float2 pair_to_f2<BF16>(uint32_t w) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
-// 16 16-bit values (32 B) as floats
+// 16 16-bit values (32 B) as 8 float pairs
 template <int DT>
-__device__ __forceinline__ void load16(float out[16], const uint16_t* p) {
+__device__ __forceinline__ void load16(float2 out[8], const uint16_t* p) {
   const uint4 a = reinterpret_cast<const uint4*>(p)[0], b = reinterpret_cast<const uint4*>(p)[1];
   const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const float2 f = pair_to_f2<DT>(w[u]);
-    out[2 * u] = f.x;
-    out[2 * u + 1] = f.y;
-  }
+  for (int u = 0; u < 8; ++u) out[u] = pair_to_f2<DT>(w[u]);
 }
+
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 
 // dense (fp16 / bf16) row pointer for token t of a side, or null
 __device__ __forceinline__ const uint16_t* dense_row(const DevSide& s, int b, int h, int t, int S) {
@@ -267,19 +275,33 @@ __device__ __forceinline__ bool is_fast_tile(const DevArgs& a, int tile) {
          t0 >= vs && t0 + kTile <= vs + nqv;
 }
 
+// Everything the attention pass needs from the query of one (batch, KV head),
+// built once by qprep_kernel and bulk-copied into each CTA of that pair.
+template <int RP>
+struct QPrep {
+  static constexpr int NT = RP / 4;
+  uint2 bk[2 * NT][4][32];  // packed-K B fragments (three int8 digits of q*f*2^e_p)
+  int qsum[RP][4];          // sum of the integer query over each K channel group
+  int e_p, e_d, pad0, pad1; // exponents of the packed / dense query scalings
+  uint2 bd[NT][8][32];      // dense-K B fragments (dtype hi/lo of q*2^e_d)
+  // bytes every CTA copies; the dense fragments follow only where needed
+  static constexpr uint32_t kHead = sizeof(uint2) * 2 * NT * 4 * 32 + sizeof(int) * (RP * 4 + 4);
+  static constexpr uint32_t kDense = sizeof(uint2) * NT * 8 * 32;
+};
+static_assert(QPrep<4>::kHead % 16 == 0 && QPrep<8>::kHead % 16 == 0, "bulk copy granularity");
+static_assert(sizeof(QPrep<4>) == QPrep<4>::kHead + QPrep<4>::kDense, "QPrep layout");
+static_assert(sizeof(QPrep<8>) == QPrep<8>::kHead + QPrep<8>::kDense, "QPrep layout");
+
 template <int RP>
 struct AttnStatic {
   static constexpr int NT = RP / 4;
   static constexpr int kStages = stages_for(RP);
+  alignas(128) QPrep<RP> qp;  // this pair's query block (bulk-copied)
   uint64_t bars[kStages];     // "stage full" barriers of the CTA's staging ring
+  uint64_t prep_bar;          // the query block has landed
   int cnt[kStages];           // warps done with each stage
-  int ctot_s[RP][4];          // K offset correction per channel group: off * sum q
-  float qsum_s[RP][4];        // sum of q over each K channel group (asymmetric zero term)
-  uint2 bk_s[2 * NT][4][32];  // packed-K B fragments (three int8 digits of q)
-  uint2 bd_s[NT][8][32];      // dense-K B fragments (dtype hi/lo)
   float p_s[kWarps][RP][kTile];
   uint8_t pd_s[kWarps][RP][2][kTile];
-  float red_s[2][kWarps];
   float cm_s[kWarps][RP];
   float cl_s[kWarps][RP];
 };
@@ -295,11 +317,12 @@ __device__ __forceinline__ void digits3(int v, int& d0, int& d1, int& d2) {
 // Logits (before the softmax scale) of the lane's 4 token rows for its
 // head(s) from packed K words: lp[nt][j] += sum_g s[j][g] * (sum_d u q - off*sum_d q)
 // (+ z[j][g] * sum_d q for asymmetric keys).  All partial sums are exact int32.
+// Rows j = 2m, 2m+1 travel as one float pair (.x, .y): lp[nt][m], sc[m][g].
 template <int BK, int NT, int NG, bool KASYM>
-__device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const float sc[4][NG],
-                                                const float zc[4][NG], const uint2 (*bks)[4][32],
+__device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const float2 sc[2][NG],
+                                                const float2 zc[2][NG], const uint2 (*bks)[4][32],
                                                 const int ctot[NT][NG], const float qsf[NT][NG],
-                                                int lane, float lp[NT][4]) {
+                                                int lane, float2 lp[NT][2]) {
   constexpr int KPG = 4 / NG;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -324,16 +347,18 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
       }
       if (kb % KPG == KPG - 1) {
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
+        for (int mt = 0; mt < 2; ++mt) {
+          float tf[2];
 #pragma unroll
           for (int rr = 0; rr < 2; ++rr) {
-            const int j = 2 * mt + rr;
             // the exact sum fits int32; intermediate terms wrap modulo 2^32
             const uint32_t t = (uint32_t)acc[mt][0][2 * rr] * 65536u +
                                (uint32_t)acc[mt][0][2 * rr + 1] * 256u + (uint32_t)acc[mt][1][2 * rr];
-            lp[nt][j] = fmaf(sc[j][g], (float)(int)t, lp[nt][j]);
-            if constexpr (KASYM) lp[nt][j] = fmaf(zc[j][g], qsf[nt][g], lp[nt][j]);
+            tf[rr] = (float)(int)t;
           }
+          lp[nt][mt] = __ffma2_rn(sc[mt][g], make_float2(tf[0], tf[1]), lp[nt][mt]);
+          if constexpr (KASYM) lp[nt][mt] = __ffma2_rn(zc[mt][g], f2(qsf[nt][g]), lp[nt][mt]);
+        }
       }
     }
   }
@@ -342,15 +367,15 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
 // O[nt][mt][h] += fv * (s * (sum_t u p - off * sum_t p) [+ z * sum_t p]) for one
 // packed V tile (integer MMA, probabilities as two u8 digits)
 template <int BV, int NT, bool VASYM>
-__device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const float sv[16],
-                                                    const float zv[16], const uint32_t pb[NT][2],
+__device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const float2 sv[8],
+                                                    const float2 zv[8], const uint32_t pb[NT][2],
                                                     const int offp[NT], const float fv[NT],
-                                                    const float zf[NT], float o[NT][8][2]) {
-  float svf[NT][16];
+                                                    const float zf[NT], float2 o[NT][8]) {
+  float2 svf[NT][8];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int u = 0; u < 16; ++u) svf[nt][u] = sv[u] * fv[nt];
+    for (int u = 0; u < 8; ++u) svf[nt][u] = __fmul2_rn(sv[u], f2(fv[nt]));
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
     const uint32_t af[4] = {col_frag<BV>(vc.w, mt, 0, 0), col_frag<BV>(vc.w, mt, 1, 0),
@@ -359,19 +384,17 @@ __device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const 
     for (int nt = 0; nt < NT; ++nt) {
       int acc[4];
       imma_u8u8(acc, af, pb[nt], 0, -offp[nt], 0, -offp[nt]);
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int t = acc[2 * hh] * 256 + acc[2 * hh + 1];
-        o[nt][mt][hh] = fmaf(svf[nt][mt * 2 + hh], (float)t, o[nt][mt][hh]);
-        if constexpr (VASYM) o[nt][mt][hh] = fmaf(zv[mt * 2 + hh], zf[nt], o[nt][mt][hh]);
-      }
+      const float t0 = (float)(acc[0] * 256 + acc[1]), t1 = (float)(acc[2] * 256 + acc[3]);
+      o[nt][mt] = __ffma2_rn(svf[nt][mt], make_float2(t0, t1), o[nt][mt]);
+      if constexpr (VASYM) o[nt][mt] = __ffma2_rn(zv[mt], f2(zf[nt]), o[nt][mt]);
     }
   }
 }
 
-// scales / zero points of the lane's 4 rows (row layout), 8*NG bytes at p
+// scales / zero points of the lane's 4 rows (row layout, [g][j]), 8*NG bytes at
+// p, as pairs of rows: out[m][g] = (row 2m, row 2m+1)
 template <int DT, int NG>
-__device__ __forceinline__ void load_kscales(float out[4][NG], const uint16_t* p) {
+__device__ __forceinline__ void load_kscales(float2 out[2][NG], const uint16_t* p) {
   uint32_t w[2 * NG];
   if constexpr (NG == 4) {
     const uint4 a = reinterpret_cast<const uint4*>(p)[0], b = reinterpret_cast<const uint4*>(p)[1];
@@ -384,11 +407,9 @@ __device__ __forceinline__ void load_kscales(float out[4][NG], const uint16_t* p
     w[0] = a.x; w[1] = a.y;
   }
 #pragma unroll
-  for (int u = 0; u < 2 * NG; ++u) {
-    const float2 f = pair_to_f2<DT>(w[u]);
-    out[(2 * u) / NG][(2 * u) % NG] = f.x;
-    out[(2 * u + 1) / NG][(2 * u + 1) % NG] = f.y;
-  }
+  for (int g = 0; g < NG; ++g)
+#pragma unroll
+    for (int m = 0; m < 2; ++m) out[m][g] = pair_to_f2<DT>(w[2 * g + m]);
 }
 
 // BK/BV: code bits; RP: query heads per KV head padded to 4 or 8; DT: dtype;
@@ -398,8 +419,6 @@ __global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 3)
 decode_attn_kernel(const DevArgs a) {
   constexpr int NT = RP / 4;
   constexpr int kStages = stages_for(RP);
-  constexpr int KPG = 4 / NG;           // 32-dim k-blocks per channel group
-  constexpr int QBITS = NG == 4 ? 22 : (NG == 2 ? 21 : 20);  // |q int| < 2^QBITS
   extern __shared__ __align__(128) uint8_t dyn[];
   __shared__ AttnStatic<RP> sm;
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
@@ -415,117 +434,7 @@ decode_attn_kernel(const DevArgs a) {
   const int koff = kasym ? 0 : (1 << (BK - 1));
   const int voff = vasym ? 0 : (1 << (BV - 1));
 
-  // ---------------------------------------------------------------- prologue
-  float* q_s = reinterpret_cast<float*>(dyn);          // [RP][128] q*f   (prologue only)
-  float* qd_s = q_s + RP * kD;                         // [RP][128] q
-  int* qi_s = reinterpret_cast<int*>(qd_s + RP * kD);  // [RP][128] integer q*f*2^e
-  float amax_p = 0.f, amax_d = 0.f;
-  for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
-    const int h = i / kD, d = i % kD;
-    float qv = 0.f, f = 1.f;
-    if (h < R) {
-      qv = to_f<DT>(a.q[b * a.q_b + (int64_t)(hk * R + h) * a.q_h + d]);
-      if (a.kf) f = to_f<DT>(a.kf[((int64_t)b * a.Hkv + hk) * kD + d]);
-    }
-    const float qp = qv * f;
-    q_s[i] = qp;
-    qd_s[i] = qv;
-    amax_p = fmaxf(amax_p, fabsf(qp));
-    amax_d = fmaxf(amax_d, fabsf(qv));
-  }
-  amax_p = warp_max(amax_p);
-  amax_d = warp_max(amax_d);
-  if (lane == 0) { sm.red_s[0][warp] = amax_p; sm.red_s[1][warp] = amax_d; }
-  if (threadIdx.x < kStages) {
-    mbar_init(&sm.bars[threadIdx.x], 1);
-    sm.cnt[threadIdx.x] = 0;
-  }
-  mbar_fence_init();
-  __syncthreads();
-  amax_p = fmaxf(fmaxf(sm.red_s[0][0], sm.red_s[0][1]), fmaxf(sm.red_s[0][2], sm.red_s[0][3]));
-  amax_d = fmaxf(fmaxf(sm.red_s[1][0], sm.red_s[1][1]), fmaxf(sm.red_s[1][2], sm.red_s[1][3]));
-  int ex, e_p = 0, e_d = 0;
-  if (amax_p > 0.f) { frexpf(amax_p, &ex); e_p = QBITS - ex; }
-  if (amax_d > 0.f) { frexpf(amax_d, &ex); e_d = 15 - ex; }
-  for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
-    qi_s[i] = __float2int_rn(ldexpf(q_s[i], e_p));
-    qd_s[i] = ldexpf(qd_s[i], e_d);
-  }
-  __syncthreads();
-  // per (head, channel group) sums of q: one warp per head, lanes over dims
-  for (int h = warp; h < RP; h += kWarps) {
-    int s[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) s[c] = qi_s[h * kD + c * 32 + lane];
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s[c] += __shfl_xor_sync(0xffffffffu, s[c], o);
-    if (lane < 4) {
-      int t = 0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) t += (c / KPG == lane) ? s[c] : 0;
-      sm.ctot_s[h][lane] = koff * t;
-      sm.qsum_s[h][lane] = (float)t;
-    }
-  }
-  // packed-K B fragments (m16n8k32): n-tile 2*quad holds digits (d2, d1) and
-  // 2*quad+1 holds (d0, 0) of each of the quad's 4 heads.  First split every
-  // q into its three digit bytes (in place of q_s, dead by now), then each
-  // fragment word is one 32-bit read of 4 consecutive digit bytes.
-  int8_t* dg_s = reinterpret_cast<int8_t*>(q_s);  // [3][RP][128]
-  for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
-    int d0, d1, d2;
-    digits3(qi_s[i], d0, d1, d2);
-    dg_s[i] = (int8_t)d0;
-    dg_s[RP * kD + i] = (int8_t)d1;
-    dg_s[2 * RP * kD + i] = (int8_t)d2;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 2 * NT * 4 * 32; i += kWarps * 32) {
-    const int ntk = i / 128, kb = (i / 32) % 4, ln = i % 32;
-    const int g2 = ln >> 2, t2 = ln & 3;
-    const int head = (ntk >> 1) * 4 + (g2 >> 1), which = g2 & 1;
-    // digit plane: n-tile 2q -> (d2, d1), n-tile 2q+1 -> (d0, none)
-    const int plane = (ntk & 1) ? (which ? -1 : 0) : (which ? 1 : 2);
-    uint32_t wrd[2] = {0u, 0u};
-    if (plane >= 0) {
-      const int8_t* src = dg_s + plane * RP * kD + head * kD + kb * 32 + 4 * t2;
-      wrd[0] = *reinterpret_cast<const uint32_t*>(src);
-      wrd[1] = *reinterpret_cast<const uint32_t*>(src + 16);
-    }
-    sm.bk_s[ntk][kb][ln] = make_uint2(wrd[0], wrd[1]);
-  }
-  // dense-K B fragments (m16n8k16, dtype hi/lo of q * 2^e_d), only for CTAs
-  // that meet a sink / recent / seam tile (packed tiles form one contiguous run)
-  const bool any_dense = tile_end > tile_beg && !(is_fast_tile(a, tile_beg) && is_fast_tile(a, tile_end - 1));
-  for (int i = threadIdx.x; any_dense && i < NT * 8 * 32; i += kWarps * 32) {
-    const int nt = i / 256, kb = (i / 32) % 8, ln = i % 32;
-    const int g2 = ln >> 2, t2 = ln & 3;
-    const int head = nt * 4 + (g2 >> 1), part = g2 & 1;
-    const int dd[4] = {kb * 16 + 2 * t2, kb * 16 + 2 * t2 + 1, kb * 16 + 2 * t2 + 8, kb * 16 + 2 * t2 + 9};
-    uint16_t v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      uint16_t hi, lo;
-      split_hilo<DT>(qd_s[head * kD + dd[u]], hi, lo);
-      v[u] = part ? lo : hi;
-    }
-    sm.bd_s[nt][kb][ln] = make_uint2(pack2(v[0], v[1]), pack2(v[2], v[3]));
-  }
-  __syncthreads();  // prologue scratch in `dyn` is dead from here on
 
-  int ctot[NT][NG];
-  float qsf[NT][NG];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int g = 0; g < NG; ++g) {
-      ctot[nt][g] = sm.ctot_s[nt * 4 + tq][g];
-      qsf[nt][g] = sm.qsum_s[nt * 4 + tq][g];
-    }
-  const float cp = ldexpf(a.scale_log2, -e_p);
-  const float cd = ldexpf(a.scale_log2, -e_d);
   const int64_t kbh = (int64_t)b * a.Hkv + hk;
   const uint8_t* kcodes = a.k.codes ? a.k.codes + kbh * a.k.cap_tiles * tile_bytes(BK) : nullptr;
   const uint16_t* kscale = a.k.scale ? a.k.scale + kbh * a.k.cap_tiles * 32 * NG : nullptr;
@@ -587,25 +496,57 @@ decode_attn_kernel(const DevArgs a) {
     if (vasym) bulk_g2s(st + o_vz, vzero + g0 * kD, nvg * 256, bar);
   };
 
-  float m_run[NT], l_run[NT], o[NT][8][2];
+  float m_run[NT], l_run[NT];
+  float2 o[NT][8];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     m_run[nt] = -INFINITY;
     l_run[nt] = 0.f;
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) o[nt][mt][0] = o[nt][mt][1] = 0.f;
+    for (int mt = 0; mt < 8; ++mt) o[nt][mt] = make_float2(0.f, 0.f);
   }
 
+  // dense-K B fragments are needed only by CTAs that meet a sink / recent /
+  // seam tile (packed tiles form one contiguous run)
+  const bool any_dense = tile_end > tile_beg && !(is_fast_tile(a, tile_beg) && is_fast_tile(a, tile_end - 1));
   if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.bars[s], 1);
+      sm.cnt[s] = 0;
+    }
+    mbar_init(&sm.prep_bar, 1);
+    mbar_fence_init();
+    // the KV tiles do not depend on the prep kernel: start them at once
 #pragma unroll 1
     for (int s = 0; s < kStages; ++s) issue(s);
   }
-  bool failed = false;
+  griddep_wait();  // the prep kernel's query blocks are complete and visible
+  if (threadIdx.x == 0) {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.qprep) + ((int64_t)b * a.Hkv + hk) * sizeof(QPrep<RP>);
+    constexpr uint32_t kH = QPrep<RP>::kHead, kDn = QPrep<RP>::kDense;
+    mbar_arrive_tx(&sm.prep_bar, kH + (any_dense ? kDn : 0u));
+    bulk_g2s(&sm.qp, src, kH, &sm.prep_bar);
+    if (any_dense) bulk_g2s(&sm.qp.bd, src + kH, kDn, &sm.prep_bar);
+  }
+  __syncthreads();  // barrier initialisation is visible to every thread
+  bool failed = !mbar_wait_bounded(&sm.prep_bar, 0, kWaitLimit);
   int i_done = 0;
+  int ctot[NT][NG];
+  float qsf[NT][NG];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const int qs = sm.qp.qsum[nt * 4 + tq][g];
+      ctot[nt][g] = koff * qs;
+      qsf[nt][g] = (float)qs;
+    }
+  const float cp = ldexpf(a.scale_log2, -sm.qp.e_p);
+  const float cd = ldexpf(a.scale_log2, -sm.qp.e_d);
 
   // ---------------------------------------------------------------- tiles
 #pragma unroll 1
-  for (int i = 0; i < n_st; ++i) {
+  for (int i = 0; i < (failed ? 0 : n_st); ++i) {
     const int slot = i % kStages;
     if (!mbar_wait_bounded(&sm.bars[slot], (uint32_t)((i / kStages) & 1), kWaitLimit)) {
       failed = true;
@@ -622,23 +563,25 @@ decode_attn_kernel(const DevArgs a) {
     // ----------------------------------------------------------- QK^T
     if (fast) {
       KRow<BK> rw[4];
-      float sc[4][NG], zc[4][NG];
+      float2 sc[2][NG], zc[2][NG];
       load_krows<BK>(rw, sg + warp * TBK, lane);
       load_kscales<DT, NG>(sc, reinterpret_cast<const uint16_t*>(sg + o_ks + warp * 64 * NG) + gid * 4 * NG);
       if (kasym)
         load_kscales<DT, NG>(zc, reinterpret_cast<const uint16_t*>(sg + o_kz + warp * 64 * NG) + gid * 4 * NG);
-      float lp[NT][4];
+      float2 lp[NT][2];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) lp[nt][j] = 0.f;
-      if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.bk_s, ctot, qsf, lane, lp);
-      else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.bk_s, ctot, qsf, lane, lp);
+      for (int nt = 0; nt < NT; ++nt) lp[nt][0] = lp[nt][1] = make_float2(0.f, 0.f);
+      if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.qp.bk, ctot, qsf, lane, lp);
+      else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.qp.bk, ctot, qsf, lane, lp);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const bool head_ok = nt * 4 + tq < R;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) x[nt][j] = head_ok ? lp[nt][j] * cp : -INFINITY;
+        for (int m = 0; m < 2; ++m) {
+          const float2 xs = __fmul2_rn(lp[nt][m], f2(cp));
+          x[nt][2 * m] = head_ok ? xs.x : -INFINITY;
+          x[nt][2 * m + 1] = head_ok ? xs.y : -INFINITY;
+        }
       }
     } else {
       int src[4];
@@ -650,11 +593,14 @@ decode_attn_kernel(const DevArgs a) {
       const int lo_t = max(t0, 0), hi_t = min(t0 + kTile, S);
       const bool kp_any = nqk > 0 && lo_t < ks + nqk && hi_t > ks;
       const bool kd_any = (lo_t < min(ks, hi_t)) || (hi_t > max(ks + nqk, lo_t));
-      float lp[NT][4], ld[NT][4];
+      float2 lp[NT][2];
+      float ld[NT][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+      for (int nt = 0; nt < NT; ++nt) {
+        lp[nt][0] = lp[nt][1] = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) lp[nt][j] = ld[nt][j] = 0.f;
+        for (int j = 0; j < 4; ++j) ld[nt][j] = 0.f;
+      }
       if (kp_any) {
         KRow<BK> rw[4];
         float sc[4][NG], zc[4][NG];
@@ -668,16 +614,24 @@ decode_attn_kernel(const DevArgs a) {
             const int p = t0 + gid + 8 * j - ks;
             const int ti = p >> 5, r = p & 31;
             load_krow<BK>(rw[j], kcodes + (int64_t)ti * tile_bytes(BK), (r & 7) * 4 + tq, r >> 3);
-            const int64_t so = (int64_t)ti * 32 * NG + ((r & 7) * 4 + (r >> 3)) * NG;
+            const int64_t so = (int64_t)ti * 32 * NG;
 #pragma unroll
             for (int g = 0; g < NG; ++g) {
-              sc[j][g] = to_f<DT>(kscale[so + g]);
-              zc[j][g] = kasym ? to_f<DT>(kzero[so + g]) : 0.f;
+              sc[j][g] = to_f<DT>(kscale[so + row_scale_idx(r, g, NG)]);
+              zc[j][g] = kasym ? to_f<DT>(kzero[so + row_scale_idx(r, g, NG)]) : 0.f;
             }
           }
         }
-        if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.bk_s, ctot, qsf, lane, lp);
-      else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.bk_s, ctot, qsf, lane, lp);
+        float2 sc2[2][NG], zc2[2][NG];
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int g = 0; g < NG; ++g) {
+            sc2[m][g] = make_float2(sc[2 * m][g], sc[2 * m + 1][g]);
+            zc2[m][g] = make_float2(zc[2 * m][g], zc[2 * m + 1][g]);
+          }
+        if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc2, zc2, sm.qp.bk, ctot, qsf, lane, lp);
+        else k_packed_logits<BK, NT, NG, false>(rw, sc2, zc2, sm.qp.bk, ctot, qsf, lane, lp);
       }
       if (kd_any) {
         const uint16_t* rp[4];
@@ -696,7 +650,7 @@ decode_attn_kernel(const DevArgs a) {
                                     r1 ? *reinterpret_cast<const uint32_t*>(r1 + c0 + 8) : 0u};
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              const uint2 bb = sm.bd_s[nt][kb][lane];
+              const uint2 bb = sm.qp.bd[nt][kb][lane];
               const uint32_t bf[2] = {bb.x, bb.y};
               float c[4] = {0.f, 0.f, 0.f, 0.f};
               mma_dt<DT>(c, af, bf);
@@ -710,7 +664,9 @@ decode_attn_kernel(const DevArgs a) {
         const bool head_ok = nt * 4 + tq < R;
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          x[nt][j] = (!head_ok || src[j] == 0) ? -INFINITY : (src[j] == 1 ? lp[nt][j] * cp : ld[nt][j] * cd);
+          x[nt][j] = (!head_ok || src[j] == 0)
+                         ? -INFINITY
+                         : (src[j] == 1 ? (j & 1 ? lp[nt][j >> 1].y : lp[nt][j >> 1].x) * cp : ld[nt][j] * cd);
       }
     }
 
@@ -734,7 +690,7 @@ decode_attn_kernel(const DevArgs a) {
       l_run[nt] = l_run[nt] * alpha + wt * ((pt[0] + pt[1]) + (pt[2] + pt[3]));
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) { o[nt][mt][0] *= alpha; o[nt][mt][1] *= alpha; }
+        for (int mt = 0; mt < 8; ++mt) o[nt][mt] = __fmul2_rn(o[nt][mt], f2(alpha));
       }
       const int head = nt * 4 + tq;
       if (vpacked) {
@@ -771,7 +727,7 @@ decode_attn_kernel(const DevArgs a) {
         zf[nt] = (float)psum[nt] * fv[nt];
       }
       VChunk<BV> vc;
-      float sv[16], zv[16];
+      float2 sv[8], zv[8];
       if (fast) {
         const int gofs = (((t0 - vs) >> vgs) - ((a.t_first + (tile - warp) * kTile - vs) >> vgs)) * 256;
         load_vchunk<BV>(vc, sg + o_vc + warp * TBV, lane);
@@ -838,8 +794,8 @@ decode_attn_kernel(const DevArgs a) {
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          o[nt][mt][0] += acc[nt][0] + acc[nt][1];
-          o[nt][mt][1] += acc[nt][2] + acc[nt][3];
+          o[nt][mt].x += acc[nt][0] + acc[nt][1];
+          o[nt][mt].y += acc[nt][2] + acc[nt][3];
         }
       }
     }
@@ -874,8 +830,8 @@ decode_attn_kernel(const DevArgs a) {
     if (gid == 0) { sm.cm_s[warp][head] = m_run[nt]; sm.cl_s[warp][head] = l; }
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
-      co_s[(warp * RP + head) * kD + mt * 16 + gid] = o[nt][mt][0];
-      co_s[(warp * RP + head) * kD + mt * 16 + 8 + gid] = o[nt][mt][1];
+      co_s[(warp * RP + head) * kD + mt * 16 + gid] = o[nt][mt].x;
+      co_s[(warp * RP + head) * kD + mt * 16 + 8 + gid] = o[nt][mt].y;
     }
   }
   __syncthreads();
@@ -898,6 +854,128 @@ decode_attn_kernel(const DevArgs a) {
     a.po[row * kD + d] = ov;
     if (d == 0) { a.pm[row] = M; a.pl[row] = lv; }
   }
+}
+
+// The query side of the attention pass for one (batch, KV head): grid (Hkv, B),
+// 128 threads.  q*f (f = the key normalisation factor, 1 without) is scaled by
+// 2^e_p so its largest entry just fits QBITS bits, rounded to an integer and
+// split into three balanced int8 digits laid out as the m16n8k32 B fragments
+// the packed-K MMA reads; q alone, scaled by 2^e_d, gives the dtype hi/lo B
+// fragments of the dense (sink / recent) rows.
+template <int DT, int RP, int NG>
+__global__ void __launch_bounds__(kWarps * 32) qprep_kernel(const DevArgs a) {
+  griddep_launch_dependents();  // the attention grid may start its KV copies now
+  constexpr int NT = RP / 4;
+  constexpr int KPG = 4 / NG;                                // 32-dim k-blocks per channel group
+  constexpr int QBITS = NG == 4 ? 22 : (NG == 2 ? 21 : 20);  // |q int| < 2^QBITS: a group sum fits int32
+  __shared__ float q_s[RP * kD];   // q*f
+  __shared__ float qd_s[RP * kD];  // q, then q*2^e_d
+  __shared__ int qi_s[RP * kD];    // integer q*f*2^e_p
+  __shared__ __align__(16) int8_t dg_s[3][RP * kD];  // balanced digits d0, d1, d2
+  __shared__ float red_s[2][kWarps];
+  const int hk = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = a.R;
+  QPrep<RP>& out = reinterpret_cast<QPrep<RP>*>(const_cast<void*>(a.qprep))[(int64_t)b * a.Hkv + hk];
+  float amax_p = 0.f, amax_d = 0.f;
+  for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
+    const int h = i / kD, d = i % kD;
+    float qv = 0.f, f = 1.f;
+    if (h < R) {
+      qv = to_f<DT>(a.q[b * a.q_b + (int64_t)(hk * R + h) * a.q_h + d]);
+      if (a.kf) f = to_f<DT>(a.kf[((int64_t)b * a.Hkv + hk) * kD + d]);
+    }
+    const float qp = qv * f;
+    q_s[i] = qp;
+    qd_s[i] = qv;
+    amax_p = fmaxf(amax_p, fabsf(qp));
+    amax_d = fmaxf(amax_d, fabsf(qv));
+  }
+  amax_p = warp_max(amax_p);
+  amax_d = warp_max(amax_d);
+  if (lane == 0) { red_s[0][warp] = amax_p; red_s[1][warp] = amax_d; }
+  __syncthreads();
+  amax_p = fmaxf(fmaxf(red_s[0][0], red_s[0][1]), fmaxf(red_s[0][2], red_s[0][3]));
+  amax_d = fmaxf(fmaxf(red_s[1][0], red_s[1][1]), fmaxf(red_s[1][2], red_s[1][3]));
+  int ex, e_p = 0, e_d = 0;
+  if (amax_p > 0.f) { frexpf(amax_p, &ex); e_p = QBITS - ex; }
+  if (amax_d > 0.f) { frexpf(amax_d, &ex); e_d = 15 - ex; }
+  for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
+    const int qi = __float2int_rn(ldexpf(q_s[i], e_p));
+    qi_s[i] = qi;
+    qd_s[i] = ldexpf(qd_s[i], e_d);
+    int d0, d1, d2;
+    digits3(qi, d0, d1, d2);
+    dg_s[0][i] = (int8_t)d0;
+    dg_s[1][i] = (int8_t)d1;
+    dg_s[2][i] = (int8_t)d2;
+  }
+  if (threadIdx.x == 0) { out.e_p = e_p; out.e_d = e_d; out.pad0 = out.pad1 = 0; }
+  __syncthreads();
+  // per (head, channel group) sums of the integer query: one warp per head
+  for (int h = warp; h < RP; h += kWarps) {
+    int s[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s[c] = qi_s[h * kD + c * 32 + lane];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s[c] += __shfl_xor_sync(0xffffffffu, s[c], o);
+    if (lane < 4) {
+      int t = 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) t += (c / KPG == lane) ? s[c] : 0;
+      out.qsum[h][lane] = t;
+    }
+  }
+  // packed-K B fragments (m16n8k32): n-tile 2*quad holds digits (d2, d1) and
+  // 2*quad+1 holds (d0, 0) of each of the quad's 4 heads; each fragment word
+  // is one 32-bit read of 4 consecutive digit bytes
+  for (int i = threadIdx.x; i < 2 * NT * 4 * 32; i += kWarps * 32) {
+    const int ntk = i / 128, kb = (i / 32) % 4, ln = i % 32;
+    const int g2 = ln >> 2, t2 = ln & 3;
+    const int head = (ntk >> 1) * 4 + (g2 >> 1), which = g2 & 1;
+    const int plane = (ntk & 1) ? (which ? -1 : 0) : (which ? 1 : 2);
+    uint32_t wrd[2] = {0u, 0u};
+    if (plane >= 0) {
+      const int8_t* src = &dg_s[plane][head * kD + kb * 32 + 4 * t2];
+      wrd[0] = *reinterpret_cast<const uint32_t*>(src);
+      wrd[1] = *reinterpret_cast<const uint32_t*>(src + 16);
+    }
+    out.bk[ntk][kb][ln] = make_uint2(wrd[0], wrd[1]);
+  }
+  // dense-K B fragments (m16n8k16, dtype hi/lo of q * 2^e_d)
+  for (int i = threadIdx.x; i < NT * 8 * 32; i += kWarps * 32) {
+    const int nt = i / 256, kb = (i / 32) % 8, ln = i % 32;
+    const int g2 = ln >> 2, t2 = ln & 3;
+    const int head = nt * 4 + (g2 >> 1), part = g2 & 1;
+    const int dd[4] = {kb * 16 + 2 * t2, kb * 16 + 2 * t2 + 1, kb * 16 + 2 * t2 + 8, kb * 16 + 2 * t2 + 9};
+    uint16_t v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      uint16_t hi, lo;
+      split_hilo<DT>(qd_s[head * kD + dd[u]], hi, lo);
+      v[u] = part ? lo : hi;
+    }
+    out.bd[nt][kb][ln] = make_uint2(pack2(v[0], v[1]), pack2(v[2], v[3]));
+  }
+}
+
+// Launch of the attention grid as a programmatic dependent of the prep grid
+// launched just before it on the same stream.
+template <typename K>
+inline cudaError_t launch_after_prep(K kern, dim3 grid, int smem, cudaStream_t s, const DevArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kWarps * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace innerq

@@ -19,8 +19,7 @@ cudaError_t go(const DevArgs& a, dim3 grid, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     set_bytes[dev] = smem;
   }
-  kern<<<grid, kWarps * 32, smem, s>>>(a);
-  return cudaGetLastError();
+  return launch_after_prep(kern, grid, smem, s, a);
 }
 
 template <int BV, int RP>

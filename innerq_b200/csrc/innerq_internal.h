@@ -40,4 +40,7 @@ INNERQ_DECL_ATTN(launch_attn_k3_bf16)
 INNERQ_DECL_ATTN(launch_attn_k4_f16)
 INNERQ_DECL_ATTN(launch_attn_k4_bf16)
 #undef INNERQ_DECL_ATTN
+// the query-prep pass that precedes every attention launch (qprep.cu)
+cudaError_t launch_qprep(const DevArgs& a, int rp, int ng, int bf16, cudaStream_t s);
+int64_t qprep_bytes(int rp);  // one (batch, KV head) block
 }  // namespace innerq
