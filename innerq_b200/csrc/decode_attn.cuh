@@ -321,7 +321,7 @@ __device__ __forceinline__ void digits3(int v, int& d0, int& d1, int& d2) {
 template <int BK, int NT, int NG, bool KASYM>
 __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const float2 sc[2][NG],
                                                 const float2 zc[2][NG], const uint2 (*bks)[4][32],
-                                                const int ctot[NT][NG], const float qsf[NT][NG],
+                                                const float ctf[NT][NG], const float qsf[NT][NG],
                                                 int lane, float2 lp[NT][2]) {
   constexpr int KPG = 4 / NG;
 #pragma unroll
@@ -339,7 +339,7 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
                                 row_frag<BK>(rw[2 * mt].w, kb, 1), row_frag<BK>(rw[2 * mt + 1].w, kb, 1)};
         if (first) {
           imma_u8s8(acc[mt][0], af, bf0, 0, 0, 0, 0);
-          imma_u8s8(acc[mt][1], af, bf1, -ctot[nt][g], 0, -ctot[nt][g], 0);
+          imma_u8s8(acc[mt][1], af, bf1, 0, 0, 0, 0);
         } else {
           imma_u8s8(acc[mt][0], af, bf0, acc[mt][0][0], acc[mt][0][1], acc[mt][0][2], acc[mt][0][3]);
           imma_u8s8(acc[mt][1], af, bf1, acc[mt][1][0], acc[mt][1][1], acc[mt][1][2], acc[mt][1][3]);
@@ -351,12 +351,15 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
           float tf[2];
 #pragma unroll
           for (int rr = 0; rr < 2; ++rr) {
-            // the exact sum fits int32; intermediate terms wrap modulo 2^32
+            // sum_d u q (|.| < 2^31); intermediate terms wrap modulo 2^32
             const uint32_t t = (uint32_t)acc[mt][0][2 * rr] * 65536u +
                                (uint32_t)acc[mt][0][2 * rr + 1] * 256u + (uint32_t)acc[mt][1][2 * rr];
             tf[rr] = (float)(int)t;
           }
-          lp[nt][mt] = __ffma2_rn(sc[mt][g], make_float2(tf[0], tf[1]), lp[nt][mt]);
+          // offset-binary correction off * sum_d q in fp32 (an MMA accumulator
+          // input would cost register moves on every MMA)
+          const float2 tc = __fadd2_rn(make_float2(tf[0], tf[1]), f2(-ctf[nt][g]));
+          lp[nt][mt] = __ffma2_rn(sc[mt][g], tc, lp[nt][mt]);
           if constexpr (KASYM) lp[nt][mt] = __ffma2_rn(zc[mt][g], f2(qsf[nt][g]), lp[nt][mt]);
         }
       }
@@ -369,7 +372,7 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
 template <int BV, int NT, bool VASYM>
 __device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const float2 sv[8],
                                                     const float2 zv[8], const uint32_t pb[NT][2],
-                                                    const int offp[NT], const float fv[NT],
+                                                    const float offp[NT], const float fv[NT],
                                                     const float zf[NT], float2 o[NT][8]) {
   float2 svf[NT][8];
 #pragma unroll
@@ -383,9 +386,10 @@ __device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const 
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       int acc[4];
-      imma_u8u8(acc, af, pb[nt], 0, -offp[nt], 0, -offp[nt]);
+      imma_u8u8(acc, af, pb[nt], 0, 0, 0, 0);
       const float t0 = (float)(acc[0] * 256 + acc[1]), t1 = (float)(acc[2] * 256 + acc[3]);
-      o[nt][mt] = __ffma2_rn(svf[nt][mt], make_float2(t0, t1), o[nt][mt]);
+      const float2 tc = __fadd2_rn(make_float2(t0, t1), f2(-offp[nt]));  // off * sum_t p
+      o[nt][mt] = __ffma2_rn(svf[nt][mt], tc, o[nt][mt]);
       if constexpr (VASYM) o[nt][mt] = __ffma2_rn(zv[mt], f2(zf[nt]), o[nt][mt]);
     }
   }
@@ -531,14 +535,14 @@ decode_attn_kernel(const DevArgs a) {
   __syncthreads();  // barrier initialisation is visible to every thread
   bool failed = !mbar_wait_bounded(&sm.prep_bar, 0, kWaitLimit);
   int i_done = 0;
-  int ctot[NT][NG];
+  float ctf[NT][NG];  // K offset correction per channel group: off * sum q
   float qsf[NT][NG];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
       const int qs = sm.qp.qsum[nt * 4 + tq][g];
-      ctot[nt][g] = koff * qs;
+      ctf[nt][g] = (float)(koff * qs);
       qsf[nt][g] = (float)qs;
     }
   const float cp = ldexpf(a.scale_log2, -sm.qp.e_p);
@@ -571,8 +575,8 @@ decode_attn_kernel(const DevArgs a) {
       float2 lp[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) lp[nt][0] = lp[nt][1] = make_float2(0.f, 0.f);
-      if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.qp.bk, ctot, qsf, lane, lp);
-      else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.qp.bk, ctot, qsf, lane, lp);
+      if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.qp.bk, ctf, qsf, lane, lp);
+      else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.qp.bk, ctf, qsf, lane, lp);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const bool head_ok = nt * 4 + tq < R;
@@ -630,8 +634,8 @@ decode_attn_kernel(const DevArgs a) {
             sc2[m][g] = make_float2(sc[2 * m][g], sc[2 * m + 1][g]);
             zc2[m][g] = make_float2(zc[2 * m][g], zc[2 * m + 1][g]);
           }
-        if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc2, zc2, sm.qp.bk, ctot, qsf, lane, lp);
-        else k_packed_logits<BK, NT, NG, false>(rw, sc2, zc2, sm.qp.bk, ctot, qsf, lane, lp);
+        if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc2, zc2, sm.qp.bk, ctf, qsf, lane, lp);
+        else k_packed_logits<BK, NT, NG, false>(rw, sc2, zc2, sm.qp.bk, ctf, qsf, lane, lp);
       }
       if (kd_any) {
         const uint16_t* rp[4];
@@ -716,14 +720,14 @@ decode_attn_kernel(const DevArgs a) {
     // ------------------------------------------------------------------ PV
     if (vpacked) {
       uint32_t pb[NT][2];
-      int offp[NT];
+      float offp[NT];
       float zf[NT];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int head = nt * 4 + (gid >> 1), digit = gid & 1;
         pb[nt][0] = *reinterpret_cast<const uint32_t*>(&sm.pd_s[warp][head][digit][4 * tq]);
         pb[nt][1] = *reinterpret_cast<const uint32_t*>(&sm.pd_s[warp][head][digit][16 + 4 * tq]);
-        offp[nt] = voff * psum[nt];
+        offp[nt] = (float)(voff * psum[nt]);
         zf[nt] = (float)psum[nt] * fv[nt];
       }
       VChunk<BV> vc;
