@@ -359,7 +359,8 @@ __global__ void lse_merge_kernel(const float* __restrict__ po, const float* __re
   float num = 0.f, den = 0.f;
   if (M != -INFINITY) {
     for (int s = 0; s < n_splits; ++s) {
-      const float w = m[s] == -INFINITY ? 0.f : exp2f(m[s] - M);
+      if (m[s] == -INFINITY) continue;  // an empty split contributes nothing
+      const float w = exp2f(m[s] - M);
       num += w * po[((int64_t)row * n_splits + s) * kD + d];
       den += w * l[s];
     }
