@@ -5,7 +5,7 @@
 // layouts hand each lane of the consuming warp exactly the bytes of its
 // m16n8k32 integer-MMA A fragments (a0: row gid, k 4tq..4tq+3; a1: row gid+8;
 // a2: row gid, k 16+4tq..; a3: row gid+8, k 16+4tq..), so a 4-bit word
-// expands to two fragment registers with one shift and two LOP3s.
+// expands to two fragment registers with at most one shift and two LOP3s.
 //
 // "row" layout (K, channel groups; A = K[token][dim]):
 //   Lane L = 4*gid + tq owns tokens r = gid + 8*j (j = 0..3) at dims
@@ -21,9 +21,14 @@
 // "col" layout (V, token groups; A = V^T[dim][token]):
 //   Lane L = 4*gid + tq owns dims d = mt*16 + h*8 + gid (mt = 0..7, h = 0..1)
 //   at tokens r = half*16 + 4*tq + i.
-//     b=4: 16 words; word mt*2 + h, nibble 2i + half
-//     b=2:  8 words; word mt, crumb 4i + h*2 + half
-//     b=3: plane L as b=2; plane H 4 words: word mt>>1, bit 8i + (mt&1)*4 + h*2 + half
+//     b=4: 16 words; word (mt&3)*4 + h*2 + half, bits 8i + 4*(mt>>2): m-tiles
+//          0-3 sit in the low nibbles and 4-7 in the high nibbles of the same
+//          bytes, so each fragment register is one AND (the high-nibble ones
+//          hold 16*u, undone in the fp32 scale)
+//     b=2:  8 words; word (mt&1)*4 + h*2 + half, bits 8i + 2*(mt>>1): crumb
+//          position p = mt>>1 gives 4^p * u
+//     b=3: plane L 8 words: word mt, crumb 4i + h*2 + half; plane H 4 words:
+//          word mt>>1, bit 8i + (mt&1)*4 + h*2 + half
 //   Scales / zero points (one per (group, dim)): [gid 8][mt 8][h 2].
 //
 // b=1 (the asymmetric half of hybrid mode) is a single plane laid out like
@@ -143,15 +148,21 @@ __device__ __forceinline__ uint32_t row_frag(const uint32_t* w, int kb, int half
   }
 }
 // Col layout (V): the lane's chunk words (b=3: 8 L words then 4 H words).
+// The register holds col_scale<BITS>(mt) * code per byte.
 template <int BITS>
 __device__ __forceinline__ uint32_t col_frag(const uint32_t* w, int mt, int h, int half) {
   if constexpr (BITS == 4) {
-    return (w[mt * 2 + h] >> (4 * half)) & 0x0F0F0F0Fu;
+    return w[(mt & 3) * 4 + h * 2 + half] & (mt < 4 ? 0x0F0F0F0Fu : 0xF0F0F0F0u);
+  } else if constexpr (BITS == 2) {
+    return w[(mt & 1) * 4 + h * 2 + half] & (0x03030303u << (2 * (mt >> 1)));
   } else {
     const uint32_t l = (w[mt] >> (2 * (h * 2 + half))) & 0x03030303u;
-    if constexpr (BITS == 2) return l;
     return l | (((w[8 + (mt >> 1)] >> ((mt & 1) * 4 + h * 2 + half)) & 0x01010101u) << 2);
   }
+}
+template <int BITS>
+__host__ __device__ constexpr int col_scale(int mt) {
+  return BITS == 4 ? (mt < 4 ? 1 : 16) : (BITS == 2 ? 1 << (2 * (mt >> 1)) : 1);
 }
 
 // --------------------------------------------------- layout index helpers ---
@@ -190,15 +201,16 @@ __host__ __device__ inline BitPos col_pos(int bits, int r, int d) {
     p.off = lane * 16 + (mt >> 1) * 4;
     p.shift = 8 * i + (mt & 1) * 4 + h * 2 + half;
   } else if (bits == 4) {
-    p.off = lane * 64 + (mt * 2 + h) * 4;
-    p.shift = 4 * (2 * i + half);
+    p.off = lane * 64 + ((mt & 3) * 4 + h * 2 + half) * 4;
+    p.shift = 8 * i + 4 * (mt >> 2);
+  } else if (bits == 2) {
+    p.off = lane * 32 + ((mt & 1) * 4 + h * 2 + half) * 4;
+    p.shift = 8 * i + 2 * (mt >> 1);
   } else {
     p.off = lane * 32 + mt * 4;
     p.shift = 2 * (4 * i + h * 2 + half);
-    if (bits == 3) {
-      p.hoff = 1024 + lane * 16 + (mt >> 1) * 4;
-      p.hshift = 8 * i + (mt & 1) * 4 + h * 2 + half;
-    }
+    p.hoff = 1024 + lane * 16 + (mt >> 1) * 4;
+    p.hshift = 8 * i + (mt & 1) * 4 + h * 2 + half;
   }
   return p;
 }

@@ -374,11 +374,12 @@ __device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const 
                                                     const float2 zv[8], const uint32_t pb[NT][2],
                                                     const float offp[NT], const float fv[NT],
                                                     const float zf[NT], float2 o[NT][8]) {
+  // m-tile mt's sums carry col_scale(mt) (a power of two): exact to undo here
   float2 svf[NT][8];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int u = 0; u < 8; ++u) svf[nt][u] = __fmul2_rn(sv[u], f2(fv[nt]));
+    for (int u = 0; u < 8; ++u) svf[nt][u] = __fmul2_rn(sv[u], f2(fv[nt] * (1.f / col_scale<BV>(u))));
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
     const uint32_t af[4] = {col_frag<BV>(vc.w, mt, 0, 0), col_frag<BV>(vc.w, mt, 1, 0),
@@ -388,7 +389,7 @@ __device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const 
       int acc[4];
       imma_u8u8(acc, af, pb[nt], 0, 0, 0, 0);
       const float t0 = (float)(acc[0] * 256 + acc[1]), t1 = (float)(acc[2] * 256 + acc[3]);
-      const float2 tc = __fadd2_rn(make_float2(t0, t1), f2(-offp[nt]));  // off * sum_t p
+      const float2 tc = __fadd2_rn(make_float2(t0, t1), f2(-offp[nt] * col_scale<BV>(mt)));  // off * sum_t p
       o[nt][mt] = __ffma2_rn(svf[nt][mt], tc, o[nt][mt]);
       if constexpr (VASYM) o[nt][mt] = __ffma2_rn(zv[mt], f2(zf[nt]), o[nt][mt]);
     }
