@@ -1,7 +1,12 @@
 // Shared device helpers for the InnerQ B200 kernels: dtype rounding, the packed
 // tile layouts, code extraction into integer-MMA fragments, mma.sync wrappers.
 //
-// Packed layouts (D = 128, tiles of 32 tokens, b = bits per code).  Both
+// Packed layouts (D = 128, tiles of 32 tokens, b = bits per code).  A lane's
+// words are grouped in 16-byte pieces stored piece-major: piece k of lane L
+// sits at byte k*512 + L*16 of its plane, so each 128-bit load of one piece
+// by a whole warp reads 512 contiguous bytes (no shared-memory bank
+// conflicts after the tile is bulk-copied).  Below, "word w of lane L" is
+// word w%4 of piece w/4.  Both
 // layouts hand each lane of the consuming warp exactly the bytes of its
 // m16n8k32 integer-MMA A fragments (a0: row gid, k 4tq..4tq+3; a1: row gid+8;
 // a2: row gid, k 16+4tq..; a3: row gid+8, k 16+4tq..), so a 4-bit word
@@ -179,10 +184,10 @@ __host__ __device__ inline BitPos row_pos(int bits, int r, int d) {
     p.off = lane * 16 + j * 4;
     p.shift = 8 * i + kb * 2 + half;
   } else if (bits == 4) {
-    p.off = lane * 64 + j * 16 + kb * 4;
+    p.off = j * 512 + lane * 16 + kb * 4;
     p.shift = 4 * (2 * i + half);
   } else {
-    p.off = lane * 32 + j * 8 + (kb >> 1) * 4;
+    p.off = (j >> 1) * 512 + lane * 16 + (j & 1) * 8 + (kb >> 1) * 4;
     p.shift = 2 * (4 * i + (kb & 1) * 2 + half);
     if (bits == 3) {
       p.hoff = 1024 + lane * 16 + j * 4;
@@ -201,13 +206,13 @@ __host__ __device__ inline BitPos col_pos(int bits, int r, int d) {
     p.off = lane * 16 + (mt >> 1) * 4;
     p.shift = 8 * i + (mt & 1) * 4 + h * 2 + half;
   } else if (bits == 4) {
-    p.off = lane * 64 + ((mt & 3) * 4 + h * 2 + half) * 4;
+    p.off = (mt & 3) * 512 + lane * 16 + (h * 2 + half) * 4;
     p.shift = 8 * i + 4 * (mt >> 2);
   } else if (bits == 2) {
-    p.off = lane * 32 + ((mt & 1) * 4 + h * 2 + half) * 4;
+    p.off = (mt & 1) * 512 + lane * 16 + (h * 2 + half) * 4;
     p.shift = 8 * i + 2 * (mt >> 1);
   } else {
-    p.off = lane * 32 + mt * 4;
+    p.off = (mt >> 2) * 512 + lane * 16 + (mt & 3) * 4;
     p.shift = 2 * (4 * i + h * 2 + half);
     p.hoff = 1024 + lane * 16 + (mt >> 1) * 4;
     p.hshift = 8 * i + (mt & 1) * 4 + h * 2 + half;

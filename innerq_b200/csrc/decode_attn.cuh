@@ -175,17 +175,17 @@ template <int BITS> struct KRow { uint32_t w[BITS == 4 ? 4 : 3]; };
 
 template <int BITS>
 __device__ __forceinline__ void load_krows(KRow<BITS> rw[4], const uint8_t* tb, int lane) {
-  // the lane's four rows of one fully packed tile (shared or global memory)
+  // the lane's four rows of one fully packed tile (shared or global memory);
+  // piece k of the lane at k*512 + lane*16
   if constexpr (BITS == 4) {
-    const uint4* p = reinterpret_cast<const uint4*>(tb + lane * 64);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint4 v = p[j];
+      const uint4 v = *reinterpret_cast<const uint4*>(tb + j * 512 + lane * 16);
       rw[j].w[0] = v.x; rw[j].w[1] = v.y; rw[j].w[2] = v.z; rw[j].w[3] = v.w;
     }
   } else {
-    const uint4* p = reinterpret_cast<const uint4*>(tb + lane * 32);
-    const uint4 v0 = p[0], v1 = p[1];
+    const uint4 v0 = *reinterpret_cast<const uint4*>(tb + lane * 16);
+    const uint4 v1 = *reinterpret_cast<const uint4*>(tb + 512 + lane * 16);
     rw[0].w[0] = v0.x; rw[0].w[1] = v0.y; rw[1].w[0] = v0.z; rw[1].w[1] = v0.w;
     rw[2].w[0] = v1.x; rw[2].w[1] = v1.y; rw[3].w[0] = v1.z; rw[3].w[1] = v1.w;
     if constexpr (BITS == 3) {
@@ -202,10 +202,10 @@ template <int BITS>
 __device__ __forceinline__ void load_krow(KRow<BITS>& r, const uint8_t* tb, int lane2, int j) {
   // one row of a tile, for tiles whose rows come from different places
   if constexpr (BITS == 4) {
-    const uint4 v = *reinterpret_cast<const uint4*>(tb + lane2 * 64 + j * 16);
+    const uint4 v = *reinterpret_cast<const uint4*>(tb + j * 512 + lane2 * 16);
     r.w[0] = v.x; r.w[1] = v.y; r.w[2] = v.z; r.w[3] = v.w;
   } else {
-    const uint2 v = *reinterpret_cast<const uint2*>(tb + lane2 * 32 + j * 8);
+    const uint2 v = *reinterpret_cast<const uint2*>(tb + (j >> 1) * 512 + lane2 * 16 + (j & 1) * 8);
     r.w[0] = v.x; r.w[1] = v.y;
     r.w[2] = BITS == 3 ? *reinterpret_cast<const uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) : 0u;
   }
@@ -216,17 +216,15 @@ template <int BITS> struct VChunk { uint32_t w[BITS == 4 ? 16 : (BITS == 2 ? 8 :
 template <int BITS>
 __device__ __forceinline__ void load_vchunk(VChunk<BITS>& c, const uint8_t* tb, int lane) {
   if constexpr (BITS == 4) {
-    const uint4* p = reinterpret_cast<const uint4*>(tb + lane * 64);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint4 v = p[i];
+      const uint4 v = *reinterpret_cast<const uint4*>(tb + i * 512 + lane * 16);
       c.w[4 * i] = v.x; c.w[4 * i + 1] = v.y; c.w[4 * i + 2] = v.z; c.w[4 * i + 3] = v.w;
     }
   } else {
-    const uint4* p = reinterpret_cast<const uint4*>(tb + lane * 32);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const uint4 v = p[i];
+      const uint4 v = *reinterpret_cast<const uint4*>(tb + i * 512 + lane * 16);
       c.w[4 * i] = v.x; c.w[4 * i + 1] = v.y; c.w[4 * i + 2] = v.z; c.w[4 * i + 3] = v.w;
     }
     if constexpr (BITS == 3) {

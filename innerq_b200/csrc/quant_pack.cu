@@ -138,10 +138,10 @@ __device__ __forceinline__ void pack_row_token(const uint2 raw, int t, int64_t b
     if (BITS == 1) {
       *reinterpret_cast<uint32_t*>(tb + lane2 * 16 + j * 4) = seg[tq];
     } else if (BITS == 4) {
-      *reinterpret_cast<uint4*>(tb + lane2 * 64 + j * 16) =
+      *reinterpret_cast<uint4*>(tb + j * 512 + lane2 * 16) =
           make_uint4(seg[tq * 4], seg[tq * 4 + 1], seg[tq * 4 + 2], seg[tq * 4 + 3]);
     } else {
-      *reinterpret_cast<uint2*>(tb + lane2 * 32 + j * 8) =
+      *reinterpret_cast<uint2*>(tb + (j >> 1) * 512 + lane2 * 16 + (j & 1) * 8) =
           make_uint2(seg[tq * kWordsPerSeg], seg[tq * kWordsPerSeg + 1]);
       if (BITS == 3) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = seg[tq * 3 + 2];
     }
