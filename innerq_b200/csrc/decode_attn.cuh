@@ -278,12 +278,16 @@ __device__ __forceinline__ bool is_fast_tile(const DevArgs& a, int tile) {
 template <int RP>
 struct QPrep {
   static constexpr int NT = RP / 4;
-  uint2 bk[2 * NT][4][32];  // packed-K B fragments (three int8 digits of q*f*2^e_p)
+  // packed-K B fragments (three int8 digits of q*f*2^e_p): n-tile nt < NT holds
+  // (d2, d1) of heads 4nt..4nt+3; n-tile NT holds d0 (GQA <= 4: (d0, 0) per
+  // head; GQA 8: (d0 of head q, d0 of head q+4), so 8 heads need 3 n-tiles)
+  static constexpr int kBTiles = NT + 1;
+  uint2 bk[kBTiles][4][32];
   int qsum[RP][4];          // sum of the integer query over each K channel group
   int e_p, e_d, pad0, pad1; // exponents of the packed / dense query scalings
   uint2 bd[NT][8][32];      // dense-K B fragments (dtype hi/lo of q*2^e_d)
   // bytes every CTA copies; the dense fragments follow only where needed
-  static constexpr uint32_t kHead = sizeof(uint2) * 2 * NT * 4 * 32 + sizeof(int) * (RP * 4 + 4);
+  static constexpr uint32_t kHead = sizeof(uint2) * kBTiles * 4 * 32 + sizeof(int) * (RP * 4 + 4);
   static constexpr uint32_t kDense = sizeof(uint2) * NT * 8 * 32;
 };
 static_assert(QPrep<4>::kHead % 16 == 0 && QPrep<8>::kHead % 16 == 0, "bulk copy granularity");
@@ -322,6 +326,49 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
                                                 const float ctf[NT][NG], const float qsf[NT][NG],
                                                 int lane, float2 lp[NT][2]) {
   constexpr int KPG = 4 / NG;
+  if constexpr (NT == 2) {
+    // 8 heads: two (d2, d1) n-tiles and one shared d0 n-tile (head q / q+4)
+    int accP[2][2][4], accD[2][4];  // [nt][mt][c], [mt][c]
+#pragma unroll
+    for (int kb = 0; kb < 4; ++kb) {
+      const int g = kb / KPG;
+      const bool first = kb % KPG == 0;
+      const uint2 p0 = bks[0][kb][lane], p1 = bks[1][kb][lane], pd = bks[2][kb][lane];
+      const uint32_t bp0[2] = {p0.x, p0.y}, bp1[2] = {p1.x, p1.y}, bd[2] = {pd.x, pd.y};
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const uint32_t af[4] = {row_frag<BK>(rw[2 * mt].w, kb, 0), row_frag<BK>(rw[2 * mt + 1].w, kb, 0),
+                                row_frag<BK>(rw[2 * mt].w, kb, 1), row_frag<BK>(rw[2 * mt + 1].w, kb, 1)};
+        if (first) {
+          imma_u8s8(accP[0][mt], af, bp0, 0, 0, 0, 0);
+          imma_u8s8(accP[1][mt], af, bp1, 0, 0, 0, 0);
+          imma_u8s8(accD[mt], af, bd, 0, 0, 0, 0);
+        } else {
+          imma_u8s8(accP[0][mt], af, bp0, accP[0][mt][0], accP[0][mt][1], accP[0][mt][2], accP[0][mt][3]);
+          imma_u8s8(accP[1][mt], af, bp1, accP[1][mt][0], accP[1][mt][1], accP[1][mt][2], accP[1][mt][3]);
+          imma_u8s8(accD[mt], af, bd, accD[mt][0], accD[mt][1], accD[mt][2], accD[mt][3]);
+        }
+      }
+      if (kb % KPG == KPG - 1) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            float tf[2];
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+              const uint32_t t = (uint32_t)accP[nt][mt][2 * rr] * 65536u +
+                                 (uint32_t)accP[nt][mt][2 * rr + 1] * 256u + (uint32_t)accD[mt][2 * rr + nt];
+              tf[rr] = (float)(int)t;
+            }
+            const float2 tc = __fadd2_rn(make_float2(tf[0], tf[1]), f2(-ctf[nt][g]));
+            lp[nt][mt] = __ffma2_rn(sc[mt][g], tc, lp[nt][mt]);
+            if constexpr (KASYM) lp[nt][mt] = __ffma2_rn(zc[mt][g], f2(qsf[nt][g]), lp[nt][mt]);
+          }
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     int acc[2][2][4];  // [mt][digit n-tile: (d2,d1) / (d0,-)][c]
@@ -329,7 +376,7 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
     for (int kb = 0; kb < 4; ++kb) {
       const int g = kb / KPG;
       const bool first = kb % KPG == 0;
-      const uint2 b0 = bks[2 * nt][kb][lane], b1 = bks[2 * nt + 1][kb][lane];
+      const uint2 b0 = bks[nt][kb][lane], b1 = bks[NT][kb][lane];
       const uint32_t bf0[2] = {b0.x, b0.y}, bf1[2] = {b1.x, b1.y};
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
@@ -931,14 +978,25 @@ __global__ void __launch_bounds__(kWarps * 32) qprep_kernel(const DevArgs a) {
       out.qsum[h][lane] = t;
     }
   }
-  // packed-K B fragments (m16n8k32): n-tile 2*quad holds digits (d2, d1) and
-  // 2*quad+1 holds (d0, 0) of each of the quad's 4 heads; each fragment word
-  // is one 32-bit read of 4 consecutive digit bytes
-  for (int i = threadIdx.x; i < 2 * NT * 4 * 32; i += kWarps * 32) {
+  // packed-K B fragments (m16n8k32), column n = g2 of an n-tile: n-tile
+  // ntk < NT holds (d2, d1) of head 4*ntk + n/2; n-tile NT holds d0 of head
+  // n/2 (n even; n odd empty) for up to 4 heads, or of head n/2 + 4*(n&1) for
+  // 8.  Each fragment word is one 32-bit read of 4 consecutive digit bytes.
+  for (int i = threadIdx.x; i < QPrep<RP>::kBTiles * 4 * 32; i += kWarps * 32) {
     const int ntk = i / 128, kb = (i / 32) % 4, ln = i % 32;
     const int g2 = ln >> 2, t2 = ln & 3;
-    const int head = (ntk >> 1) * 4 + (g2 >> 1), which = g2 & 1;
-    const int plane = (ntk & 1) ? (which ? -1 : 0) : (which ? 1 : 2);
+    const int which = g2 & 1;
+    int head, plane;
+    if (ntk < NT) {
+      head = ntk * 4 + (g2 >> 1);
+      plane = which ? 1 : 2;
+    } else if (NT == 1) {
+      head = g2 >> 1;
+      plane = which ? -1 : 0;
+    } else {
+      head = (g2 >> 1) + 4 * which;
+      plane = 0;
+    }
     uint32_t wrd[2] = {0u, 0u};
     if (plane >= 0) {
       const int8_t* src = &dg_s[plane][head * kD + kb * 32 + 4 * t2];
