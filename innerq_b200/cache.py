@@ -168,11 +168,19 @@ class InnerqDynamicLayer(CacheLayerMixin):
             self.lazy_initialization(key_states, value_states)
             return key_states, value_states
         self.add_to_cache(key_states, value_states)
-        if self.fused and key_states.shape[-2] == 1 and self._k.fusable and self._v.fusable:
+        if self.fused and key_states.shape[-2] == 1 and self._fusable():
             # the "innerq" attention function reads the packed store
             key_states._innerq_layer = self
             return key_states, value_states
         return self.get_deq_tensors()
+
+    def _fusable(self) -> bool:
+        """Both stores are in layouts the fused kernel reads: channel-grouped
+        values need the keys' group size."""
+        k, v = self._k, self._v
+        if not (k.fusable and v.fusable):
+            return False
+        return not (v.quantize and not v.over_token and k.quantize and v.group != k.group)
 
     def attend(self, query: torch.Tensor, scaling: float | None = None,
                out: torch.Tensor | None = None, reuse: bool = False) -> torch.Tensor:

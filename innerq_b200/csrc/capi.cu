@@ -68,14 +68,14 @@ int check_side(const innerq_side& s, int dtype, int role, const char* name) {
     // the fused kernel reads the InnerQ layouts (cache.py:87-88 defaults)
     if (role == INNERQ_ROLE_K && s.over_token)
       return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens (use innerq_dequant)");
-    if (role == INNERQ_ROLE_V && !s.over_token)
-      return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: values grouped over channels (use innerq_dequant)");
     if (!s.codes || !s.scale || (s.mode == INNERQ_ASYM && !s.zero))
       return fail(INNERQ_ERR_ARG, "%s: missing store pointer", name);
     if (!aligned(s.codes, 16) || !aligned(s.scale, 16) || (s.zero && !aligned(s.zero, 16)))
       return fail(INNERQ_ERR_ARG, "%s: store pointers must be 16-byte aligned", name);
     if ((int64_t)s.n_q > s.cap_tiles * 32) return fail(INNERQ_ERR_ARG, "%s: n_q beyond capacity", name);
-    if (role == INNERQ_ROLE_V && s.n_q % 32) return fail(INNERQ_ERR_ARG, "%s: n_q %% 32", name);
+    // token-grouped values come in whole groups; channel-grouped ones may end
+    // inside a tile (whose unwritten code slots are zero)
+    if (role == INNERQ_ROLE_V && s.over_token && s.n_q % 32) return fail(INNERQ_ERR_ARG, "%s: n_q %% 32", name);
   }
   if (s.n_sink > 0 && (!s.sink || !aligned(s.sink, 4) || (s.sink_st % 2) || (s.sink_sh % 2) || (s.sink_sb % 2)))
     return fail(INNERQ_ERR_ARG, "%s: sink pointer / strides must be 4-byte aligned", name);
@@ -99,6 +99,11 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   if (rc) return rc;
   rc = check_side(a->v, a->dtype, INNERQ_ROLE_V, "v");
   if (rc) return rc;
+  // values grouped over channels share the keys' channel-group count
+  if (a->v.n_q > 0 && !a->v.over_token && a->k.n_q > 0 && a->v.group != a->k.group)
+    return fail(INNERQ_ERR_UNSUPPORTED,
+                "fused attention: channel-grouped values need the keys' group size (%d vs %d; use innerq_dequant)",
+                a->v.group, a->k.group);
   const int64_t Sk = (int64_t)a->k.n_sink + a->k.n_q + a->k.n_recent;
   const int64_t Sv = (int64_t)a->v.n_sink + a->v.n_q + a->v.n_recent;
   if (Sk != Sv) return fail(INNERQ_ERR_ARG, "K holds %lld tokens, V holds %lld", (long long)Sk, (long long)Sv);
@@ -149,6 +154,7 @@ DevSide dev_side(const innerq_side& s) {
   d.n_sink = s.n_sink; d.n_q = s.n_q; d.n_rec = s.n_recent;
   d.group = s.n_q > 0 ? s.group : 32;
   d.asym = s.n_q > 0 && s.mode == INNERQ_ASYM;
+  d.chan = 0;
   return d;
 }
 
@@ -168,6 +174,7 @@ int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm,
   DevArgs d;
   d.k = dev_side(a->k);
   d.v = dev_side(a->v);
+  d.v.chan = a->v.n_q > 0 && !a->v.over_token;
   d.q = (const uint16_t*)a->q;
   d.q_b = a->q_sb;
   d.q_h = a->q_sh;
@@ -182,7 +189,7 @@ int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm,
   d.R = p.R;
   dim3 grid(p.n_splits, a->Hkv, a->B);
   const int rp = p.R <= 4 ? 4 : 8;
-  const int ng = a->k.n_q > 0 ? kD / a->k.group : 4;
+  const int ng = a->k.n_q > 0 ? kD / a->k.group : (d.v.chan ? kD / a->v.group : 4);
   const bool bf = a->dtype == INNERQ_DT_BF16;
   cudaError_t e = launch_qprep(d, rp, ng, bf, st);
   if (e != cudaSuccess) return cuda_status(e, "qprep");

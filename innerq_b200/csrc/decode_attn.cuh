@@ -55,6 +55,7 @@ struct DevSide {
   int n_sink, n_q, n_rec;
   int group;
   int asym;
+  int chan;   // values grouped over channels (scales per token and channel group)
 };
 
 struct DevArgs {
@@ -463,14 +464,18 @@ __device__ __forceinline__ void load_kscales(float2 out[2][NG], const uint16_t* 
 }
 
 // BK/BV: code bits; RP: query heads per KV head padded to 4 or 8; DT: dtype;
-// NG: K channel groups per token (4, 2, 1 for groups of 32, 64, 128)
-template <int BK, int BV, int RP, int DT, int NG>
+// NG: K channel groups per token (4, 2, 1 for groups of 32, 64, 128); VCH:
+// values grouped over channels too (same group size as the keys) instead of
+// over tokens
+template <int BK, int BV, int RP, int DT, int NG, int VCH>
 __global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 3)
 decode_attn_kernel(const DevArgs a) {
   constexpr int NT = RP / 4;
   constexpr int kStages = stages_for(RP);
   extern __shared__ __align__(128) uint8_t dyn[];
   __shared__ AttnStatic<RP> sm;
+  // channel-grouped values: probability digits per (channel group, head)
+  __shared__ __align__(16) uint8_t pdc_s[VCH ? kWarps : 1][VCH ? NG : 1][RP][2][kTile];
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
   const int R = a.R;
@@ -493,8 +498,10 @@ decode_attn_kernel(const DevArgs a) {
   // V token-group size is 32, 64 or 128: divide by shifting
   const int vgs = a.v.group == 32 ? 5 : (a.v.group == 64 ? 6 : 7);
   const int64_t vgroups_cap = a.v.codes ? (a.v.cap_tiles * 32) >> vgs : 0;
-  const uint16_t* vscale = a.v.scale ? a.v.scale + kbh * vgroups_cap * kD : nullptr;
-  const uint16_t* vzero = a.v.zero ? a.v.zero + kbh * vgroups_cap * kD : nullptr;
+  // token groups: [groups][128] per pair; channel groups: [tiles][32][NG] like K
+  const int64_t vsc_pair = VCH ? a.v.cap_tiles * 32 * NG : vgroups_cap * kD;
+  const uint16_t* vscale = a.v.scale ? a.v.scale + kbh * vsc_pair : nullptr;
+  const uint16_t* vzero = a.v.zero ? a.v.zero + kbh * vsc_pair : nullptr;
 
   // One ring per CTA: stage i holds the kWarps consecutive tiles
   // tile_beg + kWarps*i + w (warp w takes tile w).  Layout of a stage:
@@ -535,15 +542,21 @@ decode_attn_kernel(const DevArgs a) {
     const int64_t g0 = (t0 - vs) >> vgs, g1 = (t0 + n_in * kTile - 1 - vs) >> vgs;
     const uint32_t nvg = (uint32_t)(g1 - g0 + 1);
     uint8_t* st = ring + slot * SBC;
-    const uint32_t kb = n_in * (TBK + 64 * NG * (1 + kasym)), vb = n_in * TBV + nvg * 256 * (1 + vasym);
+    const uint32_t kb = n_in * (TBK + 64 * NG * (1 + kasym));
+    const uint32_t vb = n_in * TBV + (VCH ? n_in * 64 * NG : nvg * 256) * (1 + vasym);
     fence_proxy_async();
     mbar_arrive_tx(bar, kb + vb);
     bulk_g2s(st, kcodes + tk * TBK, n_in * TBK, bar);
     bulk_g2s(st + o_ks, kscale + tk * 32 * NG, n_in * 64 * NG, bar);
     if (kasym) bulk_g2s(st + o_kz, kzero + tk * 32 * NG, n_in * 64 * NG, bar);
     bulk_g2s(st + o_vc, vcodes + tv * TBV, n_in * TBV, bar);
-    bulk_g2s(st + o_vs, vscale + g0 * kD, nvg * 256, bar);
-    if (vasym) bulk_g2s(st + o_vz, vzero + g0 * kD, nvg * 256, bar);
+    if (VCH) {
+      bulk_g2s(st + o_vs, vscale + tv * 32 * NG, n_in * 64 * NG, bar);
+      if (vasym) bulk_g2s(st + o_vz, vzero + tv * 32 * NG, n_in * 64 * NG, bar);
+    } else {
+      bulk_g2s(st + o_vs, vscale + g0 * kD, nvg * 256, bar);
+      if (vasym) bulk_g2s(st + o_vz, vzero + g0 * kD, nvg * 256, bar);
+    }
   };
 
   float m_run[NT], l_run[NT];
@@ -722,8 +735,31 @@ decode_attn_kernel(const DevArgs a) {
 
     // ------------------------------------------------------------ softmax
     const bool vpacked = nqv > 0 && t0 >= vs && t0 + kTile <= vs + nqv;
+    // channel-grouped values may end inside a tile: its packed rows take the
+    // packed path and its dense rows the dense path
+    const bool vseam = VCH && nqv > 0 && t0 >= vs && t0 < vs + nqv && t0 + kTile > vs + nqv;
     float fv[NT];
     int psum[NT];
+    // channel-grouped values: per (head, group) tile factor, offset term, zero term
+    float fvg[VCH ? NT : 1][VCH ? NG : 1], offg[VCH ? NT : 1][VCH ? NG : 1], zsg[VCH ? NT : 1][VCH ? NG : 1];
+    float2 vsc[VCH ? 2 : 1][VCH ? NG : 1], vzc[VCH ? 2 : 1][VCH ? NG : 1];
+    if (VCH && (vpacked || vseam)) {
+      // the lane's 4 tokens' V scales (and zero points), rows 2m, 2m+1 paired
+      const uint16_t* sp;
+      const uint16_t* zp = nullptr;
+      if (fast) {
+        sp = reinterpret_cast<const uint16_t*>(sg + o_vs + warp * 64 * NG) + gid * 4 * NG;
+        if (vasym) zp = reinterpret_cast<const uint16_t*>(sg + o_vz + warp * 64 * NG) + gid * 4 * NG;
+      } else {
+        const int64_t ti = (t0 - vs) >> 5;
+        sp = vscale + ti * 32 * NG + gid * 4 * NG;
+        if (vasym) zp = vzero + ti * 32 * NG + gid * 4 * NG;
+      }
+      if constexpr (VCH) {
+        load_kscales<DT, NG>(vsc, sp);
+        if (vasym) load_kscales<DT, NG>(vzc, zp);
+      }
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const float mx = gid_max(fmaxf(fmaxf(x[nt][0], x[nt][1]), fmaxf(x[nt][2], x[nt][3])));
@@ -743,7 +779,45 @@ decode_attn_kernel(const DevArgs a) {
         for (int mt = 0; mt < 8; ++mt) o[nt][mt] = __fmul2_rn(o[nt][mt], f2(alpha));
       }
       const int head = nt * 4 + tq;
-      if (vpacked) {
+      if (VCH && (vpacked || vseam)) {
+        if constexpr (VCH) {
+        // p * s per channel group, 16-bit fixed point relative to the group's
+        // largest product in this tile (65000: stays below 2^16 after rounding).
+        // Rows past the packed end (a seam tile) are selected out: their
+        // scale slots were never written.
+        bool pin[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) pin[j] = vpacked || t0 + gid + 8 * j < vs + nqv;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          const float2 p01 = __fmul2_rn(make_float2(pt[0], pt[1]), vsc[0][g]);
+          const float2 p23 = __fmul2_rn(make_float2(pt[2], pt[3]), vsc[VCH ? 1 : 0][g]);
+          const float pr[4] = {pin[0] ? p01.x : 0.f, pin[1] ? p01.y : 0.f, pin[2] ? p23.x : 0.f,
+                               pin[3] ? p23.y : 0.f};
+          const float mg = gid_max(fmaxf(fmaxf(pr[0], pr[1]), fmaxf(pr[2], pr[3])));
+          const float inv = mg > 0.f ? __fdividef(65000.f, mg) : 0.f;
+          int ps = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int v = __float_as_int(fmaf(pr[j], inv, 12582912.f)) - 0x4B400000;
+            ps += v;
+            pdc_s[warp][g][head][0][gid + 8 * j] = (uint8_t)(v >> 8);
+            pdc_s[warp][g][head][1][gid + 8 * j] = (uint8_t)(v & 255);
+          }
+          fvg[nt][g] = wt * mg * (1.f / 65000.f);
+          offg[nt][g] = (float)(voff * gid_isum(ps));
+          if (vasym) {
+            const float2 z01 = __fmul2_rn(make_float2(pt[0], pt[1]), vzc[0][g]);
+            const float2 z23 = __fmul2_rn(make_float2(pt[2], pt[3]), vzc[VCH ? 1 : 0][g]);
+            const float zr = (pin[0] ? z01.x : 0.f) + (pin[1] ? z01.y : 0.f) + (pin[2] ? z23.x : 0.f) +
+                             (pin[3] ? z23.y : 0.f);
+            zsg[nt][g] = wt * gid_sum(zr);
+          } else {
+            zsg[nt][g] = 0.f;
+          }
+        }
+        }
+      } else if (vpacked) {
         int ps = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -756,7 +830,8 @@ decode_attn_kernel(const DevArgs a) {
         }
         psum[nt] = gid_isum(ps);
         fv[nt] = wt * (1.f / 65535.f);
-      } else {
+      }
+      if (!vpacked) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) sm.p_s[warp][head][gid + 8 * j] = pt[j] * wt;
       }
@@ -764,7 +839,32 @@ decode_attn_kernel(const DevArgs a) {
     __syncwarp();
 
     // ------------------------------------------------------------------ PV
-    if (vpacked) {
+    if (VCH && (vpacked || vseam)) {
+      if constexpr (VCH) {
+      VChunk<BV> vc;
+      if (fast) load_vchunk<BV>(vc, sg + o_vc + warp * TBV, lane);
+      else load_vchunk<BV>(vc, vcodes + (int64_t)((t0 - vs) >> 5) * tile_bytes(BV), lane);
+      constexpr int MPG = 8 / NG;  // 16-dim m-tiles per channel group
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int g = mt / MPG;
+        const uint32_t af[4] = {col_frag<BV>(vc.w, mt, 0, 0), col_frag<BV>(vc.w, mt, 1, 0),
+                                col_frag<BV>(vc.w, mt, 0, 1), col_frag<BV>(vc.w, mt, 1, 1)};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int head = nt * 4 + (gid >> 1), digit = gid & 1;
+          const uint32_t pb[2] = {*reinterpret_cast<const uint32_t*>(&pdc_s[warp][g][head][digit][4 * tq]),
+                                  *reinterpret_cast<const uint32_t*>(&pdc_s[warp][g][head][digit][16 + 4 * tq])};
+          int acc[4];
+          imma_u8u8(acc, af, pb, 0, 0, 0, 0);
+          const float t0f = (float)(acc[0] * 256 + acc[1]), t1f = (float)(acc[2] * 256 + acc[3]);
+          const float2 tc = __fadd2_rn(make_float2(t0f, t1f), f2(-offg[nt][g] * col_scale<BV>(mt)));
+          o[nt][mt] = __ffma2_rn(f2(fvg[nt][g] * (1.f / col_scale<BV>(mt))), tc, o[nt][mt]);
+          if (vasym) o[nt][mt] = __fadd2_rn(o[nt][mt], f2(zsg[nt][g]));
+        }
+      }
+      }
+    } else if (vpacked) {
       uint32_t pb[NT][2];
       float offp[NT];
       float zf[NT];
@@ -792,8 +892,9 @@ decode_attn_kernel(const DevArgs a) {
       }
       if (vasym) v_packed_accumulate<BV, NT, true>(vc, sv, zv, pb, offp, fv, zf, o);
       else v_packed_accumulate<BV, NT, false>(vc, sv, zv, pb, offp, fv, zf, o);
-    } else {
-      // dense V tile (sink / recent / masked rows), probabilities as dtype hi/lo
+    }
+    if (!vpacked) {
+      // dense V rows (sink / recent / masked rows), probabilities as dtype hi/lo
       uint32_t pb[NT][2][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {

@@ -7,9 +7,9 @@
 namespace innerq {
 
 namespace {
-template <int BV, int RP, int NG>
+template <int BV, int RP, int NG, int VCH>
 cudaError_t go(const DevArgs& a, dim3 grid, cudaStream_t s) {
-  auto kern = decode_attn_kernel<3, BV, RP, BF16, NG>;
+  auto kern = decode_attn_kernel<3, BV, RP, BF16, NG, VCH>;
   const int smem = attn_dyn_smem(3, BV, NG, a.k.asym, a.v.asym, RP);
   int dev = 0;
   cudaGetDevice(&dev);
@@ -25,9 +25,9 @@ cudaError_t go(const DevArgs& a, dim3 grid, cudaStream_t s) {
 template <int BV, int RP>
 cudaError_t go_ng(const DevArgs& a, int ng, dim3 grid, cudaStream_t s) {
   switch (ng) {
-    case 4: return go<BV, RP, 4>(a, grid, s);
-    case 2: return go<BV, RP, 2>(a, grid, s);
-    case 1: return go<BV, RP, 1>(a, grid, s);
+    case 4: return a.v.chan ? go<BV, RP, 4, 1>(a, grid, s) : go<BV, RP, 4, 0>(a, grid, s);
+    case 2: return a.v.chan ? go<BV, RP, 2, 1>(a, grid, s) : go<BV, RP, 2, 0>(a, grid, s);
+    case 1: return a.v.chan ? go<BV, RP, 1, 1>(a, grid, s) : go<BV, RP, 1, 0>(a, grid, s);
     default: return cudaErrorNotSupported;
   }
 }

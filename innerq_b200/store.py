@@ -92,10 +92,11 @@ class PackedSide:
     @property
     def fusable(self) -> bool:
         """The fused decode attention reads this side's layout: keys grouped
-        over channels, values over tokens (the InnerQ defaults)."""
+        over channels; values over tokens (the InnerQ default) or over
+        channels with the keys' group size (checked by the layer)."""
         if not self.quantize:
             return True
-        return self.over_token == (self.role == _lib.ROLE_V)
+        return self.role == _lib.ROLE_V or not self.over_token
 
     @property
     def n_sink(self) -> int:

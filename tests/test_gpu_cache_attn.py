@@ -72,7 +72,7 @@ def test_layer_matches_reference_fixture(cache_golden, name):
 def test_kivi_layout_materialised_and_not_fused():
     """KIVI (keys grouped over tokens, values over channels, asymmetric) runs
     through the packed store and the dequant kernel, bit-exact with the
-    reference; the fused kernel refuses that layout."""
+    reference; the fused kernel refuses token-grouped keys."""
     from innerq_b200.attention import decode_attention
     from innerq_b200.cache import InnerqDynamicLayer
     from innerq_b200._lib import InnerqError
@@ -86,7 +86,7 @@ def test_kivi_layout_materialised_and_not_fused():
         Kr, Vr = ol.update(to_np32(k[:, :, t:t + 1]), to_np32(v[:, :, t:t + 1]))
     np.testing.assert_array_equal(to_np32(K), Kr)
     np.testing.assert_array_equal(to_np32(V), Vr)
-    assert not layer.key_side.fusable and not layer.value_side.fusable
+    assert not layer.key_side.fusable and not layer._fusable()
     with pytest.raises(InnerqError):
         decode_attention(synth_q(1, 8), layer.key_side, layer.value_side)
 
@@ -119,15 +119,35 @@ CASES = [
 ]
 
 
+# values grouped over channels (the BASELINE-literal layout: groups along
+# head_dim for K and V); value_flush_size 32 keeps whole packed tiles
+CASES_VCH = [
+    (4, 4, "symmetric", "symmetric", 4, "fp16", 32, 32, 0, 32, True, 1000, 5),
+    (2, 2, "asymmetric", "asymmetric", 8, "bf16", 32, 32, 32, 96, False, 700, 40),
+    (3, 3, "symmetric", "asymmetric", 1, "fp16", 64, 64, 4, 32, True, 517, 33),
+    (4, 2, "asymmetric", "symmetric", 2, "fp16", 128, 128, 0, 64, False, 900, 3),
+]
+
+
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
 def test_decode_attention_vs_oracle(case):
+    _check_case(case, value_over_token=True)
+
+
+@pytest.mark.parametrize("case", CASES_VCH, ids=[f"v{i}" for i in range(len(CASES_VCH))])
+def test_decode_attention_value_channel_groups(case):
+    _check_case(case, value_over_token=False)
+
+
+def _check_case(case, value_over_token):
     from innerq_b200.attention import decode_attention, decode_attention_partials
     from innerq_b200.cache import InnerqDynamicLayer
     bk, bv, km, vm, R, dtype, gk, gv, sink, recent, norm, T0, steps = case
     kw = dict(k_bits=bk, v_bits=bv, key_quantize_mode=km, value_quantize_mode=vm,
               key_group_size=gk, value_group_size=gv, key_w_sink=sink, value_w_sink=sink,
               key_w_recent=recent, value_w_recent=recent, key_flush_size=1,
-              value_flush_size=gv, key_normalize=norm)
+              value_flush_size=gv if value_over_token else 32, key_normalize=norm,
+              value_quantize_over_token=value_over_token)
     Hkv, B = 2, 2
     k, v = synth_kv(B, Hkv, T0 + steps, dtype=dtype, seed=T0)
     layer = InnerqDynamicLayer(cfg(**kw), 0)
@@ -137,6 +157,7 @@ def test_decode_attention_vs_oracle(case):
     for t in range(T0, T0 + steps):
         layer.update(k[:, :, t:t + 1], v[:, :, t:t + 1])
         Kr, Vr = ol.update(to_np32(k[:, :, t:t + 1]), to_np32(v[:, :, t:t + 1]))
+    assert layer._fusable()
     q = synth_q(B, Hkv * R, dtype=dtype, seed=T0 + 1)
     qn = to_np32(q)
     # (1) the 1e-3 bar: reference fp32 dequantize (quant.py:121-131, cache.py:241-271)
