@@ -51,19 +51,29 @@ def parse():
     ap.add_argument("--kbits", type=int, default=4)
     ap.add_argument("--vbits", type=int, default=4)
     ap.add_argument("--group", type=int, default=32)
+    ap.add_argument("--v-layout", default="tokens", choices=["tokens", "channels"],
+                    help="value groups over tokens (InnerQ default) or over channels "
+                         "(groups along head_dim for K and V)")
+    ap.add_argument("--mode", default="symmetric", choices=["symmetric", "asymmetric"],
+                    help="quantisation mode of both K and V")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", default="c1", choices=["c1", "c3"],
+    ap.add_argument("--workload", default="c1", choices=["c1", "c3", "sweep"],
                     help="c1: decode attention over a 32-layer cache (default); "
-                         "c3: full decode step of a random-init Llama-3-8B-shaped model")
+                         "c3: full decode step of a random-init Llama-3-8B-shaped model; "
+                         "sweep: the C1/C2/C4 attention and append grid, one JSON line per "
+                         "configuration (not the one-line bench contract)")
     return ap.parse_args()
 
 
 def cache_kw(a):
+    vtok = getattr(a, "v_layout", "tokens") == "tokens"
+    mode = getattr(a, "mode", "symmetric")
     return dict(k_bits=a.kbits, v_bits=a.vbits, key_group_size=a.group, value_group_size=a.group,
-                key_flush_size=1, value_flush_size=max(32, a.group), key_w_sink=32, value_w_sink=32,
-                key_w_recent=96, value_w_recent=96, key_normalize=True,
-                key_quantize_over_token=False, value_quantize_over_token=True)
+                key_flush_size=1, value_flush_size=max(32, a.group) if vtok else 32,
+                key_w_sink=32, value_w_sink=32, key_w_recent=96, value_w_recent=96,
+                key_normalize=True, key_quantize_over_token=False, value_quantize_over_token=vtok,
+                key_quantize_mode=mode, value_quantize_mode=mode)
 
 
 def side_bytes(n_q, n_sink, n_recent, bits, group, over_token, asym=False, norm=False):
@@ -82,7 +92,7 @@ def side_bytes(n_q, n_sink, n_recent, bits, group, over_token, asym=False, norm=
 def layer_bytes(layer, B, Hkv, Hq):
     k, v = layer.key_side, layer.value_side
     per_bh = side_bytes(k.n_q, k.n_sink, k.n_recent, k.bits, k.group, False, k.mode == 1, k.normalize) \
-        + side_bytes(v.n_q, v.n_sink, v.n_recent, v.bits, v.group, True, v.mode == 1)
+        + side_bytes(v.n_q, v.n_sink, v.n_recent, v.bits, v.group, v.over_token, v.mode == 1)
     return B * Hkv * per_bh + 2 * B * Hq * D * 2
 
 
@@ -96,16 +106,24 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.f = None
+        self.skip = 0
 
     def start(self):
+        """Start sampling every 20 ms and return once the first sample is in,
+        so that a short timed region that follows is covered."""
         try:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t_end = time.time() + 5.0
+        while time.time() < t_end and os.path.getsize(self.f.name) == 0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.skip = sum(1 for _ in open(self.f.name))  # samples taken before the region
 
     def stop(self):
         if self.proc is None:
@@ -118,6 +136,11 @@ class ClockSampler:
         self.f.seek(0)
         rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
         os.unlink(self.f.name)
+        # samples inside the timed region; the last one before it (taken under
+        # the same load, just after warm-up) when the region was shorter than
+        # the sampling period
+        inside = rows[self.skip:] if len(rows) > self.skip else rows[-1:]
+        rows = inside
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -386,6 +409,7 @@ def run_ours(a):
                 "workload": "C1: decode step over a 32-layer Llama-3-8B-shaped 4-bit InnerQ cache",
                 "batch": B, "context": a.ctx, "layers": L, "q_heads": a.hq, "kv_heads": a.hkv,
                 "head_dim": D, "k_bits": a.kbits, "v_bits": a.vbits, "group": a.group,
+                "v_groups_over": a.v_layout, "mode": a.mode,
                 "parallelism": f"kv-head shards x{world}",
                 "l2": f"inputs larger than L2 ({total_bytes / 1e9:.1f} GB of cache read per step)",
                 "us_per_layer": round(ms * 1e3 / L, 2),
@@ -480,10 +504,119 @@ def run_c3(a):
     print(json.dumps(line), flush=True)
 
 
+SWEEP = [
+    # (name, B, Hq, context, bits, group, v_layout, mode)
+    ("C1", 1, 32, 32768, 4, 32, "tokens", "symmetric"),
+    ("C1", 8, 32, 32768, 4, 32, "tokens", "symmetric"),
+    ("C1", 32, 32, 32768, 4, 32, "tokens", "symmetric"),
+    ("C1 BASELINE-literal", 32, 32, 32768, 4, 32, "channels", "symmetric"),
+    ("C1 asym", 32, 32, 32768, 4, 32, "tokens", "asymmetric"),
+] + [("C2", 16, 32, ctx, bits, g, "tokens", "symmetric")
+     for bits in (2, 3) for ctx in (4096, 16384, 65536) for g in (32, 64, 128)] + [
+    ("C2 BASELINE-literal", 16, 32, 16384, 2, 32, "channels", "symmetric"),
+    ("C2 BASELINE-literal", 16, 32, 16384, 3, 32, "channels", "symmetric"),
+    ("C2 asym", 16, 32, 16384, 2, 32, "tokens", "asymmetric"),
+    ("C4 (1 GPU, 4 layers)", 8, 64, 131072, 2, 32, "tokens", "symmetric"),
+]
+
+
+def run_sweep(a):
+    """Fused decode attention (query prep + attention + merge, replayed from a
+    CUDA graph so batch-1 launches are not host bound) and the append kernels
+    over the BASELINE configurations; one JSON line per configuration.
+    Several independent layer caches rotate so each launch reads HBM, not L2."""
+    import torch
+
+    from innerq_b200.attention import decode_attention
+    from innerq_b200.cache import InnerqDynamicLayer
+    from innerq_b200.store import PackedSide
+    from innerq_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("hbm_gbs", 6650.0)) \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
+    for name, B, hq, ctx, bits, group, vlay, mode in SWEEP:
+        a2 = types.SimpleNamespace(kbits=bits, vbits=bits, group=group, v_layout=vlay, mode=mode)
+        kw = cache_kw(a2)
+        hkv = 8
+        per_layer = B * hkv * ctx * (bits * 32 + 16)
+        nl = max(4, min(8, int(1.2e9 // per_layer) + 1))
+        g = torch.Generator(device=dev)
+        g.manual_seed(0)
+        layers = []
+        for _ in range(nl):
+            layer = InnerqDynamicLayer(types.SimpleNamespace(**kw), 0)
+            k = torch.randn((B, hkv, ctx, D), device=dev, generator=g)
+            k *= torch.exp(torch.randn(D, device=dev, generator=g))
+            k = k.half()
+            v = torch.randn((B, hkv, ctx, D), device=dev, generator=g).half()
+            layer.update(k, v)
+            del k, v
+            layers.append(layer)
+        q = torch.randn((B, hq, 1, D), device=dev, generator=g).half()
+        outs = [torch.empty((B, hq, D), dtype=q.dtype, device=dev) for _ in layers]
+        for l, o in zip(layers, outs):
+            decode_attention(q, l.key_side, l.value_side, out=o)
+        torch.cuda.synchronize()
+        reps = 4
+        st = torch.cuda.Stream(dev)
+        with torch.cuda.stream(st):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                for _ in range(reps):
+                    for l, o in zip(layers, outs):
+                        decode_attention(q, l.key_side, l.value_side, out=o)
+        torch.cuda.synchronize()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (5 * reps * nl)
+        nb = layer_bytes(layers[0], B, hkv, hq)
+        del graph, layers, outs
+        torch.cuda.empty_cache()
+        # append: one K token (channel groups) and one 4096-token chunk
+        side = PackedSide(_lib.ROLE_K, bits, group, _lib.SYM if mode == "symmetric" else _lib.ASYM,
+                          False, 0, 0, 1)
+        x = torch.randn((B, hkv, 4096, D), device=dev, generator=g).half()
+        side.prefill(x[:, :, :1])
+        side.reserve(8192)
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(20):
+            side._quantize(x[:, :, i:i + 1])
+        e1.record()
+        torch.cuda.synchronize()
+        us_tok = e0.elapsed_time(e1) * 1e3 / 20
+        side.n_q = 0
+        e0.record()
+        side._quantize(x)
+        e1.record()
+        torch.cuda.synchronize()
+        us_chunk = e0.elapsed_time(e1) * 1e3
+        del side, x
+        torch.cuda.empty_cache()
+        print(json.dumps({
+            "config": name, "batch": B, "q_heads": hq, "kv_heads": hkv, "context": ctx,
+            "bits": bits, "group": group, "v_groups_over": vlay, "mode": mode,
+            "attn_us": round(us, 1), "attn_GBs": round(nb / us / 1e3, 1),
+            "frac_of_measured_hbm": round(nb / us / 1e3 / peak, 3), "bytes_per_launch": nb,
+            "append_1_token_us": round(us_tok, 1), "append_4096_chunk_us": round(us_chunk, 1),
+            "chunk_read_GBs": round(B * hkv * 4096 * D * 2 / us_chunk / 1e3, 1)}), flush=True)
+
+
 def main():
     a = parse()
     if a.workload == "c3" and a.impl != "reference":
         run_c3(a)
+        return
+    if a.workload == "sweep":
+        run_sweep(a)
         return
     if a.impl == "reference":
         run_reference(a)
