@@ -83,6 +83,21 @@ __device__ __forceinline__ uint32_t pack2(uint16_t lo, uint16_t hi) {
   return (uint32_t)lo | ((uint32_t)hi << 16);
 }
 
+// Correctly rounded a / b given rb = RN(1/b): Markstein's division
+// (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Develop. 34(1), 1990).  q = RN(a*rb) is
+// within one ulp of a/b, the remainder r = a - q*b is exact in one FMA, and
+// RN(q + r*rb) = RN(a/b) provided no intermediate overflows or underflows.
+// Called only with fp16 operands (exact in fp32, |a| <= 65504 and
+// 2^-24 <= b <= 65504), where that holds; a GPU test compares it bit for bit
+// with the IEEE '/' over every pair of fp16 values.
+__device__ __forceinline__ float div_rn(float a, float b, float rb) {
+  const float q = __fmul_rn(a, rb);
+  const float r = __fmaf_rn(-q, b, a);
+  // an exact quotient keeps q (and with it the sign of a zero a)
+  return r == 0.f ? q : __fmaf_rn(r, rb, q);
+}
+
 // ------------------------------------------------------------------ mma ---
 __device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], const uint32_t b[2]) {
   asm volatile(

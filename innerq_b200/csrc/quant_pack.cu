@@ -8,7 +8,9 @@
 //                                  c = rint(clamp(h(|x| / s), 0, 2^(b-1)-1))
 //   asymmetric (quant.py:58-73):   s = h(h(max-min) / (2^b-1)),
 //                                  c = rint(clamp(h(h(x-min) / s), 0, 2^b-1))
-// Division is the IEEE fp32 '/' (this file must not be built with fast math).
+// Division gives the IEEE fp32 '/' result (this file must not be built with
+// fast math); with fp16 operands it is computed by Markstein's sequence from
+// one correctly rounded reciprocal per divisor (div_rn in common.cuh).
 // A group whose scale is 0 makes the reference divide 0/0 (NaN, stored as
 // INT32_MIN); the packed format stores code 0 there, which dequantizes to the
 // same value.
@@ -23,9 +25,37 @@ namespace innerq {
 template <int BITS>
 __device__ __forceinline__ int qmax_sym() { return (1 << (BITS - 1)) - 1; }
 
+// rint(clamp(q, 0, qmax)) with a NaN quotient (0 / 0 scale) giving code 0:
+// fmaxf returns its non-NaN operand; adding 1.5 * 2^23 rounds to the nearest
+// integer, ties to even, like rintf (q <= 15 here)
 __device__ __forceinline__ int code_of(float q, float qmax) {
-  if (q != q) return 0;  // NaN from a zero scale
-  return (int)rintf(fminf(fmaxf(q, 0.f), qmax));
+  return __float_as_int(fminf(fmaxf(q, 0.f), qmax) + 12582912.f) - 0x4B400000;
+}
+
+// a / b as the IEEE fp32 '/' computes it for a non-negative numerator and a
+// divisor shared by many numerators: fp16 operands take Markstein's sequence
+// with one reciprocal per divisor (rb = __frcp_rn(b), computed by the caller);
+// bf16 operands, whose range can underflow that sequence, use '/'.
+template <int DT>
+__device__ __forceinline__ float shared_div(float a, float b, float rb) {
+  if (DT == F16) {
+    // a zero or infinite divisor gives the IEEE quotient of a non-negative a
+    // by select: a / 0 = inf (NaN for 0 / 0), a / inf = 0
+    const float special = b == 0.f ? (a > 0.f ? INFINITY : NAN) : 0.f;
+    const float q = div_rn(a, b, rb);
+    return (b > 0.f && b < INFINITY) ? q : special;
+  }
+  return a / b;
+}
+template <int DT>
+__device__ __forceinline__ float shared_rcp(float b) {
+  return (DT == F16 && b > 0.f && b < INFINITY) ? __frcp_rn(b) : 0.f;
+}
+// a / q for the constant q = 2^k - 1 of a quantizer (IEEE result; fp16 a)
+template <int DT, int Q>
+__device__ __forceinline__ float div_qmax(float a) {
+  if (DT == F16) return div_rn(a, (float)Q, 1.f / (float)Q);  // RN(1/Q) folds at compile time
+  return a / (float)Q;
 }
 
 // --------------------------------------------------------------------------
@@ -54,19 +84,26 @@ __device__ __forceinline__ void pack_row_token(const uint2 raw, int t, int64_t b
                 to_f<DT>(raw.y >> 16)};
   if (nf) {  // cache.py:125 key_states / factor, in the dtype
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = rnd<DT>(v[i] / to_f<DT>(nf[bh * kD + 4 * lane + i]));
+    for (int i = 0; i < 4; ++i) {
+      const float f = to_f<DT>(nf[bh * kD + 4 * lane + i]);
+      // signed numerator, and a zero factor is possible for a channel that was
+      // all zero in the first chunk: IEEE '/' outside the fast range
+      v[i] = rnd<DT>((DT == F16 && f > 0.f && f < INFINITY) ? div_rn(v[i], f, __frcp_rn(f)) : v[i] / f);
+    }
   }
-  const int gl = group / 4;  // lanes per group
+  const int gl = group >> 2;  // lanes per group (8, 16, 32): powers of two
+  const int glog = 31 - __clz(gl);
   float s, z = 0.f;
   int u[4];
   if (!asym) {
     float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     for (int o = 1; o < gl; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const float qmax = (float)qmax_sym<BITS>();
-    s = rnd<DT>(mx / qmax);
+    s = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx));
+    const float rs = shared_rcp<DT>(s);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int c = code_of(rnd<DT>(fabsf(v[i]) / s), qmax);
+      const int c = code_of(rnd<DT>(shared_div<DT>(fabsf(v[i]), s, rs)), qmax);
       u[i] = (v[i] < 0.f ? -c : c) + (1 << (BITS - 1));
     }
   } else {
@@ -77,17 +114,18 @@ __device__ __forceinline__ void pack_row_token(const uint2 raw, int t, int64_t b
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
     const float qmax = (float)((1 << BITS) - 1);
-    s = rnd<DT>(rnd<DT>(mx - mn) / qmax);
+    s = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx - mn)));
     z = mn;
+    const float rs = shared_rcp<DT>(s);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) u[i] = code_of(rnd<DT>(rnd<DT>(v[i] - mn) / s), qmax);
+    for (int i = 0; i < 4; ++i) u[i] = code_of(rnd<DT>(shared_div<DT>(rnd<DT>(v[i] - mn), s, rs)), qmax);
   }
   const int64_t p = t_off + t;
   const int64_t ti = p >> 5;
   const int r = (int)(p & 31);
-  const int ng = kD / group;
-  if (lane % gl == 0) {
-    const int g = lane / gl;
+  const int ng = 32 >> glog;  // kD / group
+  if ((lane & (gl - 1)) == 0) {
+    const int g = lane >> glog;
     const int64_t si = (bh * cap_tiles + ti) * 32 * ng + row_scale_idx(r, g, ng);
     scale[si] = from_f<DT>(s);
     if (asym) zero[si] = from_f<DT>(z);
@@ -110,40 +148,47 @@ __device__ __forceinline__ void pack_row_token(const uint2 raw, int t, int64_t b
     }
     return;
   }
-  // assemble the row's four lane segments (one per tq) with the layout map
-  constexpr int kWordsPerSeg = BITS == 4 ? 4 : (BITS == 2 ? 2 : (BITS == 3 ? 3 : 1));  // b=3: L0, L1, H
-  __syncwarp();  // the previous token's segment reads are done
-  if (lane < 4 * kWordsPerSeg) seg[lane] = 0u;
-  __syncwarp();
+  // Row layout (keys): a token row's codes never share a 32-bit word with
+  // another row, and this lane's 4 codes (dims 4*lane + i) all land in one
+  // word: word kb = lane>>3 of the row's segment for lane2 = gid*4 + (lane&3),
+  // at bit offsets 8i + (position of this lane among the word's sharers).
+  // Build the word in registers, OR it across the sharing lanes with
+  // shuffles, and store whole words (no atomics, no staging).
+  (void)seg;
+  const int half = (lane >> 2) & 1, kb = lane >> 3, tq = lane & 3;
+  const int gid = r & 7, j = r >> 3, lane2 = gid * 4 + tq;
+  uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
+  if (BITS == 4) {
+    uint32_t w = 0u;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int d = 4 * lane + i;
-    const BitPos bp = row_pos(BITS, r, d);
-    const int tq = (d >> 2) & 3;
-    const uint32_t uc = (uint32_t)u[i];
-    if (BITS == 1) {
-      atomicOr(&seg[tq], uc << bp.shift);
-    } else if (BITS == 4) {
-      atomicOr(&seg[tq * 4 + ((bp.off & 15) >> 2)], uc << bp.shift);
-    } else {
-      atomicOr(&seg[tq * kWordsPerSeg + ((bp.off & 7) >> 2)], (uc & 3u) << bp.shift);
-      if (BITS == 3) atomicOr(&seg[tq * 3 + 2], (uc >> 2) << bp.hshift);
+    for (int i = 0; i < 4; ++i) w |= (uint32_t)u[i] << (8 * i + 4 * half);
+    w |= __shfl_xor_sync(0xffffffffu, w, 4);
+    if (!half) *reinterpret_cast<uint32_t*>(tb + j * 512 + lane2 * 16 + kb * 4) = w;
+  } else if (BITS == 1) {
+    uint32_t w = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w |= ((uint32_t)u[i] & 1u) << (8 * i + kb * 2 + half);
+    w |= __shfl_xor_sync(0xffffffffu, w, 4);
+    w |= __shfl_xor_sync(0xffffffffu, w, 8);
+    w |= __shfl_xor_sync(0xffffffffu, w, 16);
+    if (lane < 4) *reinterpret_cast<uint32_t*>(tb + lane2 * 16 + j * 4) = w;
+  } else {
+    // low two bits: word kb>>1 of the row's 8 bytes, crumb 4i + (kb&1)*2 + half
+    uint32_t w = 0u, wh = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      w |= ((uint32_t)u[i] & 3u) << (8 * i + 4 * (kb & 1) + 2 * half);
+      if (BITS == 3) wh |= (((uint32_t)u[i] >> 2) & 1u) << (8 * i + kb * 2 + half);
     }
-  }
-  __syncwarp();
-  if (lane < 4) {
-    const int tq = lane;
-    uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
-    const int lane2 = (r & 7) * 4 + tq, j = r >> 3;
-    if (BITS == 1) {
-      *reinterpret_cast<uint32_t*>(tb + lane2 * 16 + j * 4) = seg[tq];
-    } else if (BITS == 4) {
-      *reinterpret_cast<uint4*>(tb + j * 512 + lane2 * 16) =
-          make_uint4(seg[tq * 4], seg[tq * 4 + 1], seg[tq * 4 + 2], seg[tq * 4 + 3]);
-    } else {
-      *reinterpret_cast<uint2*>(tb + (j >> 1) * 512 + lane2 * 16 + (j & 1) * 8) =
-          make_uint2(seg[tq * kWordsPerSeg], seg[tq * kWordsPerSeg + 1]);
-      if (BITS == 3) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = seg[tq * 3 + 2];
+    w |= __shfl_xor_sync(0xffffffffu, w, 4);
+    w |= __shfl_xor_sync(0xffffffffu, w, 8);
+    if ((lane & 12) == 0)
+      *reinterpret_cast<uint32_t*>(tb + (j >> 1) * 512 + lane2 * 16 + (j & 1) * 8 + (kb >> 1) * 4) = w;
+    if (BITS == 3) {
+      wh |= __shfl_xor_sync(0xffffffffu, wh, 4);
+      wh |= __shfl_xor_sync(0xffffffffu, wh, 8);
+      wh |= __shfl_xor_sync(0xffffffffu, wh, 16);
+      if (lane < 4) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = wh;
     }
   }
 }
@@ -168,10 +213,12 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
   for (int k = 0; k < 4; ++k)
     if (t0 + k < T)
       raw[k] = *reinterpret_cast<const uint2*>(x + b * sb + h * sh + (int64_t)(t0 + k) * st + 4 * lane);
-#pragma unroll 1
-  for (int k = 0; k < 4 && t0 + k < T; ++k)
-    pack_row_token<DT, BITS, ROLEV>(raw[k], t0 + k, bh, lane, wbuf[warp], nf, group, asym, codes,
-                                    scale, zero, cap_tiles, t_off);
+  // unrolled so raw[] stays in registers
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (t0 + k < T)
+      pack_row_token<DT, BITS, ROLEV>(raw[k], t0 + k, bh, lane, wbuf[warp], nf, group, asym, codes,
+                                      scale, zero, cap_tiles, t_off);
 }
 
 // --------------------------------------------------------------------------
@@ -184,8 +231,12 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
                       int group, int asym, uint8_t* __restrict__ codes,
                       uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
                       int64_t cap_tiles, int64_t t_off) {
-  __shared__ uint8_t cb[128][kD];
-  __shared__ __align__(16) uint32_t tw[4 * tile_bytes(4) / 4];
+  // col layout (values), 2-4 bits: codes per dim as words of 4 tokens,
+  // [dim][token/4] (+1 pad word: conflict-free); otherwise [token][dim] bytes
+  constexpr bool kWords = ROLEV && BITS >= 2;
+  __shared__ uint8_t cb[kWords ? 1 : 128][kWords ? 1 : kD];
+  __shared__ uint32_t cbt[kWords ? kD : 1][kWords ? 33 : 1];
+  __shared__ __align__(16) uint32_t tw[kWords ? 4 : 4 * tile_bytes(4) / 4];
   const int gi = blockIdx.x, h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
   const int64_t bh = (int64_t)b * H + h;
   const int d = threadIdx.x;
@@ -195,11 +246,19 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
     float mx = 0.f;
     for (int t = 0; t < group; ++t) mx = fmaxf(mx, fabsf(to_f<DT>(xp[(int64_t)t * st])));
     const float qmax = (float)qmax_sym<BITS>();
-    s = rnd<DT>(mx / qmax);
+    s = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx));
+    const float rs = shared_rcp<DT>(s);
+    uint32_t w4 = 0u;
     for (int t = 0; t < group; ++t) {
       const float v = to_f<DT>(xp[(int64_t)t * st]);
-      const int c = code_of(rnd<DT>(fabsf(v) / s), qmax);
-      cb[t][d] = (uint8_t)((v < 0.f ? -c : c) + (1 << (BITS - 1)));
+      const int c = code_of(rnd<DT>(shared_div<DT>(fabsf(v), s, rs)), qmax);
+      const uint32_t uc = (uint32_t)((v < 0.f ? -c : c) + (1 << (BITS - 1)));
+      if (kWords) {
+        w4 |= uc << (8 * (t & 3));
+        if ((t & 3) == 3) { cbt[d][t >> 2] = w4; w4 = 0u; }
+      } else {
+        cb[t][d] = (uint8_t)uc;
+      }
     }
   } else {
     float mn = INFINITY, mx = -INFINITY;
@@ -209,11 +268,19 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
       mx = fmaxf(mx, v);
     }
     const float qmax = (float)((1 << BITS) - 1);
-    s = rnd<DT>(rnd<DT>(mx - mn) / qmax);
+    s = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx - mn)));
     z = mn;
+    const float rs = shared_rcp<DT>(s);
+    uint32_t w4 = 0u;
     for (int t = 0; t < group; ++t) {
       const float v = to_f<DT>(xp[(int64_t)t * st]);
-      cb[t][d] = (uint8_t)code_of(rnd<DT>(rnd<DT>(v - mn) / s), qmax);
+      const uint32_t uc = (uint32_t)code_of(rnd<DT>(shared_div<DT>(rnd<DT>(v - mn), s, rs)), qmax);
+      if (kWords) {
+        w4 |= uc << (8 * (t & 3));
+        if ((t & 3) == 3) { cbt[d][t >> 2] = w4; w4 = 0u; }
+      } else {
+        cb[t][d] = (uint8_t)uc;
+      }
     }
   }
   const int64_t groups_cap = cap_tiles * 32 / group;
@@ -222,9 +289,51 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
   scale[si] = from_f<DT>(s);
   if (asym) zero[si] = from_f<DT>(z);
   __syncthreads();
-  // assemble each 32-token tile of the group in shared memory with the layout map
   const int n_tiles = group / 32;
   constexpr int TW = tile_bytes(BITS) / 4;
+  if constexpr (kWords) {
+    // every word of the group's tiles from 2-8 word loads of 4 tokens' codes
+    // (the col-layout map of common.cuh); stored straight to global memory
+    const int64_t ti0 = (t_off + (int64_t)gi * group) / 32;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(codes + (bh * cap_tiles + ti0) * tile_bytes(BITS));
+    for (int i = threadIdx.x; i < n_tiles * TW; i += blockDim.x) {
+      const int k = i / TW, wi = i % TW;
+      uint32_t w = 0u;
+      if (BITS == 4) {
+        const int pc = wi >> 7, L = (wi >> 2) & 31, c = wi & 3;
+        const int hh = c >> 1, hf = c & 1, g8 = L >> 2, tq = L & 3;
+        const int widx = 8 * k + hf * 4 + tq;
+        const int d0 = pc * 16 + hh * 8 + g8;
+        w = cbt[d0][widx] | (cbt[d0 + 64][widx] << 4);
+      } else if (BITS == 2) {
+        const int pc = wi >> 7, L = (wi >> 2) & 31, c = wi & 3;
+        const int hh = c >> 1, hf = c & 1, g8 = L >> 2, tq = L & 3;
+        const int widx = 8 * k + hf * 4 + tq;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w |= cbt[(2 * q + pc) * 16 + hh * 8 + g8][widx] << (2 * q);
+      } else if (wi < 256) {  // 3-bit plane L
+        const int L = (wi >> 2) & 31, mt = (wi >> 7) * 4 + (wi & 3);
+        const int g8 = L >> 2, tq = L & 3;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int hh = c >> 1, hf = c & 1;
+          w |= (cbt[mt * 16 + hh * 8 + g8][8 * k + hf * 4 + tq] & 0x03030303u) << (2 * c);
+        }
+      } else {  // 3-bit plane H
+        const int wj = wi - 256, L = wj >> 2, mq = wj & 3;
+        const int g8 = L >> 2, tq = L & 3;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int m1 = c >> 2, hh = (c >> 1) & 1, hf = c & 1;
+          const int mt = 2 * mq + m1;
+          w |= ((cbt[mt * 16 + hh * 8 + g8][8 * k + hf * 4 + tq] >> 2) & 0x01010101u) << c;
+        }
+      }
+      dst[(int64_t)k * TW + wi] = w;
+    }
+    return;
+  }
+  // assemble each 32-token tile of the group in shared memory with the layout map
   for (int i = threadIdx.x; i < n_tiles * TW; i += blockDim.x) tw[i] = 0u;
   __syncthreads();
   for (int t = 0; t < group; ++t) {
