@@ -56,6 +56,9 @@ def parse():
                          "(groups along head_dim for K and V)")
     ap.add_argument("--mode", default="symmetric", choices=["symmetric", "asymmetric"],
                     help="quantisation mode of both K and V")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch every kernel from the host each step instead of replaying the "
+                         "recorded decode step (CUDA graph, cache graph mode)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="c1", choices=["c1", "c3", "sweep"],
@@ -89,10 +92,14 @@ def side_bytes(n_q, n_sink, n_recent, bits, group, over_token, asym=False, norm=
     return b
 
 
-def layer_bytes(layer, B, Hkv, Hq):
+def layer_bytes(layer, B, Hkv, Hq, graph_steps=None):
+    """Algorithmic bytes one attention launch reads and writes; graph_steps:
+    the layer is in graph mode, that many steps after its step-0 state."""
     k, v = layer.key_side, layer.value_side
-    per_bh = side_bytes(k.n_q, k.n_sink, k.n_recent, k.bits, k.group, False, k.mode == 1, k.normalize) \
-        + side_bytes(v.n_q, v.n_sink, v.n_recent, v.bits, v.group, v.over_token, v.mode == 1)
+    (knq, knr), (vnq, vnr) = ((k.n_q, k.n_recent), (v.n_q, v.n_recent)) if graph_steps is None else \
+        (k.state_after(graph_steps), v.state_after(graph_steps))
+    per_bh = side_bytes(knq, k.n_sink, knr, k.bits, k.group, False, k.mode == 1, k.normalize) \
+        + side_bytes(vnq, v.n_sink, vnr, v.bits, v.group, v.over_token, v.mode == 1)
     return B * Hkv * per_bh + 2 * B * Hq * D * 2
 
 
@@ -305,8 +312,12 @@ def run_ours(a):
         if world > 1:
             gather_heads(out)  # [L, B, Hq, D] across the KV-head shards
 
+    gsteps = [None]  # graph-mode steps replayed so far (None: eager)
+
     def bytes_now():
-        return sum(layer_bytes(l, B, hkv, hq) for l in layers)
+        # the step about to run: appends one token, then attends
+        n = None if gsteps[0] is None else gsteps[0] + 1
+        return sum(layer_bytes(l, B, hkv, hq, n) for l in layers)
 
     def sync_all():
         torch.cuda.synchronize()
@@ -326,6 +337,81 @@ def run_ours(a):
     stream = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
+    # ---- kernel roofline: attention launches alone (query prep + attention +
+    #      merge), eager, before the cache enters graph mode
+    sync_all()
+    ev0.record(stream)
+    reps = 3
+    for r in range(reps):
+        for li, layer in enumerate(layers):
+            layer.attend(qs[0][li], out=out[li])
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    per_launch_ms = ev0.elapsed_time(ev1) / (reps * L)
+    per_launch_bytes = sum(layer_bytes(l, B, hkv, hq) for l in layers) / L
+    achieved = per_launch_bytes / (per_launch_ms * 1e-3) / 1e9
+
+    # ---- launch mode: the decode step launched from the host each step
+    #      (eager), or recorded once in a CUDA graph (cache graph mode: the
+    #      per-step state comes from a device counter) and replayed.  A few
+    #      timed steps of each decide (max over ranks, same choice on every
+    #      rank): replay wins where host time per layer exceeds device time
+    #      (small batches, many GPUs), eager where the device is the bound.
+    graph = None
+    per_step_launches = None
+    q_in, k_in, v_in = torch.empty_like(qs[0]), torch.empty_like(ks[0]), torch.empty_like(vs[0])
+    trial = 3
+
+    def time_steps(fn, i0):
+        sync_all()
+        ev0.record(stream)
+        for i in range(trial):
+            fn(i0 + i)
+        ev1.record(stream)
+        sync_all()
+        return max_over_ranks(ev0.elapsed_time(ev1)) / trial
+
+    mode_ms = {"eager": time_steps(step, max(3, a.warmup))}
+    eager_step = step
+    if not a.no_graph:
+        gstep = torch.zeros(1, dtype=torch.int64, device=dev)
+        for layer in layers:
+            layer.graph_begin(gstep, 2 * max(3, a.warmup) + 2 * a.steps + 2 * trial + 4)
+        n0 = _lib.launch_count[0]
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(graph, stream=cs):
+                gstep.add_(1)
+                for li, layer in enumerate(layers):
+                    layer.update(k_in[li], v_in[li])
+                    layer.attend(q_in[li], out=out[li])
+                if world > 1:
+                    gather_heads(out)
+        torch.cuda.current_stream().wait_stream(cs)
+        per_step_launches = _lib.launch_count[0] - n0
+        gsteps[0] = 0
+
+        def graph_step(i, q=None, k=None, v=None):
+            q_in.copy_(qs[i % NPOOL] if q is None else q)
+            k_in.copy_(ks[i % NPOOL] if k is None else k)
+            v_in.copy_(vs[i % NPOOL] if v is None else v)
+            graph.replay()
+            gsteps[0] += 1
+
+        for i in range(max(3, a.warmup)):
+            graph_step(i)
+        mode_ms["graph"] = time_steps(graph_step, 0)
+        if mode_ms["graph"] < mode_ms["eager"]:
+            step = graph_step
+        else:  # leave graph mode: the host takes the state back
+            torch.cuda.synchronize()
+            for layer in layers:
+                layer.graph_end(gsteps[0])
+            graph, gsteps[0], per_step_launches = None, None, None
+            step = eager_step
+
     # ---- device-resident timed region
     sampler = ClockSampler(local)
     nbytes = 0
@@ -339,23 +425,10 @@ def run_ours(a):
     ev1.record(stream)
     sync_all()
     clocks = sampler.stop()
-    launches = _lib.launch_count[0] - launches0
+    launches = _lib.launch_count[0] - launches0 if graph is None else per_step_launches * a.steps
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / a.steps
     total_bytes = max_over_ranks(nbytes / a.steps) * world  # ranks hold equal shares
     value = total_bytes / (ms * 1e-3) / 1e9
-
-    # ---- kernel roofline: attention launches alone (attention + its merge)
-    sync_all()
-    ev0.record(stream)
-    reps = 3
-    for r in range(reps):
-        for li, layer in enumerate(layers):
-            layer.attend(qs[0][li], out=out[li])
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    per_launch_ms = ev0.elapsed_time(ev1) / (reps * L)
-    per_launch_bytes = sum(layer_bytes(l, B, hkv, hq) for l in layers) / L
-    achieved = per_launch_bytes / (per_launch_ms * 1e-3) / 1e9
 
     # ---- end to end through the public API with host buffers
     qh = qs[0].cpu().pin_memory()
@@ -411,6 +484,8 @@ def run_ours(a):
                 "head_dim": D, "k_bits": a.kbits, "v_bits": a.vbits, "group": a.group,
                 "v_groups_over": a.v_layout, "mode": a.mode,
                 "parallelism": f"kv-head shards x{world}",
+                "step": "eager launches" if graph is None else "recorded once (CUDA graph), replayed",
+                "step_trial_ms": {k_: round(v_, 3) for k_, v_ in mode_ms.items()},
                 "l2": f"inputs larger than L2 ({total_bytes / 1e9:.1f} GB of cache read per step)",
                 "us_per_layer": round(ms * 1e3 / L, 2),
             },
@@ -468,7 +543,8 @@ def run_c3(a):
         v = torch.randn((B, 8, S - 1, 128), device=dev, generator=g).bfloat16()
         layer.update(k, v)
         del k, v
-    ids = torch.randint(0, cfg.vocab_size, (a.steps + a.warmup + 8, B, 1), device=dev, generator=g)
+    ids = torch.randint(0, cfg.vocab_size, (a.steps + 2 * max(3, a.warmup) + 8, B, 1), device=dev,
+                        generator=g)
     pos0 = S - 1
 
     def step(i):
@@ -480,17 +556,46 @@ def run_c3(a):
         for i in range(max(3, a.warmup)):
             step(i)
         torch.cuda.synchronize()
+        per_step_launches = None
+        if not a.no_graph:
+            # record one decode step of the whole model (cache in graph mode) and
+            # replay it: token ids and positions go into the recorded step's inputs
+            ids_in = torch.empty((B, 1), dtype=torch.long, device=dev)
+            pos_in = torch.empty((B, 1), dtype=torch.long, device=dev)
+            cache.graph_begin(2 * max(3, a.warmup) + a.steps + 4)
+            n0 = _lib.launch_count[0]
+            cs = torch.cuda.Stream(dev)
+            cs.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(cs):
+                with torch.cuda.graph(graph, stream=cs):
+                    cache.graph_advance()
+                    logits_out = model(input_ids=ids_in, past_key_values=cache, position_ids=pos_in,
+                                       use_cache=True).logits
+            torch.cuda.current_stream().wait_stream(cs)
+            per_step_launches = _lib.launch_count[0] - n0
+
+            def step(i):  # noqa: F811 - the recorded step
+                ids_in.copy_(ids[i])
+                pos_in.fill_(pos0 + i)
+                graph.replay()
+                return logits_out
+
+            for i in range(max(3, a.warmup)):
+                step(max(3, a.warmup) + i)
+            torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         sampler = ClockSampler(0)
         sampler.start()
         n0 = _lib.launch_count[0]
+        i0 = max(3, a.warmup) * (1 if per_step_launches is None else 2)
         e0.record()
         for i in range(a.steps):
-            step(max(3, a.warmup) + i)
+            step(i0 + i)
         e1.record()
         torch.cuda.synchronize()
         clocks = sampler.stop()
-        ours = _lib.launch_count[0] - n0
+        ours = _lib.launch_count[0] - n0 if per_step_launches is None else per_step_launches * a.steps
     ms = e0.elapsed_time(e1) / a.steps
     line = {
         "metric": "decode tokens/s (Llama-3-8B-shaped, 4-bit InnerQ cache)", "value": round(B / (ms * 1e-3), 1),
@@ -498,7 +603,8 @@ def run_c3(a):
         "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02), uniform token ids, synthetic cache)",
         "config": {"workload": "C3: full decode step, random-init Llama-3-8B shape", "batch": B,
-                   "context": S, "layers": 32, "k_bits": a.kbits, "v_bits": a.vbits},
+                   "context": S, "layers": 32, "k_bits": a.kbits, "v_bits": a.vbits,
+                   "step": "eager" if a.no_graph else "recorded once (CUDA graph), replayed"},
         "gpu_launches": ours, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define INNERQ_ABI_VERSION 2
+#define INNERQ_ABI_VERSION 3
 
 enum {
   INNERQ_OK = 0,
@@ -136,6 +136,10 @@ typedef struct {
   int32_t group;
   int32_t mode;        /* INNERQ_SYM / INNERQ_ASYM */
   int32_t over_token;  /* 0 for K (channel groups), 1 for V (token groups) */
+  /* Graph mode only (innerq_attn_args.step set), else 0: n_q / n_recent are
+   * the counts at step 0, `recent` is the FIFO buffer base, r0 the window's
+   * FIFO offset at step 0 and flush the side's flush size (0: no quantization). */
+  int32_t r0, flush;
 } innerq_side;
 
 typedef struct {
@@ -149,6 +153,11 @@ typedef struct {
   float softmax_scale; /* the reference consumer uses head_dim^-0.5 */
   int32_t n_splits;    /* 0 = choose for the GPU; else the split-KV count */
   int32_t tile_lo, tile_hi; /* 0,0 = all tiles; else a sub-range (context sharding) */
+  /* Graph mode: device counter of decode steps appended since the state in k
+   * and v (innerq_append_step advances the cache, the caller the counter), so
+   * one recorded CUDA graph serves every step; NULL: the state in k, v is
+   * current.  The split count is fixed when the plan is made. */
+  const int64_t* step;
 } innerq_attn_args;
 
 /* Number of 32-token tiles the fused kernel iterates for these args, and the
@@ -182,6 +191,35 @@ int innerq_decode_attn(const innerq_attn_args* args, void* workspace, int64_t wo
 int innerq_decode_attn_partials(const innerq_attn_args* args, float* part_o, float* part_m,
                                 float* part_l, void* workspace, int64_t workspace_bytes,
                                 void* stream);
+
+/*
+ * One decode-step append of one side in graph mode (cache.py:283-307 then
+ * 314-380: append the new token to the recent window, then quantize and pack
+ * the oldest `flush` tokens when the window holds at least that many), with
+ * the step taken from the device counter `step` (this step counted), so the
+ * launch can be recorded in a CUDA graph once and replayed.  The FIFO and the
+ * packed store must already hold the capacity the replays need.  One launch.
+ */
+typedef struct {
+  int32_t struct_size;  /* sizeof(innerq_append_args) */
+  int32_t dtype, B, H, D;
+  const void* x;        /* the new token [B][H][D] with strides (x_sb, x_sh) */
+  int64_t x_sb, x_sh;
+  void* fifo;           /* recent FIFO buffer [B][H][*][D] */
+  int64_t f_sb, f_sh, f_st;
+  int32_t fifo_cap;     /* tokens the FIFO buffer holds */
+  void* codes;          /* packed store of the side (see innerq_quant_pack) */
+  void* scale;
+  void* zero;
+  int64_t cap_tiles;
+  const void* norm_f;   /* key normalisation factor or NULL */
+  int32_t bits;         /* 1-4, or 16: no quantization (the window only grows) */
+  int32_t group, mode, role, over_token;
+  int32_t flush;        /* the side's flush size */
+  int32_t n_q, n_recent, r0;  /* packed count, window size and its FIFO offset at step 0 */
+} innerq_append_args;
+
+int innerq_append_step(const innerq_append_args* args, const int64_t* step, void* stream);
 
 /* Merge split partials: out[row] = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s,
  * rows = B * rows_per_b, out row (b, h) at b*o_sb + h*o_sh. */

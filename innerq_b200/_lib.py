@@ -21,7 +21,7 @@ EXPORTS = (
     "innerq_abi_version", "innerq_last_error", "innerq_tile_bytes", "innerq_norm_factor",
     "innerq_quant_pack", "innerq_unpack_ref", "innerq_dequant", "innerq_attn_plan",
     "innerq_decode_attn_workspace", "innerq_decode_attn", "innerq_decode_attn_partials",
-    "innerq_lse_merge", "innerq_dequant_ref", "innerq_decode_attn_noalloc",
+    "innerq_lse_merge", "innerq_dequant_ref", "innerq_decode_attn_noalloc", "innerq_append_step",
 )
 
 
@@ -41,6 +41,22 @@ class Side(C.Structure):
         ("recent", C.c_void_p), ("rec_sb", C.c_int64), ("rec_sh", C.c_int64), ("rec_st", C.c_int64),
         ("n_sink", C.c_int32), ("n_q", C.c_int32), ("n_recent", C.c_int32),
         ("bits", C.c_int32), ("group", C.c_int32), ("mode", C.c_int32), ("over_token", C.c_int32),
+        ("r0", C.c_int32), ("flush", C.c_int32),
+    ]
+
+
+class AppendArgs(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_int32), ("dtype", C.c_int32), ("B", C.c_int32), ("H", C.c_int32),
+        ("D", C.c_int32),
+        ("x", C.c_void_p), ("x_sb", C.c_int64), ("x_sh", C.c_int64),
+        ("fifo", C.c_void_p), ("f_sb", C.c_int64), ("f_sh", C.c_int64), ("f_st", C.c_int64),
+        ("fifo_cap", C.c_int32),
+        ("codes", C.c_void_p), ("scale", C.c_void_p), ("zero", C.c_void_p), ("cap_tiles", C.c_int64),
+        ("norm_f", C.c_void_p),
+        ("bits", C.c_int32), ("group", C.c_int32), ("mode", C.c_int32), ("role", C.c_int32),
+        ("over_token", C.c_int32), ("flush", C.c_int32),
+        ("n_q", C.c_int32), ("n_recent", C.c_int32), ("r0", C.c_int32),
     ]
 
 
@@ -53,6 +69,7 @@ class AttnArgs(C.Structure):
         ("k", Side), ("v", Side),
         ("softmax_scale", C.c_float),
         ("n_splits", C.c_int32), ("tile_lo", C.c_int32), ("tile_hi", C.c_int32),
+        ("step", C.c_void_p),
     ]
 
 
@@ -87,13 +104,14 @@ def load() -> C.CDLL:
         "innerq_decode_attn": (i32, [C.POINTER(AttnArgs), vp, i64, vp, i64, i64, vp, vp]),
         "innerq_decode_attn_partials": (i32, [C.POINTER(AttnArgs), vp, vp, vp, vp, i64, vp]),
         "innerq_decode_attn_noalloc": (i32, [C.POINTER(AttnArgs), vp, i64, i64, vp, vp]),
+        "innerq_append_step": (i32, [C.POINTER(AppendArgs), vp, vp]),
         "innerq_lse_merge": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp, i64, i64, vp, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)
         f.restype = res
         f.argtypes = args
-    if lib.innerq_abi_version() != 2:
+    if lib.innerq_abi_version() != 3:
         raise ImportError("libinnerq_b200.so ABI version mismatch; rebuild it")
     _lib = lib
     return lib
@@ -103,7 +121,7 @@ def load() -> C.CDLL:
 KERNELS_PER_CALL = {
     "innerq_norm_factor": 1, "innerq_quant_pack": 1, "innerq_unpack_ref": 1, "innerq_dequant": 1,
     "innerq_dequant_ref": 1, "innerq_decode_attn": 3, "innerq_decode_attn_partials": 2,
-    "innerq_lse_merge": 1, "innerq_decode_attn_noalloc": 3,
+    "innerq_lse_merge": 1, "innerq_decode_attn_noalloc": 3, "innerq_append_step": 1,
 }
 launch_count = [0]
 

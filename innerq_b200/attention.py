@@ -76,7 +76,9 @@ class DecodeAttention:
         self._lib = _lib.load()
 
     def __call__(self, q: torch.Tensor, k: PackedSide, v: PackedSide, scale: float | None = None,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, step: torch.Tensor | None = None) -> torch.Tensor:
+        """step: graph mode (the stores' step-0 state plus the device step
+        counter; the launch can be recorded in a CUDA graph and replayed)."""
         if not q.is_cuda or q.dtype != k.dtype:
             require_cuda(q, "query")
             raise TypeError(f"query dtype {q.dtype} != cache dtype {k.dtype}")
@@ -91,8 +93,10 @@ class DecodeAttention:
         a.q = q.data_ptr()
         a.q_sb, a.q_sh = q.stride(0), q.stride(1)
         a.key_norm = k.norm_f.data_ptr() if (k.normalize and k.norm_f is not None and k.n_q) else None
-        k.fill_side(a.k)
-        v.fill_side(a.v)
+        graph = step is not None
+        k.fill_side(a.k, graph)
+        v.fill_side(a.v, graph)
+        a.step = step.data_ptr() if graph else None
         a.softmax_scale = float(scale if scale is not None else 1.0 / math.sqrt(D))
         ref = C.byref(a)
         ws_bytes = self._lib.innerq_decode_attn_workspace(ref)

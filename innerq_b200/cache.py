@@ -45,6 +45,7 @@ class InnerqDynamicLayer(CacheLayerMixin):
         self.cumulative_length = 0
         self.fused = bool(getattr(config, "_attn_implementation", None) == "innerq")
         self._attn = None
+        self._gstep = None  # graph mode: the cache's device step counter
         super().__init__()
 
     # cache.py:70-119
@@ -163,6 +164,12 @@ class InnerqDynamicLayer(CacheLayerMixin):
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor,
                cache_kwargs: dict[str, Any] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         """cache.py:382-396."""
+        if self._gstep is not None:
+            # graph mode: one append launch per side, state on the device
+            self._k.append_graph(key_states, self._gstep)
+            self._v.append_graph(value_states, self._gstep)
+            key_states._innerq_layer = self
+            return key_states, value_states
         self.cumulative_length += key_states.shape[-2]
         if not self.is_initialized:
             self.lazy_initialization(key_states, value_states)
@@ -173,6 +180,23 @@ class InnerqDynamicLayer(CacheLayerMixin):
             key_states._innerq_layer = self
             return key_states, value_states
         return self.get_deq_tensors()
+
+    # ------------------------------------------------------------ graph mode
+    def graph_begin(self, step: torch.Tensor, max_steps: int) -> None:
+        """Enter graph mode (see DynamicCache.graph_begin)."""
+        if not (self.is_initialized and self.fused and self._fusable()):
+            raise NotImplementedError("graph mode needs a prefilled layer on the fused attention path")
+        if isinstance(self._k, HybridSide) or isinstance(self._v, HybridSide):
+            raise NotImplementedError("graph mode does not cover hybrid stores")
+        self._k.graph_begin(max_steps)
+        self._v.graph_begin(max_steps)
+        self._gstep = step
+
+    def graph_end(self, n_steps: int) -> None:
+        self._k.graph_end(n_steps)
+        self._v.graph_end(n_steps)
+        self.cumulative_length += n_steps
+        self._gstep = None
 
     def _fusable(self) -> bool:
         """Both stores are in layouts the fused kernel reads: channel-grouped
@@ -190,7 +214,7 @@ class InnerqDynamicLayer(CacheLayerMixin):
         if self._attn is None:
             from .attention import DecodeAttention
             self._attn = DecodeAttention()
-        out_ = self._attn(query, self._k, self._v, scaling, out=out)
+        out_ = self._attn(query, self._k, self._v, scaling, out=out, step=self._gstep)
         # the launcher reuses its buffer on the next step: hand out a copy-free
         # view only when the caller gave the destination
         return out_ if (out is not None or reuse) else out_.clone()
@@ -282,6 +306,35 @@ class DynamicCache(Cache):
                     layers.append(InnerqDynamicLayer(config=config, layer_idx=layer_idx))
         super().__init__(layers=layers, offloading=offloading,
                          offload_only_non_sliding=offload_only_non_sliding)
+
+    # ------------------------------------------------------------ graph mode
+    def graph_begin(self, max_steps: int) -> torch.Tensor:
+        """Switch every layer to graph mode for up to `max_steps` decode steps:
+        the stores reserve the capacity those steps need, and each step's
+        appends and attention read the step from a device counter instead of
+        from host-side arguments, so a recorded decode step (a CUDA graph)
+        replays correctly step after step.  Each recorded step must begin with
+        graph_advance().  Returns the counter (int64, 1 element)."""
+        layers = [l for l in self.layers if getattr(l, "is_initialized", False)]
+        if not layers:
+            raise RuntimeError("graph mode needs a prefilled cache")
+        self._gstep = torch.zeros(1, dtype=torch.int64, device=layers[0].device)
+        for layer in layers:
+            layer.graph_begin(self._gstep, max_steps)
+        return self._gstep
+
+    def graph_advance(self) -> None:
+        """The first operation of every graph-mode decode step."""
+        self._gstep.add_(1)
+
+    def graph_end(self) -> int:
+        """Leave graph mode; returns the number of steps taken."""
+        n = int(self._gstep.item())
+        for layer in self.layers:
+            if getattr(layer, "_gstep", None) is not None:
+                layer.graph_end(n)
+        self._gstep = None
+        return n
 
     def __iter__(self):
         for layer in self.layers:

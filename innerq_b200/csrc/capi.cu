@@ -55,13 +55,16 @@ int sm_count() {
   return cached[dev];
 }
 
+// a side with a packed part now, or one that will pack during graph-mode steps
+inline bool packed(const innerq_side& s) { return s.n_q > 0 || s.flush > 0; }
+
 struct Plan {
   int S, t_first, n_tiles, tile_lo, tile_hi, n_splits, tps, R, bk, bv;
 };
 
 int check_side(const innerq_side& s, int dtype, int role, const char* name) {
   if (s.n_sink < 0 || s.n_q < 0 || s.n_recent < 0) return fail(INNERQ_ERR_ARG, "%s: negative count", name);
-  if (s.n_q > 0) {
+  if (packed(s)) {
     int rc = check_common(dtype, kD, s.bits, s.group, s.mode, role, s.over_token);
     if (rc) return rc;
     if (s.bits < 2) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: %s bits %d (2, 3, 4)", name, s.bits);
@@ -100,7 +103,7 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   rc = check_side(a->v, a->dtype, INNERQ_ROLE_V, "v");
   if (rc) return rc;
   // values grouped over channels share the keys' channel-group count
-  if (a->v.n_q > 0 && !a->v.over_token && a->k.n_q > 0 && a->v.group != a->k.group)
+  if (packed(a->v) && !a->v.over_token && packed(a->k) && a->v.group != a->k.group)
     return fail(INNERQ_ERR_UNSUPPORTED,
                 "fused attention: channel-grouped values need the keys' group size (%d vs %d; use innerq_dequant)",
                 a->v.group, a->k.group);
@@ -110,7 +113,7 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   if (Sk > (1ll << 30)) return fail(INNERQ_ERR_ARG, "context too long");
   p.S = (int)Sk;
   const int vs = a->v.n_sink;
-  p.t_first = a->v.n_q > 0 ? vs - 32 * ((vs + 31) / 32) : 0;
+  p.t_first = packed(a->v) ? vs - 32 * ((vs + 31) / 32) : 0;
   p.n_tiles = (p.S - p.t_first + 31) / 32;
   p.tile_lo = a->tile_lo, p.tile_hi = a->tile_hi;
   if (p.tile_lo == 0 && p.tile_hi == 0) p.tile_hi = p.n_tiles;
@@ -136,8 +139,8 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   if (splits > 65535) splits = 65535;
   p.tps = ntr > 0 ? (ntr + splits - 1) / splits : 1;
   p.n_splits = ntr > 0 ? (ntr + p.tps - 1) / p.tps : 1;
-  p.bk = a->k.n_q > 0 ? a->k.bits : 4;
-  p.bv = a->v.n_q > 0 ? a->v.bits : 4;
+  p.bk = packed(a->k) ? a->k.bits : 4;
+  p.bv = packed(a->v) ? a->v.bits : 4;
   return INNERQ_OK;
 }
 
@@ -152,9 +155,11 @@ DevSide dev_side(const innerq_side& s) {
   d.rec = (const uint16_t*)s.recent;
   d.rc_b = s.rec_sb; d.rc_h = s.rec_sh; d.rc_t = s.rec_st;
   d.n_sink = s.n_sink; d.n_q = s.n_q; d.n_rec = s.n_recent;
-  d.group = s.n_q > 0 ? s.group : 32;
-  d.asym = s.n_q > 0 && s.mode == INNERQ_ASYM;
+  d.group = packed(s) ? s.group : 32;
+  d.asym = packed(s) && s.mode == INNERQ_ASYM;
   d.chan = 0;
+  d.r0 = s.r0;
+  d.flush = s.flush;
   return d;
 }
 
@@ -174,7 +179,7 @@ int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm,
   DevArgs d;
   d.k = dev_side(a->k);
   d.v = dev_side(a->v);
-  d.v.chan = a->v.n_q > 0 && !a->v.over_token;
+  d.v.chan = packed(a->v) && !a->v.over_token;
   d.q = (const uint16_t*)a->q;
   d.q_b = a->q_sb;
   d.q_h = a->q_sh;
@@ -185,18 +190,27 @@ int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm,
   d.tiles_per_split = p.tps; d.n_splits = p.n_splits;
   d.scale_log2 = a->softmax_scale * 1.4426950408889634f;
   d.po = po; d.pm = pm; d.pl = pl;
+  d.step = a->step;
   d.qprep = qprep;
   d.R = p.R;
   dim3 grid(p.n_splits, a->Hkv, a->B);
   const int rp = p.R <= 4 ? 4 : 8;
-  const int ng = a->k.n_q > 0 ? kD / a->k.group : (d.v.chan ? kD / a->v.group : 4);
+  const int ng = packed(a->k) ? kD / a->k.group : (d.v.chan ? kD / a->v.group : 4);
   const bool bf = a->dtype == INNERQ_DT_BF16;
   cudaError_t e = launch_qprep(d, rp, ng, bf, st);
   if (e != cudaSuccess) return cuda_status(e, "qprep");
-  switch (p.bk) {
-    case 2: e = bf ? launch_attn_k2_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k2_f16(d, p.bv, rp, ng, grid, st); break;
-    case 3: e = bf ? launch_attn_k3_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k3_f16(d, p.bv, rp, ng, grid, st); break;
-    default: e = bf ? launch_attn_k4_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k4_f16(d, p.bv, rp, ng, grid, st); break;
+  if (a->step) {  // graph mode: separate instantiations
+    switch (p.bk) {
+      case 2: e = bf ? launch_attn_k2_bf16_graph(d, p.bv, rp, ng, grid, st) : launch_attn_k2_f16_graph(d, p.bv, rp, ng, grid, st); break;
+      case 3: e = bf ? launch_attn_k3_bf16_graph(d, p.bv, rp, ng, grid, st) : launch_attn_k3_f16_graph(d, p.bv, rp, ng, grid, st); break;
+      default: e = bf ? launch_attn_k4_bf16_graph(d, p.bv, rp, ng, grid, st) : launch_attn_k4_f16_graph(d, p.bv, rp, ng, grid, st); break;
+    }
+  } else {
+    switch (p.bk) {
+      case 2: e = bf ? launch_attn_k2_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k2_f16(d, p.bv, rp, ng, grid, st); break;
+      case 3: e = bf ? launch_attn_k3_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k3_f16(d, p.bv, rp, ng, grid, st); break;
+      default: e = bf ? launch_attn_k4_bf16(d, p.bv, rp, ng, grid, st) : launch_attn_k4_f16(d, p.bv, rp, ng, grid, st); break;
+    }
   }
   return cuda_status(e, "decode_attn");
 }
@@ -350,6 +364,46 @@ int innerq_decode_attn(const innerq_attn_args* args, void* workspace, int64_t wo
   return cuda_status(launch_lse_merge(po, pm, pl, args->B * args->Hq, args->Hq, p.n_splits,
                                       args->dtype, out, o_sb, o_sh, lse, (cudaStream_t)stream),
                      "lse_merge");
+}
+
+int innerq_append_step(const innerq_append_args* a, const int64_t* step, void* stream) {
+  if (!a) return fail(INNERQ_ERR_ARG, "null args");
+  if (a->struct_size != (int32_t)sizeof(innerq_append_args))
+    return fail(INNERQ_ERR_ARG, "struct_size %d != %d (ABI mismatch)", a->struct_size,
+                (int)sizeof(innerq_append_args));
+  if (a->dtype != INNERQ_DT_F16 && a->dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype");
+  if (a->D != kD) return fail(INNERQ_ERR_UNSUPPORTED, "head_dim %d (only 128 is built)", a->D);
+  if (a->B <= 0 || a->H <= 0 || a->B > 65535 || a->H > 65535) return fail(INNERQ_ERR_ARG, "B, H");
+  if (!step || !a->x || !a->fifo) return fail(INNERQ_ERR_ARG, "null pointer");
+  if (a->n_q < 0 || a->n_recent < 0 || a->r0 < 0 || a->r0 + a->n_recent > a->fifo_cap)
+    return fail(INNERQ_ERR_ARG, "FIFO state outside its buffer");
+  AppendArgs g;
+  g.x = a->x; g.x_sb = a->x_sb; g.x_sh = a->x_sh;
+  g.fifo = a->fifo; g.f_sb = a->f_sb; g.f_sh = a->f_sh; g.f_st = a->f_st; g.fifo_cap = a->fifo_cap;
+  g.codes = a->codes; g.scale = a->scale; g.zero = a->zero; g.cap_tiles = a->cap_tiles;
+  g.norm_f = a->norm_f;
+  g.dt = a->dtype; g.B = a->B; g.H = a->H; g.bits = a->bits; g.group = a->group;
+  g.asym = a->mode == INNERQ_ASYM; g.flush = a->flush;
+  g.n_q = a->n_q; g.n_rec = a->n_recent; g.r0 = a->r0;
+  if (a->bits == 16) {
+    g.mode = 3;
+  } else {
+    int rc = check_common(a->dtype, a->D, a->bits, a->group, a->mode, a->role, a->over_token);
+    if (rc) return rc;
+    if (a->flush <= 0) return fail(INNERQ_ERR_ARG, "flush %d", a->flush);
+    if (!a->codes || !a->scale || (a->mode == INNERQ_ASYM && !a->zero))
+      return fail(INNERQ_ERR_ARG, "null store pointer");
+    if (a->over_token) {
+      if (a->flush % a->group || a->n_q % a->group)
+        return fail(INNERQ_ERR_ARG, "token groups need flush (%d) and n_q (%d) divisible by group %d",
+                    a->flush, a->n_q, a->group);
+      g.mode = 1;
+    } else {
+      if (a->norm_f && a->role == INNERQ_ROLE_V) return fail(INNERQ_ERR_ARG, "normalised values");
+      g.mode = a->role == INNERQ_ROLE_V ? 2 : 0;
+    }
+  }
+  return cuda_status(launch_append_step(g, step, (cudaStream_t)stream), "append_step");
 }
 
 int innerq_lse_merge(const float* part_o, const float* part_m, const float* part_l, int B,

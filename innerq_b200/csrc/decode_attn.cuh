@@ -56,7 +56,24 @@ struct DevSide {
   int group;
   int asym;
   int chan;   // values grouped over channels (scales per token and channel group)
+  // graph mode (DevArgs::step set): n_q / n_rec are the counts at step 0, rec
+  // the FIFO base, r0 the window's FIFO offset at step 0, flush the flush size
+  int r0, flush;
 };
+
+// A side's geometry after n decode steps of graph mode: each step appends one
+// token to the recent FIFO, then flushes `flush` tokens whenever it holds at
+// least that many (at most one flush per step), so after n steps
+// min(n, (n_rec0 + n) / flush) flushes have happened.
+struct SideNow { int nq, nrec, r0; };
+__device__ __forceinline__ SideNow side_after(const DevSide& s, int n) {
+  SideNow o;
+  const int k = s.flush > 0 ? min(n, (s.n_rec + n) / s.flush) : 0;
+  o.nq = s.n_q + s.flush * k;
+  o.nrec = s.n_rec + n - s.flush * k;
+  o.r0 = s.r0 + s.flush * k;
+  return o;
+}
 
 struct DevArgs {
   DevSide k, v;
@@ -72,6 +89,7 @@ struct DevArgs {
   float* po;           // [B][Hq][n_splits][D]
   float* pm;           // [B][Hq][n_splits]
   float* pl;
+  const int64_t* step;  // graph mode: device count of decode steps taken (else null)
 };
 
 constexpr int kWarps = 4;
@@ -256,20 +274,22 @@ __device__ __forceinline__ void load16(float2 out[8], const uint16_t* p) {
 __device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 
 // dense (fp16 / bf16) row pointer for token t of a side, or null
-__device__ __forceinline__ const uint16_t* dense_row(const DevSide& s, int b, int h, int t, int S) {
+// (nq: the side's packed count now; r0: FIFO offset of the recent window)
+__device__ __forceinline__ const uint16_t* dense_row(const DevSide& s, int b, int h, int t, int S, int nq,
+                                                     int r0) {
   if (t < 0 || t >= S) return nullptr;
   if (t < s.n_sink) return s.sink + b * s.sk_b + h * s.sk_h + (int64_t)t * s.sk_t;
-  const int r = t - s.n_sink - s.n_q;
-  if (r >= 0) return s.rec + b * s.rc_b + h * s.rc_h + (int64_t)r * s.rc_t;
+  const int r = t - s.n_sink - nq;
+  if (r >= 0) return s.rec + b * s.rc_b + h * s.rc_h + (int64_t)(r + r0) * s.rc_t;
   return nullptr;
 }
 
 
 // a tile whose 32 K rows and 32 V rows all sit in the packed stores, both
 // tile-aligned: it is staged by the bulk-copy ring
-__device__ __forceinline__ bool is_fast_tile(const DevArgs& a, int tile) {
+__device__ __forceinline__ bool is_fast_tile(const DevArgs& a, int nqk, int nqv, int tile) {
   const int t0 = a.t_first + tile * kTile;
-  const int ks = a.k.n_sink, nqk = a.k.n_q, vs = a.v.n_sink, nqv = a.v.n_q;
+  const int ks = a.k.n_sink, vs = a.v.n_sink;
   return nqk > 0 && t0 >= ks && t0 + kTile <= ks + nqk && ((t0 - ks) & 31) == 0 && nqv > 0 &&
          t0 >= vs && t0 + kTile <= vs + nqv;
 }
@@ -307,6 +327,7 @@ struct AttnStatic {
   uint8_t pd_s[kWarps][RP][2][kTile];
   float cm_s[kWarps][RP];
   float cl_s[kWarps][RP];
+  int geo[5];                 // graph mode: this step's S, packed K / V counts, K / V FIFO offsets
 };
 
 // balanced base-256 digits of an integer |v| < 2^23: v = d2*65536 + d1*256 + d0
@@ -466,8 +487,10 @@ __device__ __forceinline__ void load_kscales(float2 out[2][NG], const uint16_t* 
 // BK/BV: code bits; RP: query heads per KV head padded to 4 or 8; DT: dtype;
 // NG: K channel groups per token (4, 2, 1 for groups of 32, 64, 128); VCH:
 // values grouped over channels too (same group size as the keys) instead of
-// over tokens
-template <int BK, int BV, int RP, int DT, int NG, int VCH>
+// over tokens; GM: graph mode (geometry from the device step counter; a
+// separate instantiation, because carrying that path costs the argument-fed
+// kernel ~10% through register allocation)
+template <int BK, int BV, int RP, int DT, int NG, int VCH, int GM>
 __global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 3)
 decode_attn_kernel(const DevArgs a) {
   constexpr int NT = RP / 4;
@@ -479,11 +502,23 @@ decode_attn_kernel(const DevArgs a) {
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
   const int R = a.R;
-  const int tile_beg = a.tile_lo + split * a.tiles_per_split;
-  const int tile_end = min(tile_beg + a.tiles_per_split, a.tile_hi);
-  const int S = a.S;
-  const int ks = a.k.n_sink, nqk = a.k.n_q;
-  const int vs = a.v.n_sink, nqv = a.v.n_q;
+  // this step's geometry: from the arguments, or in graph mode from the
+  // device step counter (the grid, i.e. the split count, stays fixed)
+  int S = a.S, nqk = a.k.n_q, nqv = a.v.n_q, kr0 = 0, vr0 = 0;
+  int tile_lo = a.tile_lo, tile_hi = a.tile_hi, tps = a.tiles_per_split;
+  if constexpr (GM) {
+    const int n = (int)*a.step;
+    const SideNow kn = side_after(a.k, n), vn = side_after(a.v, n);
+    nqk = kn.nq; nqv = vn.nq; kr0 = kn.r0; vr0 = vn.r0;
+    S = a.k.n_sink + kn.nq + kn.nrec;
+    tile_lo = 0;
+    tile_hi = (S - a.t_first + kTile - 1) / kTile;
+    tps = (tile_hi + a.n_splits - 1) / a.n_splits;
+  }
+  const int tile_beg = tile_lo + split * tps;
+  const int tile_end = min(tile_beg + tps, tile_hi);
+  const int ks = a.k.n_sink;
+  const int vs = a.v.n_sink;
   const int kasym = a.k.asym, vasym = a.v.asym;
   const int SB = stage_bytes(BK, BV, NG, kasym, vasym);
   const int koff = kasym ? 0 : (1 << (BK - 1));
@@ -571,7 +606,8 @@ decode_attn_kernel(const DevArgs a) {
 
   // dense-K B fragments are needed only by CTAs that meet a sink / recent /
   // seam tile (packed tiles form one contiguous run)
-  const bool any_dense = tile_end > tile_beg && !(is_fast_tile(a, tile_beg) && is_fast_tile(a, tile_end - 1));
+  const bool any_dense =
+      tile_end > tile_beg && !(is_fast_tile(a, nqk, nqv, tile_beg) && is_fast_tile(a, nqk, nqv, tile_end - 1));
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.bars[s], 1);
@@ -591,6 +627,11 @@ decode_attn_kernel(const DevArgs a) {
     bulk_g2s(&sm.qp, src, kH, &sm.prep_bar);
     if (any_dense) bulk_g2s(&sm.qp.bd, src + kH, kDn, &sm.prep_bar);
   }
+  if constexpr (GM) {
+    // the tile loop reads the step's geometry from shared memory (kept in
+    // registers across the loop it spills)
+    if (threadIdx.x == 0) { sm.geo[0] = S; sm.geo[1] = nqk; sm.geo[2] = nqv; sm.geo[3] = kr0; sm.geo[4] = vr0; }
+  }
   __syncthreads();  // barrier initialisation is visible to every thread
   bool failed = !mbar_wait_bounded(&sm.prep_bar, 0, kWaitLimit);
   int i_done = 0;
@@ -609,6 +650,13 @@ decode_attn_kernel(const DevArgs a) {
 
   // ---------------------------------------------------------------- tiles
 #pragma unroll 1
+  // this step's geometry inside the loop: launch arguments, or (graph mode)
+  // shared memory
+  auto gS = [&]() -> int { if constexpr (GM) return sm.geo[0]; else return a.S; };
+  auto gNQK = [&]() -> int { if constexpr (GM) return sm.geo[1]; else return a.k.n_q; };
+  auto gNQV = [&]() -> int { if constexpr (GM) return sm.geo[2]; else return a.v.n_q; };
+  auto gKR0 = [&]() -> int { if constexpr (GM) return sm.geo[3]; else return 0; };
+  auto gVR0 = [&]() -> int { if constexpr (GM) return sm.geo[4]; else return 0; };
   for (int i = 0; i < (failed ? 0 : n_st); ++i) {
     const int slot = i % kStages;
     if (!mbar_wait_bounded(&sm.bars[slot], (uint32_t)((i / kStages) & 1), kWaitLimit)) {
@@ -651,8 +699,9 @@ decode_attn_kernel(const DevArgs a) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int t = t0 + gid + 8 * j;
-        src[j] = (t < 0 || t >= S) ? 0 : ((t >= ks && t < ks + nqk) ? 1 : 2);
+        src[j] = (t < 0 || t >= gS()) ? 0 : ((t >= ks && t < ks + gNQK()) ? 1 : 2);
       }
+      const int S = gS(), nqk = gNQK();
       const int lo_t = max(t0, 0), hi_t = min(t0 + kTile, S);
       const bool kp_any = nqk > 0 && lo_t < ks + nqk && hi_t > ks;
       const bool kd_any = (lo_t < min(ks, hi_t)) || (hi_t > max(ks + nqk, lo_t));
@@ -699,7 +748,7 @@ decode_attn_kernel(const DevArgs a) {
       if (kd_any) {
         const uint16_t* rp[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) rp[j] = src[j] == 2 ? dense_row(a.k, b, hk, t0 + gid + 8 * j, S) : nullptr;
+        for (int j = 0; j < 4; ++j) rp[j] = src[j] == 2 ? dense_row(a.k, b, hk, t0 + gid + 8 * j, S, nqk, gKR0()) : nullptr;
 #pragma unroll
         for (int kb = 0; kb < 8; ++kb)
 #pragma unroll
@@ -734,6 +783,7 @@ decode_attn_kernel(const DevArgs a) {
     }
 
     // ------------------------------------------------------------ softmax
+    const int nqv = gNQV();
     const bool vpacked = nqv > 0 && t0 >= vs && t0 + kTile <= vs + nqv;
     // channel-grouped values may end inside a tile: its packed rows take the
     // packed path and its dense rows the dense path
@@ -920,8 +970,9 @@ decode_attn_kernel(const DevArgs a) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int t = t0 + rr[u];
+          const int S = gS();
           const bool dense = t >= 0 && t < S && !(t >= vs && t < vs + nqv);
-          vp[kb][u] = dense ? dense_row(a.v, b, hk, t, S) : nullptr;
+          vp[kb][u] = dense ? dense_row(a.v, b, hk, t, S, nqv, gVR0()) : nullptr;
         }
       }
 #pragma unroll

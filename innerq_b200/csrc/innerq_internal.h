@@ -39,7 +39,24 @@ INNERQ_DECL_ATTN(launch_attn_k3_f16)
 INNERQ_DECL_ATTN(launch_attn_k3_bf16)
 INNERQ_DECL_ATTN(launch_attn_k4_f16)
 INNERQ_DECL_ATTN(launch_attn_k4_bf16)
+INNERQ_DECL_ATTN(launch_attn_k2_f16_graph)
+INNERQ_DECL_ATTN(launch_attn_k2_bf16_graph)
+INNERQ_DECL_ATTN(launch_attn_k3_f16_graph)
+INNERQ_DECL_ATTN(launch_attn_k3_bf16_graph)
+INNERQ_DECL_ATTN(launch_attn_k4_f16_graph)
+INNERQ_DECL_ATTN(launch_attn_k4_bf16_graph)
 #undef INNERQ_DECL_ATTN
+// graph-mode decode append of one side (quant_pack.cu); mode 0: channel
+// groups / row layout, 1: token groups / col layout, 2: channel groups / col
+// layout, 3: no quantization
+struct AppendArgs {
+  const void* x; int64_t x_sb, x_sh;
+  void* fifo; int64_t f_sb, f_sh, f_st; int fifo_cap;
+  void* codes; void* scale; void* zero; int64_t cap_tiles;
+  const void* norm_f;
+  int dt, B, H, bits, group, asym, mode, flush, n_q, n_rec, r0;
+};
+cudaError_t launch_append_step(const AppendArgs& a, const int64_t* step, cudaStream_t s);
 // the query-prep pass that precedes every attention launch (qprep.cu)
 cudaError_t launch_qprep(const DevArgs& a, int rp, int ng, int bf16, cudaStream_t s);
 int64_t qprep_bytes(int rp);  // one (batch, KV head) block

@@ -225,22 +225,21 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
 // Col layout, token groups (V): one CTA of 128 threads (one per dim) per
 // group of `group` tokens.
 // --------------------------------------------------------------------------
+// One group of `group` tokens of pair bh (x0: its first token, dim 0; token
+// stride st), stored at packed position t_abs; 128 threads, one per dim.
 template <int DT, int BITS, int ROLEV>
-__global__ void __launch_bounds__(128)
-pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st,
-                      int group, int asym, uint8_t* __restrict__ codes,
-                      uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
-                      int64_t cap_tiles, int64_t t_off) {
+__device__ __forceinline__ void pack_col_group(const uint16_t* __restrict__ x0, int64_t st, int group,
+                                               int asym, uint8_t* __restrict__ codes,
+                                               uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
+                                               int64_t cap_tiles, int64_t t_abs, int64_t bh) {
   // col layout (values), 2-4 bits: codes per dim as words of 4 tokens,
   // [dim][token/4] (+1 pad word: conflict-free); otherwise [token][dim] bytes
   constexpr bool kWords = ROLEV && BITS >= 2;
   __shared__ uint8_t cb[kWords ? 1 : 128][kWords ? 1 : kD];
   __shared__ uint32_t cbt[kWords ? kD : 1][kWords ? 33 : 1];
   __shared__ __align__(16) uint32_t tw[kWords ? 4 : 4 * tile_bytes(4) / 4];
-  const int gi = blockIdx.x, h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
-  const int64_t bh = (int64_t)b * H + h;
   const int d = threadIdx.x;
-  const uint16_t* xp = x + b * sb + h * sh + (int64_t)gi * group * st + d;
+  const uint16_t* xp = x0 + d;
   float s, z = 0.f;
   if (!asym) {
     float mx = 0.f;
@@ -284,7 +283,7 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
     }
   }
   const int64_t groups_cap = cap_tiles * 32 / group;
-  const int64_t gglob = (t_off + (int64_t)gi * group) / group;
+  const int64_t gglob = t_abs / group;
   const int64_t si = (bh * groups_cap + gglob) * kD + col_scale_idx(d);
   scale[si] = from_f<DT>(s);
   if (asym) zero[si] = from_f<DT>(z);
@@ -294,7 +293,7 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
   if constexpr (kWords) {
     // every word of the group's tiles from 2-8 word loads of 4 tokens' codes
     // (the col-layout map of common.cuh); stored straight to global memory
-    const int64_t ti0 = (t_off + (int64_t)gi * group) / 32;
+    const int64_t ti0 = t_abs / 32;
     uint32_t* dst = reinterpret_cast<uint32_t*>(codes + (bh * cap_tiles + ti0) * tile_bytes(BITS));
     for (int i = threadIdx.x; i < n_tiles * TW; i += blockDim.x) {
       const int k = i / TW, wi = i % TW;
@@ -348,10 +347,76 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
     }
   }
   __syncthreads();
-  const int64_t ti0 = (t_off + (int64_t)gi * group) / 32;
+  const int64_t ti0 = t_abs / 32;
   uint4* dst = reinterpret_cast<uint4*>(codes + (bh * cap_tiles + ti0) * tile_bytes(BITS));
   const uint4* src = reinterpret_cast<const uint4*>(tw);
   for (int i = threadIdx.x; i < n_tiles * TW / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+template <int DT, int BITS, int ROLEV>
+__global__ void __launch_bounds__(128)
+pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st,
+                      int group, int asym, uint8_t* __restrict__ codes,
+                      uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
+                      int64_t cap_tiles, int64_t t_off) {
+  const int gi = blockIdx.x, h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
+  pack_col_group<DT, BITS, ROLEV>(x + b * sb + h * sh + (int64_t)gi * group * st, st, group, asym, codes,
+                                  scale, zero, cap_tiles, t_off + (int64_t)gi * group, (int64_t)b * H + h);
+}
+
+// --------------------------------------------------------------------------
+// Graph-mode decode append of one side (cache.py:283-307, 314-380): the new
+// token goes to the recent FIFO; when the window then holds >= flush tokens
+// the oldest `flush` are quantized and packed.  The step comes from a device
+// counter (steps taken, this one included) and the state at step 0, so the
+// launch replays from a CUDA graph.  Grid (H, B), 128 threads.
+// MODE 0: channel groups, row layout (keys); 1: token groups, col layout
+// (values); 2: channel groups, col layout (values); 3: no quantization.
+// --------------------------------------------------------------------------
+struct AppendDev {
+  const uint16_t* x;
+  int64_t x_b, x_h;
+  uint16_t* fifo;
+  int64_t f_b, f_h, f_t;
+  int fifo_cap;
+  uint8_t* codes;
+  uint16_t* scale;
+  uint16_t* zero;
+  int64_t cap_tiles;
+  const uint16_t* nf;
+  int group, asym, flush, n_q, n_rec, r0;
+};
+
+template <int DT, int BITS, int MODE>
+__global__ void __launch_bounds__(128) append_step_kernel(const AppendDev a, const int64_t* __restrict__ step) {
+  __shared__ uint32_t seg_unused[16];
+  const int h = blockIdx.x, b = blockIdx.y, H = gridDim.x, d = threadIdx.x;
+  const int64_t bh = (int64_t)b * H + h;
+  const int n1 = (int)*step, n0 = n1 - 1;
+  uint16_t* fifo = a.fifo + b * a.f_b + h * a.f_h;
+  const int pos = a.r0 + a.n_rec + n0;
+  if (pos < a.fifo_cap) fifo[(int64_t)pos * a.f_t + d] = a.x[b * a.x_b + h * a.x_h + d];
+  if (MODE == 3) return;
+  const int k0 = min(n0, (a.n_rec + n0) / a.flush), k1 = min(n1, (a.n_rec + n1) / a.flush);
+  if (k1 == k0) return;
+  const int f0 = a.r0 + a.flush * k0;
+  const int64_t t0 = (int64_t)a.n_q + (int64_t)a.flush * k0;
+  if (f0 + a.flush > a.fifo_cap || t0 + a.flush > a.cap_tiles * 32) return;  // beyond the reserved capacity
+  __syncthreads();  // the new token may be one of those flushed
+  if (MODE == 1) {
+    for (int g = 0; g < a.flush; g += a.group) {
+      pack_col_group<DT, BITS, 1>(fifo + (int64_t)(f0 + g) * a.f_t, a.f_t, a.group, a.asym, a.codes, a.scale,
+                                  a.zero, a.cap_tiles, t0 + g, bh);
+      __syncthreads();
+    }
+  } else {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = warp; i < a.flush; i += 4) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(fifo + (int64_t)(f0 + i) * a.f_t + 4 * lane);
+      pack_row_token<DT, BITS, MODE == 2 ? 1 : 0>(raw, i, bh, lane, seg_unused, a.nf, a.group, a.asym, a.codes,
+                                                  a.scale, a.zero, a.cap_tiles, t0);
+    }
+  }
 }
 
 // --------------------------------------------------------------------------
@@ -527,6 +592,24 @@ cudaError_t launch_norm_factor(const void* x, int dt, int B, int H, int T, int64
                                int64_t st, void* f, cudaStream_t s) {
   DT_DISPATCH(dt, norm_factor_kernel<DTC><<<B * H, kD, 0, s>>>(
                       (const uint16_t*)x, sb, sh, st, H, T, (uint16_t*)f));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_append_step(const AppendArgs& g, const int64_t* step, cudaStream_t s) {
+  AppendDev a;
+  a.x = (const uint16_t*)g.x; a.x_b = g.x_sb; a.x_h = g.x_sh;
+  a.fifo = (uint16_t*)g.fifo; a.f_b = g.f_sb; a.f_h = g.f_sh; a.f_t = g.f_st; a.fifo_cap = g.fifo_cap;
+  a.codes = (uint8_t*)g.codes; a.scale = (uint16_t*)g.scale; a.zero = (uint16_t*)g.zero;
+  a.cap_tiles = g.cap_tiles; a.nf = (const uint16_t*)g.norm_f;
+  a.group = g.group; a.asym = g.asym; a.flush = g.flush; a.n_q = g.n_q; a.n_rec = g.n_rec; a.r0 = g.r0;
+  const dim3 grid((unsigned)g.H, (unsigned)g.B, 1);
+  const int dt = g.dt, bits = g.bits;
+  switch (g.mode) {
+    case 0: DT_DISPATCH(dt, BITS_DISPATCH(bits, append_step_kernel<DTC, BC, 0><<<grid, 128, 0, s>>>(a, step))); break;
+    case 1: DT_DISPATCH(dt, BITS_DISPATCH(bits, append_step_kernel<DTC, BC, 1><<<grid, 128, 0, s>>>(a, step))); break;
+    case 2: DT_DISPATCH(dt, BITS_DISPATCH(bits, append_step_kernel<DTC, BC, 2><<<grid, 128, 0, s>>>(a, step))); break;
+    default: DT_DISPATCH(dt, (append_step_kernel<DTC, 4, 3><<<grid, 128, 0, s>>>(a, step))); break;
+  }
   return cudaGetLastError();
 }
 

@@ -33,7 +33,9 @@ def innerq_attention_forward(module, query, key, value, attention_mask, dropout:
     layer = getattr(key, "_innerq_layer", None)
     if layer is not None:
         key._innerq_layer = None
-        if query.shape[2] == 1 and _trivial_mask(attention_mask):
+        # graph mode (a recorded decode step) is single-token decode without
+        # padding by contract; checking the mask would synchronise the host
+        if query.shape[2] == 1 and (layer._gstep is not None or _trivial_mask(attention_mask)):
             out = layer.attend(query, scaling, reuse=True)  # [B, Hq, D]
             return out.unsqueeze(1), None                # [B, q_len=1, Hq, D]
         key, value = layer.get_deq_tensors()

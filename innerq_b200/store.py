@@ -77,6 +77,7 @@ class PackedSide:
         self._r0 = 0
         self._rn = 0
         self.headroom = 1024          # tokens of spare packed capacity per growth
+        self._g0 = None               # graph mode: (n_q, n_recent, r0) at step 0
 
     # ------------------------------------------------------------- geometry
     def _check_supported(self):
@@ -267,9 +268,84 @@ class PackedSide:
                   scale.data_ptr(), _ptr(zs if sign is None else None), stream_ptr(self.device))
         return codes, scale, zs
 
-    def fill_side(self, s: _lib.Side) -> _lib.Side:
+    # ---------------------------------------------------------- graph mode
+    def graph_begin(self, max_steps: int):
+        """Prepare for up to `max_steps` decode steps replayed from a CUDA
+        graph: the packed store and the recent FIFO get all the capacity those
+        steps need (nothing reallocates inside the graph), the FIFO is
+        compacted, and the state at step 0 is recorded.  The kernels derive
+        each step's state from it and the device step counter."""
+        if self.quantize:
+            self.reserve(self.n_q + max_steps + self.flush)
+        need = self._rn + max_steps + 1
+        if self._rbuf is None or self._r0 + need > self._rbuf.shape[2] or self._r0:
+            buf = torch.empty((self.B, self.H, max(need, self._rbuf.shape[2] if self._rbuf is not None else 0),
+                               self.D), dtype=self.dtype, device=self.device)
+            if self._rn:
+                buf[:, :, :self._rn].copy_(self.recent)
+            self._rbuf, self._r0 = buf, 0
+        self._g0 = (self.n_q, self._rn, self._r0)
+        self._g_args = _lib.AppendArgs()
+        self._g_args.struct_size = C.sizeof(_lib.AppendArgs)
+
+    def append_graph(self, x: torch.Tensor, step: torch.Tensor):
+        """The decode append of one token x [B, H, 1, D] in graph mode: one
+        launch of innerq_append_step, state taken from the step counter."""
+        a = self._g_args
+        nq0, rn0, r00 = self._g0
+        a.dtype, a.B, a.H, a.D = dtype_code(self.dtype), self.B, self.H, self.D
+        a.x, a.x_sb, a.x_sh = x.data_ptr(), x.stride(0), x.stride(1)
+        rb = self._rbuf
+        a.fifo = rb.data_ptr()
+        a.f_sb, a.f_sh, a.f_st = rb.stride()[:3]
+        a.fifo_cap = rb.shape[2]
+        a.codes, a.scale, a.zero = _ptr(self.codes), _ptr(self.scale), _ptr(self.zero)
+        a.cap_tiles = self.cap_tiles
+        a.norm_f = self.norm_f.data_ptr() if (self.normalize and self.norm_f is not None) else None
+        a.bits = self.bits if self.quantize else 16
+        a.group, a.mode, a.role, a.over_token = self.group, self.mode, self.role, int(self.over_token)
+        a.flush = self.flush
+        a.n_q, a.n_recent, a.r0 = nq0, rn0, r00
+        _lib.call("innerq_append_step", C.byref(a), step.data_ptr(), stream_ptr(self.device))
+
+    def state_after(self, n_steps: int) -> tuple[int, int]:
+        """(n_q, n_recent) after n_steps graph-mode steps (host arithmetic)."""
+        nq0, rn0, _ = self._g0
+        f = self.flush if self.quantize else 0
+        k = min(n_steps, (rn0 + n_steps) // f) if f else 0
+        return nq0 + f * k, rn0 + n_steps - f * k
+
+    def graph_end(self, n_steps: int):
+        """Bring the host-side state up to date after n_steps replayed steps."""
+        nq0, rn0, r00 = self._g0
+        f = self.flush if self.quantize else 0
+        k = min(n_steps, (rn0 + n_steps) // f) if f else 0
+        self.n_q, self._rn, self._r0 = nq0 + f * k, rn0 + n_steps - f * k, r00 + f * k
+        self._g0 = None
+
+    def fill_side(self, s: _lib.Side, graph: bool = False) -> _lib.Side:
         """Write this side's current geometry into a (reused) C struct; the
-        recent-window pointer is computed without building a tensor view."""
+        recent-window pointer is computed without building a tensor view.
+        graph=True: the step-0 state of graph mode (FIFO base, offset and
+        flush size; the kernel advances it by the step counter)."""
+        if graph:
+            nq0, rn0, r00 = self._g0
+            s.codes, s.scale, s.zero = _ptr(self.codes), _ptr(self.scale), _ptr(self.zero)
+            s.cap_tiles = self.cap_tiles
+            if self.sink is not None and self.sink.shape[2]:
+                s.sink = self.sink.data_ptr()
+                s.sink_sb, s.sink_sh, s.sink_st = self.sink.stride()[:3]
+                s.n_sink = self.sink.shape[2]
+            else:
+                s.sink, s.n_sink = None, 0
+            rb = self._rbuf
+            s.recent = rb.data_ptr()
+            s.rec_sb, s.rec_sh, s.rec_st = rb.stride()[:3]
+            s.n_q, s.n_recent, s.r0 = nq0, rn0, r00
+            s.flush = self.flush if self.quantize else 0
+            s.bits, s.group, s.mode, s.over_token = self.bits, self.group, self.mode, int(self.over_token)
+            return s
+        s.r0, s.flush = 0, 0
         nq = self.n_q
         s.codes = self.codes.data_ptr() if nq else None
         s.scale = self.scale.data_ptr() if nq else None

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
         assert n in _lib.EXPORTS, f"{n} has no ctypes signature"
-    assert lib.innerq_abi_version() == 2
+    assert lib.innerq_abi_version() == 3
     assert lib.innerq_tile_bytes(4) == 2048 and lib.innerq_tile_bytes(3) == 1536
     assert lib.innerq_tile_bytes(2) == 1024 and lib.innerq_tile_bytes(5) == -1 and lib.innerq_tile_bytes(1) == 512
 
@@ -40,15 +40,33 @@ def test_ctypes_structs_match_c_layout(tmp_path):
     from innerq_b200 import _lib
     c = tmp_path / "s.c"
     c.write_text('#include "innerq_b200.h"\n#include <stdio.h>\n#include <stddef.h>\n'
-                 'int main(){printf("%zu %zu %zu %zu %zu\\n", sizeof(innerq_attn_args),'
+                 'int main(){printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(innerq_attn_args),'
                  ' sizeof(innerq_side), offsetof(innerq_attn_args, k), offsetof(innerq_attn_args, v),'
-                 ' offsetof(innerq_attn_args, softmax_scale));}\n')
+                 ' offsetof(innerq_attn_args, softmax_scale), offsetof(innerq_attn_args, step),'
+                 ' sizeof(innerq_append_args), offsetof(innerq_append_args, norm_f),'
+                 ' offsetof(innerq_append_args, r0));}\n')
     exe = tmp_path / "s"
     subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(c), "-o", str(exe)], check=True)
     got = list(map(int, subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()))
     A = _lib.AttnArgs
+    P = _lib.AppendArgs
     assert got == [ctypes.sizeof(A), ctypes.sizeof(_lib.Side), A.k.offset, A.v.offset,
-                   A.softmax_scale.offset]
+                   A.softmax_scale.offset, A.step.offset, ctypes.sizeof(P), P.norm_f.offset,
+                   P.r0.offset]
+
+
+def test_append_step_rejects_bad_arguments_without_a_gpu():
+    from innerq_b200 import _lib
+    lib = _lib.load()
+    a = _lib.AppendArgs()
+    a.struct_size = ctypes.sizeof(_lib.AppendArgs)
+    a.dtype, a.B, a.H, a.D = _lib.DT_F16, 1, 1, 64
+    step = ctypes.c_int64(0)
+    assert lib.innerq_append_step(ctypes.byref(a), ctypes.byref(step), None) == -2
+    assert "head_dim" in _lib.last_error()
+    a.D, a.x, a.fifo, a.fifo_cap, a.n_recent, a.r0 = 128, 8, 8, 16, 12, 8
+    assert lib.innerq_append_step(ctypes.byref(a), ctypes.byref(step), None) == -1
+    assert "FIFO" in _lib.last_error()
 
 
 def test_argument_errors_are_reported_without_a_gpu():
