@@ -327,7 +327,8 @@ struct AttnStatic {
   uint8_t pd_s[kWarps][RP][2][kTile];
   float cm_s[kWarps][RP];
   float cl_s[kWarps][RP];
-  int geo[5];                 // graph mode: this step's S, packed K / V counts, K / V FIFO offsets
+  int geo[9];                 // graph mode: this step's S, packed K / V counts, K / V FIFO
+                              // offsets, the split's tile range, the packed tile run
 };
 
 // balanced base-256 digits of an integer |v| < 2^23: v = d2*65536 + d1*256 + d0
@@ -389,8 +390,7 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
           }
       }
     }
-    return;
-  }
+  } else {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     int acc[2][2][4];  // [mt][digit n-tile: (d2,d1) / (d0,-)][c]
@@ -431,6 +431,7 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
         }
       }
     }
+  }
   }
 }
 
@@ -558,9 +559,22 @@ decode_attn_kernel(const DevArgs a) {
     fast_hi = (hi_tok - a.t_first) >> 5;  // floor: the tile must end inside
   }
   const int n_st = (tile_end - tile_beg + kWarps - 1) / kWarps;
+  if constexpr (GM) {
+    // graph mode: the tile loop reads this step's geometry from shared memory
+    // (it cannot be re-derived from the launch arguments, and kept in
+    // registers across the loop it spills); written before thread 0's first
+    // copies and read by the others after the barrier below
+    if (threadIdx.x == 0) {
+      sm.geo[0] = S; sm.geo[1] = nqk; sm.geo[2] = nqv; sm.geo[3] = kr0; sm.geo[4] = vr0;
+      sm.geo[5] = tile_beg; sm.geo[6] = tile_end; sm.geo[7] = fast_lo; sm.geo[8] = fast_hi;
+    }
+  }
+  auto gTB = [&]() -> int { if constexpr (GM) return sm.geo[5]; else return tile_beg; };
+  auto gTE = [&]() -> int { if constexpr (GM) return sm.geo[6]; else return tile_end; };
   auto stage_fast = [&](int i) -> bool {
-    const int ta = tile_beg + kWarps * i, tb = min(ta + kWarps, tile_end) - 1;
-    return ta >= fast_lo && tb < fast_hi;
+    const int ta = gTB() + kWarps * i, tb = min(ta + kWarps, gTE()) - 1;
+    if constexpr (GM) return ta >= sm.geo[7] && tb < sm.geo[8];
+    else return ta >= fast_lo && tb < fast_hi;
   };
   // issued by one thread: the last warp to release the slot (or thread 0 at start)
   auto issue = [&](int i) {
@@ -571,7 +585,7 @@ decode_attn_kernel(const DevArgs a) {
       mbar_arrive(bar);
       return;
     }
-    const int ta = tile_beg + kWarps * i, n_in = min(kWarps, tile_end - ta);
+    const int ta = gTB() + kWarps * i, n_in = min(kWarps, gTE() - ta);
     const int t0 = a.t_first + ta * kTile;
     const int64_t tk = (t0 - ks) >> 5, tv = (t0 - vs) >> 5;
     const int64_t g0 = (t0 - vs) >> vgs, g1 = (t0 + n_in * kTile - 1 - vs) >> vgs;
@@ -627,12 +641,7 @@ decode_attn_kernel(const DevArgs a) {
     bulk_g2s(&sm.qp, src, kH, &sm.prep_bar);
     if (any_dense) bulk_g2s(&sm.qp.bd, src + kH, kDn, &sm.prep_bar);
   }
-  if constexpr (GM) {
-    // the tile loop reads the step's geometry from shared memory (kept in
-    // registers across the loop it spills)
-    if (threadIdx.x == 0) { sm.geo[0] = S; sm.geo[1] = nqk; sm.geo[2] = nqv; sm.geo[3] = kr0; sm.geo[4] = vr0; }
-  }
-  __syncthreads();  // barrier initialisation is visible to every thread
+  __syncthreads();  // barrier initialisation (and graph-mode geometry) visible to every thread
   bool failed = !mbar_wait_bounded(&sm.prep_bar, 0, kWaitLimit);
   int i_done = 0;
   float ctf[NT][NG];  // K offset correction per channel group: off * sum q
@@ -649,7 +658,6 @@ decode_attn_kernel(const DevArgs a) {
   const float cd = ldexpf(a.scale_log2, -sm.qp.e_d);
 
   // ---------------------------------------------------------------- tiles
-#pragma unroll 1
   // this step's geometry inside the loop: launch arguments, or (graph mode)
   // shared memory
   auto gS = [&]() -> int { if constexpr (GM) return sm.geo[0]; else return a.S; };
@@ -657,6 +665,7 @@ decode_attn_kernel(const DevArgs a) {
   auto gNQV = [&]() -> int { if constexpr (GM) return sm.geo[2]; else return a.v.n_q; };
   auto gKR0 = [&]() -> int { if constexpr (GM) return sm.geo[3]; else return 0; };
   auto gVR0 = [&]() -> int { if constexpr (GM) return sm.geo[4]; else return 0; };
+#pragma unroll 1
   for (int i = 0; i < (failed ? 0 : n_st); ++i) {
     const int slot = i % kStages;
     if (!mbar_wait_bounded(&sm.bars[slot], (uint32_t)((i / kStages) & 1), kWaitLimit)) {
@@ -664,11 +673,11 @@ decode_attn_kernel(const DevArgs a) {
       break;
     }
     i_done = i + 1;
-    const int tile = tile_beg + kWarps * i + warp;
+    const int tile = gTB() + kWarps * i + warp;
     const int t0 = a.t_first + tile * kTile;
     const bool fast = stage_fast(i);
     const uint8_t* sg = ring + slot * SBC;
-    if (tile < tile_end) {
+    if (tile < gTE()) {
     float x[NT][4];
 
     // ----------------------------------------------------------- QK^T
