@@ -35,6 +35,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode attn HBM GB/s (4-bit QK^T+AV, Llama-3-8B attention shape)"
 D = 128
+NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e, nominal (DGX figure)
 
 
 def parse():
@@ -169,71 +170,83 @@ class ClockSampler:
 
 
 # ------------------------------------------------------- CPU reference ---
-def cpu_reference_sample(a, seconds=None, steps=None, warmup=0):
-    """The reference's CPU algorithm (oracle port of cache.py + the HF
-    consumer): per decode step, append the token, dequantize the whole cache
-    in fp32, cast, and run fp32 GQA attention.  Sample = one layer, batch 1,
-    all KV heads, full context; KV heads run on a thread pool (numpy releases
-    the GIL).  Returns (GB/s, cores, sample description, seconds per step)."""
-    import concurrent.futures as cf
+def cpu_reference_sample(a, seconds=None, steps=None, warmup=0, budget_s=150.0):
+    """The reference's decode step on the host cores: the torch restatement of
+    cache.py's update (append, flush, quantize, cat, dequantize the whole
+    store in fp32, cast) and the Hugging Face sdpa consumer, torch running on
+    every host core (torch.set_num_threads(os.cpu_count())).  Sample = one
+    layer of the benchmark's configuration; the batch is the benchmark's
+    unless host memory or the time budget (`budget_s` for warm-up + timed
+    steps, estimated from a batch-1 probe) needs a smaller one, in which case
+    the sample says so.  Returns (GB/s of the same algorithmic bytes as the
+    GPU metric, threads, sample description, seconds per step)."""
+    import torch
 
-    import numpy as np
-
-    from oracle import cache_ref as C
+    from oracle.torch_ref import TorchRefLayer, consumer_attention
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
     kw = cache_kw(a)
     S = a.ctx
-    cores = min(a.hkv, os.cpu_count() or 1)
-    rng = np.random.default_rng(0)
-    rep = a.hq // a.hkv
+    gen = torch.Generator().manual_seed(0)
 
-    def one_head(h):
-        r = np.random.default_rng(h)
-        k = (r.standard_normal((1, 1, S - 1, D), dtype=np.float32)
-             * np.exp(r.standard_normal(D)).astype(np.float32)).astype(np.float16).astype(np.float32)
-        v = r.standard_normal((1, 1, S - 1, D), dtype=np.float32).astype(np.float16).astype(np.float32)
-        layer = C.OracleLayer(C.CacheConfig(**kw), "fp16")
-        layer.update(k, v)
-        return layer
+    def make(b):
+        layer = TorchRefLayer(**kw)
+        k = torch.randn((b, a.hkv, S - 1, D), generator=gen)
+        k *= torch.exp(torch.randn(D, generator=gen))
+        v = torch.randn((b, a.hkv, S - 1, D), generator=gen)
+        layer.update(k.half(), v.half())
+        del k, v
+        q = torch.randn((b, a.hq, 1, D), generator=gen).half()
+        new = torch.randn((b, a.hkv, 1, D), generator=gen).half()
+        return layer, q, new
 
-    with cf.ThreadPoolExecutor(cores) as ex:
-        layers = list(ex.map(one_head, range(a.hkv)))
-    q = rng.standard_normal((1, rep, D), dtype=np.float32).astype(np.float16).astype(np.float32)
-    newk = rng.standard_normal((1, 1, 1, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    def step(layer, q, new):
+        K, V = layer.update(new, new)
+        return consumer_attention(q, K, V)
 
-    def head_step(layer):
-        K, V = layer.update(newk, newk)
-        Kf = K[0, 0].astype(np.float32)
-        Vf = V[0, 0].astype(np.float32)
-        logits = (q[0] @ Kf.T) / math.sqrt(D)
-        m = logits.max(-1, keepdims=True)
-        p = np.exp(logits - m)
-        return (p / p.sum(-1, keepdims=True)) @ Vf
-
-    def step():
-        with cf.ThreadPoolExecutor(cores) as ex:
-            list(ex.map(head_step, layers))
-
+    # batch-1 probe: per-step time scales with the batch
+    layer, q, new = make(1)
+    step(layer, q, new)
+    t0 = time.perf_counter()
+    step(layer, q, new)
+    t1 = time.perf_counter() - t0
+    del layer
+    n_steps = (steps if steps is not None else 2) + warmup
+    # host bytes per (batch row): fp16 inputs, int32 codes, fp16 signs, fp32
+    # dequantization, the cast and the repeated KV heads, K and V
+    per_row = a.hkv * S * D * (2 + 4 + 2 + 4 + 4 + 2 * (a.hq // a.hkv)) * 2
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except ImportError:
+        avail = 16 << 30
+    B = a.batch
+    while B > 1 and (per_row * B > 0.4 * avail or t1 * B * n_steps > budget_s):
+        B //= 2
+    layer, q, new = make(B)
     for _ in range(warmup):
-        step()
+        step(layer, q, new)
     times = []
     t_end = time.perf_counter() + (seconds or 1e9)
     n = 0
     while True:
         t0 = time.perf_counter()
-        step()
+        step(layer, q, new)
         times.append(time.perf_counter() - t0)
         n += 1
         if (steps is not None and n >= steps) or (steps is None and time.perf_counter() > t_end):
             break
-    k0 = layers[0].k
-    v0 = layers[0].v
-    per_bh = side_bytes(k0.n_quantized(), k0.sink.shape[2], k0.recent.shape[2], a.kbits, a.group,
-                        False, norm=True) \
-        + side_bytes(v0.n_quantized(), v0.sink.shape[2], v0.recent.shape[2], a.vbits, a.group, True)
-    nbytes = a.hkv * per_bh + 2 * a.hq * D * 2
+    k0, v0 = layer.k, layer.v
+    per_bh = side_bytes(k0.codes.shape[2], k0.sink.shape[2], k0.recent.shape[2], a.kbits, a.group,
+                        False, kw["key_quantize_mode"] == "asymmetric", norm=True) \
+        + side_bytes(v0.codes.shape[2], v0.sink.shape[2], v0.recent.shape[2], a.vbits, a.group,
+                     kw["value_quantize_over_token"], kw["value_quantize_mode"] == "asymmetric")
+    nbytes = B * a.hkv * per_bh + 2 * B * a.hq * D * 2
     t = statistics.median(times)
-    sample = (f"1 layer, batch 1, {a.hkv} kv heads x {a.hq // a.hkv} q heads, context {S}, "
-              f"{len(times)} steps; KV heads on {cores} threads")
+    why = "" if B == a.batch else f" (batch {a.batch} reduced to fit host memory / the time budget)"
+    sample = (f"torch restatement of the reference decode step (cache.py update + sdpa consumer), "
+              f"1 layer, batch {B}{why}, {a.hkv} kv heads x {a.hq // a.hkv} q heads, context {S}, "
+              f"{len(times)} steps; torch on {cores} threads")
     return nbytes / t / 1e9, cores, sample, t
 
 
@@ -273,7 +286,7 @@ def run_ours(a):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-    from innerq_b200.sharding import gather_heads, head_shard
+    from innerq_b200.sharding import HeadGather, head_shard
     h_lo, h_hi = head_shard(a.hkv, world, rank)
     hkv, hq = h_hi - h_lo, (h_hi - h_lo) * (a.hq // a.hkv)
     B, L = a.batch, a.layers
@@ -301,6 +314,9 @@ def run_ours(a):
     ks = torch.randn((NPOOL, L, B, hkv, 1, D), device=dev, generator=g).half()
     vs = torch.randn((NPOOL, L, B, hkv, 1, D), device=dev, generator=g).half()
     out = torch.empty((L, B, hq, D), device=dev, dtype=torch.float16)
+    # the one collective per step: the KV-head shards' outputs gathered into a
+    # buffer allocated here, once
+    gather = HeadGather(out) if world > 1 else None
 
     def step(i, q=None, k=None, v=None):
         q = qs[i % NPOOL] if q is None else q
@@ -309,8 +325,8 @@ def run_ours(a):
         for li, layer in enumerate(layers):
             layer.update(k[li], v[li])
             layer.attend(q[li], out=out[li])
-        if world > 1:
-            gather_heads(out)  # [L, B, Hq, D] across the KV-head shards
+        if gather is not None:
+            gather()  # [L, B, Hq, D] across the KV-head shards
 
     gsteps = [None]  # graph-mode steps replayed so far (None: eager)
 
@@ -397,8 +413,8 @@ def run_ours(a):
             v_in.copy_(vs[i % NPOOL] if v is None else v)
             graph.replay()
             gsteps[0] += 1
-            if world > 1:
-                gather_heads(out)  # the one collective per step stays outside the recording
+            if gather is not None:
+                gather()  # the one collective per step stays outside the recording
 
         for i in range(max(3, a.warmup)):
             graph_step(i)
@@ -429,6 +445,17 @@ def run_ours(a):
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / a.steps
     total_bytes = max_over_ranks(nbytes / a.steps) * world  # ranks hold equal shares
     value = total_bytes / (ms * 1e-3) / 1e9
+
+    # ---- the per-step all-gather alone (its share of the step)
+    gather_ms = None
+    if gather is not None:
+        sync_all()
+        ev0.record(stream)
+        for i in range(a.steps):
+            gather()
+        ev1.record(stream)
+        sync_all()
+        gather_ms = max_over_ranks(ev0.elapsed_time(ev1)) / a.steps
 
     # ---- end to end through the public API with host buffers
     qh = qs[0].cpu().pin_memory()
@@ -488,13 +515,18 @@ def run_ours(a):
                 "step_trial_ms": {k_: round(v_, 3) for k_, v_ in mode_ms.items()},
                 "l2": f"inputs larger than L2 ({total_bytes / 1e9:.1f} GB of cache read per step)",
                 "us_per_layer": round(ms * 1e3 / L, 2),
+                "allgather_ms_per_step": None if gather_ms is None else round(gather_ms, 4),
+                "allgather_share": None if gather_ms is None else round(gather_ms / ms, 4),
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": "decode_attn_kernel (+ lse_merge)",
                          "per_launch_bytes": int(per_launch_bytes),
                          "per_launch_us": round(per_launch_ms * 1e3, 2),
-                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
+                         "frac_of_nominal": round(achieved / NOMINAL_HBM_GBS, 4),
+                         "value_frac_of_measured": round(value / world / peak, 4),
+                         "value_frac_of_nominal": round(value / world / NOMINAL_HBM_GBS, 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": launches,

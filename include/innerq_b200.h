@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define INNERQ_ABI_VERSION 3
+#define INNERQ_ABI_VERSION 4
 
 enum {
   INNERQ_OK = 0,
@@ -138,8 +138,11 @@ typedef struct {
   int32_t over_token;  /* 0 for K (channel groups), 1 for V (token groups) */
   /* Graph mode only (innerq_attn_args.step set), else 0: n_q / n_recent are
    * the counts at step 0, `recent` is the FIFO buffer base, r0 the window's
-   * FIFO offset at step 0 and flush the side's flush size (0: no quantization). */
-  int32_t r0, flush;
+   * FIFO offset at step 0 and flush the side's flush size (0: no quantization).
+   * max_steps: the steps the buffers were reserved for; the kernel reads the
+   * state after min(*step, max_steps) steps, so a counter run past the
+   * reservation never reads outside the buffers (the caller checks the count). */
+  int32_t r0, flush, max_steps;
 } innerq_side;
 
 typedef struct {
@@ -217,6 +220,8 @@ typedef struct {
   int32_t group, mode, role, over_token;
   int32_t flush;        /* the side's flush size */
   int32_t n_q, n_recent, r0;  /* packed count, window size and its FIFO offset at step 0 */
+  int32_t max_steps;    /* steps the FIFO and the store were reserved for; a counter
+                         * beyond it makes the launch write nothing */
 } innerq_append_args;
 
 int innerq_append_step(const innerq_append_args* args, const int64_t* step, void* stream);
@@ -234,11 +239,16 @@ int innerq_lse_merge(const float* part_o, const float* part_m, const float* part
  * reference, which has no native entry points.
  *
  * The split-KV partials live in a file-scope device array of
- * INNERQ_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
- * exit.  The first call on a device looks up that array's device address
- * (cudaGetSymbolAddress) with the device current; make that first call
- * before any stream capture.  Calls whose partials would not fit are rejected
- * with INNERQ_ERR_ARG (pass a smaller n_splits or batch).  All calls share the
+ * INNERQ_NOALLOC_SCRATCH_BYTES.  A device takes that memory when the
+ * library's module is loaded on it: with CUDA's lazy module loading (the
+ * default of CUDA 12) that is the first valid call of this function on the
+ * device, which looks up the array's address (cudaGetSymbolAddress) with the
+ * device current; without lazy loading it is the library's first use of the
+ * device.  Either way the memory stays taken until the process exits.  Make
+ * the first call on each device before any stream capture.  Arguments are
+ * checked first: a rejected call takes no memory.  Calls whose partials would
+ * not fit are rejected with INNERQ_ERR_ARG (pass a smaller n_splits or
+ * batch); other bad arguments get the status innerq_decode_attn gives them.  All calls share the
  * one array: calls that overlap on the GPU (two streams, two threads) race.
  * Nothing in it needs to start at zero.  Allocates nothing; arguments and
  * results as innerq_decode_attn.

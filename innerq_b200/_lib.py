@@ -41,7 +41,7 @@ class Side(C.Structure):
         ("recent", C.c_void_p), ("rec_sb", C.c_int64), ("rec_sh", C.c_int64), ("rec_st", C.c_int64),
         ("n_sink", C.c_int32), ("n_q", C.c_int32), ("n_recent", C.c_int32),
         ("bits", C.c_int32), ("group", C.c_int32), ("mode", C.c_int32), ("over_token", C.c_int32),
-        ("r0", C.c_int32), ("flush", C.c_int32),
+        ("r0", C.c_int32), ("flush", C.c_int32), ("max_steps", C.c_int32),
     ]
 
 
@@ -57,6 +57,7 @@ class AppendArgs(C.Structure):
         ("bits", C.c_int32), ("group", C.c_int32), ("mode", C.c_int32), ("role", C.c_int32),
         ("over_token", C.c_int32), ("flush", C.c_int32),
         ("n_q", C.c_int32), ("n_recent", C.c_int32), ("r0", C.c_int32),
+        ("max_steps", C.c_int32),
     ]
 
 
@@ -111,7 +112,7 @@ def load() -> C.CDLL:
         f = getattr(lib, name)
         f.restype = res
         f.argtypes = args
-    if lib.innerq_abi_version() != 3:
+    if lib.innerq_abi_version() != 4:
         raise ImportError("libinnerq_b200.so ABI version mismatch; rebuild it")
     _lib = lib
     return lib

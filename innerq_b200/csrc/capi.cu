@@ -1,6 +1,8 @@
 // C-ABI entry points of libinnerq_b200.so (declared in include/innerq_b200.h):
 // argument validation, split-KV planning and kernel dispatch.
 #include <cuda_runtime.h>
+
+#include <algorithm>
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
@@ -87,6 +89,21 @@ int check_side(const innerq_side& s, int dtype, int role, const char* name) {
   return INNERQ_OK;
 }
 
+// tokens a side's packed store holds after max_steps graph-mode steps (one
+// token appended per step, `flush` packed whenever the window holds that many)
+int64_t graph_packed_need(int n_q, int n_rec, int flush, int max_steps) {
+  const int64_t k = flush > 0 ? std::min<int64_t>(max_steps, ((int64_t)n_rec + max_steps) / flush) : 0;
+  return (int64_t)n_q + (int64_t)flush * k;
+}
+
+int check_graph_side(const innerq_side& s, const char* which) {
+  if (s.max_steps < 0) return fail(INNERQ_ERR_ARG, "%s: max_steps %d", which, s.max_steps);
+  if (s.flush > 0 && graph_packed_need(s.n_q, s.n_recent, s.flush, s.max_steps) > s.cap_tiles * 32)
+    return fail(INNERQ_ERR_ARG, "%s: packed store of %lld tiles cannot take %d steps", which,
+                (long long)s.cap_tiles, s.max_steps);
+  return INNERQ_OK;
+}
+
 int make_plan(const innerq_attn_args* a, Plan& p) {
   if (!a) return fail(INNERQ_ERR_ARG, "null args");
   if (a->struct_size != (int32_t)sizeof(innerq_attn_args))
@@ -102,6 +119,10 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   if (rc) return rc;
   rc = check_side(a->v, a->dtype, INNERQ_ROLE_V, "v");
   if (rc) return rc;
+  if (a->step) {
+    if ((rc = check_graph_side(a->k, "k"))) return rc;
+    if ((rc = check_graph_side(a->v, "v"))) return rc;
+  }
   // values grouped over channels share the keys' channel-group count
   if (packed(a->v) && !a->v.over_token && packed(a->k) && a->v.group != a->k.group)
     return fail(INNERQ_ERR_UNSUPPORTED,
@@ -160,6 +181,7 @@ DevSide dev_side(const innerq_side& s) {
   d.chan = 0;
   d.r0 = s.r0;
   d.flush = s.flush;
+  d.max_steps = s.max_steps;
   return d;
 }
 
@@ -377,6 +399,12 @@ int innerq_append_step(const innerq_append_args* a, const int64_t* step, void* s
   if (!step || !a->x || !a->fifo) return fail(INNERQ_ERR_ARG, "null pointer");
   if (a->n_q < 0 || a->n_recent < 0 || a->r0 < 0 || a->r0 + a->n_recent > a->fifo_cap)
     return fail(INNERQ_ERR_ARG, "FIFO state outside its buffer");
+  if (a->max_steps < 0 || (int64_t)a->r0 + a->n_recent + a->max_steps > a->fifo_cap)
+    return fail(INNERQ_ERR_ARG, "FIFO of %d tokens cannot take %d steps", a->fifo_cap, a->max_steps);
+  if (a->bits != 16 && a->flush > 0 &&
+      graph_packed_need(a->n_q, a->n_recent, a->flush, a->max_steps) > a->cap_tiles * 32)
+    return fail(INNERQ_ERR_ARG, "packed store of %lld tiles cannot take %d steps",
+                (long long)a->cap_tiles, a->max_steps);
   AppendArgs g;
   g.x = a->x; g.x_sb = a->x_sb; g.x_sh = a->x_sh;
   g.fifo = a->fifo; g.f_sb = a->f_sb; g.f_sh = a->f_sh; g.f_st = a->f_st; g.fifo_cap = a->fifo_cap;
@@ -384,7 +412,7 @@ int innerq_append_step(const innerq_append_args* a, const int64_t* step, void* s
   g.norm_f = a->norm_f;
   g.dt = a->dtype; g.B = a->B; g.H = a->H; g.bits = a->bits; g.group = a->group;
   g.asym = a->mode == INNERQ_ASYM; g.flush = a->flush;
-  g.n_q = a->n_q; g.n_rec = a->n_recent; g.r0 = a->r0;
+  g.n_q = a->n_q; g.n_rec = a->n_recent; g.r0 = a->r0; g.max_steps = a->max_steps;
   if (a->bits == 16) {
     g.mode = 3;
   } else {

@@ -57,8 +57,9 @@ struct DevSide {
   int asym;
   int chan;   // values grouped over channels (scales per token and channel group)
   // graph mode (DevArgs::step set): n_q / n_rec are the counts at step 0, rec
-  // the FIFO base, r0 the window's FIFO offset at step 0, flush the flush size
-  int r0, flush;
+  // the FIFO base, r0 the window's FIFO offset at step 0, flush the flush size,
+  // max_steps the steps its buffers were reserved for
+  int r0, flush, max_steps;
 };
 
 // A side's geometry after n decode steps of graph mode: each step appends one
@@ -508,7 +509,9 @@ decode_attn_kernel(const DevArgs a) {
   int S = a.S, nqk = a.k.n_q, nqv = a.v.n_q, kr0 = 0, vr0 = 0;
   int tile_lo = a.tile_lo, tile_hi = a.tile_hi, tps = a.tiles_per_split;
   if constexpr (GM) {
-    const int n = (int)*a.step;
+    // a counter past the reservation reads the last reserved state, never
+    // beyond the buffers
+    const int n = (int)min(*a.step, (int64_t)min(a.k.max_steps, a.v.max_steps));
     const SideNow kn = side_after(a.k, n), vn = side_after(a.v, n);
     nqk = kn.nq; nqv = vn.nq; kr0 = kn.r0; vr0 = vn.r0;
     S = a.k.n_sink + kn.nq + kn.nrec;

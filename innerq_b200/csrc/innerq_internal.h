@@ -54,7 +54,7 @@ struct AppendArgs {
   void* fifo; int64_t f_sb, f_sh, f_st; int fifo_cap;
   void* codes; void* scale; void* zero; int64_t cap_tiles;
   const void* norm_f;
-  int dt, B, H, bits, group, asym, mode, flush, n_q, n_rec, r0;
+  int dt, B, H, bits, group, asym, mode, flush, n_q, n_rec, r0, max_steps;
 };
 cudaError_t launch_append_step(const AppendArgs& a, const int64_t* step, cudaStream_t s);
 // the query-prep pass that precedes every attention launch (qprep.cu)

@@ -32,6 +32,19 @@ extern "C" {
 
 int innerq_decode_attn_noalloc(const innerq_attn_args* args, void* out, int64_t o_sb,
                                int64_t o_sh, float* lse, void* stream) {
+  // arguments first: a rejected call neither touches the scratch nor loads
+  // the module that holds it; the plan's own status (INNERQ_ERR_ARG or
+  // INNERQ_ERR_UNSUPPORTED) is returned unchanged
+  const int rc = innerq_attn_plan(args, nullptr, nullptr);
+  if (rc != INNERQ_OK) return rc;  // innerq_last_error() holds the reason
+  const int64_t need = innerq_decode_attn_workspace(args);
+  if (need < 0) return INNERQ_ERR_ARG;
+  if (need > kScratchBytes) {
+    return innerq::set_last_error(INNERQ_ERR_ARG,
+             "noalloc: split-KV partials need %lld bytes, above the fixed %lld-byte scratch; pass a "
+             "smaller n_splits or a smaller batch, or use innerq_decode_attn with a workspace",
+             (long long)need, (long long)kScratchBytes);
+  }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     return innerq::set_last_error(INNERQ_ERR_CUDA, "noalloc: no usable current CUDA device");
@@ -49,14 +62,6 @@ int innerq_decode_attn_noalloc(const innerq_attn_args* args, void* out, int64_t 
       }
     }
     ptr = g_addr[dev];
-  }
-  const int64_t need = innerq_decode_attn_workspace(args);
-  if (need < 0) return INNERQ_ERR_ARG;  // innerq_last_error() holds the reason
-  if (need > kScratchBytes) {
-    return innerq::set_last_error(INNERQ_ERR_ARG,
-             "noalloc: split-KV partials need %lld bytes, above the fixed %lld-byte scratch; pass a "
-             "smaller n_splits or a smaller batch, or use innerq_decode_attn with a workspace",
-             (long long)need, (long long)kScratchBytes);
   }
   // Every partial row is written by the attention pass before the merge reads
   // it, so nothing in the scratch has to start at zero.

@@ -384,7 +384,7 @@ struct AppendDev {
   uint16_t* zero;
   int64_t cap_tiles;
   const uint16_t* nf;
-  int group, asym, flush, n_q, n_rec, r0;
+  int group, asym, flush, n_q, n_rec, r0, max_steps;
 };
 
 template <int DT, int BITS, int MODE>
@@ -392,6 +392,7 @@ __global__ void __launch_bounds__(128) append_step_kernel(const AppendDev a, con
   __shared__ uint32_t seg_unused[16];
   const int h = blockIdx.x, b = blockIdx.y, H = gridDim.x, d = threadIdx.x;
   const int64_t bh = (int64_t)b * H + h;
+  if (*step < 1 || *step > a.max_steps) return;  // outside the reserved steps: write nothing
   const int n1 = (int)*step, n0 = n1 - 1;
   uint16_t* fifo = a.fifo + b * a.f_b + h * a.f_h;
   const int pos = a.r0 + a.n_rec + n0;
@@ -602,6 +603,7 @@ cudaError_t launch_append_step(const AppendArgs& g, const int64_t* step, cudaStr
   a.codes = (uint8_t*)g.codes; a.scale = (uint16_t*)g.scale; a.zero = (uint16_t*)g.zero;
   a.cap_tiles = g.cap_tiles; a.nf = (const uint16_t*)g.norm_f;
   a.group = g.group; a.asym = g.asym; a.flush = g.flush; a.n_q = g.n_q; a.n_rec = g.n_rec; a.r0 = g.r0;
+  a.max_steps = g.max_steps;
   const dim3 grid((unsigned)g.H, (unsigned)g.B, 1);
   const int dt = g.dt, bits = g.bits;
   switch (g.mode) {

@@ -20,12 +20,23 @@ from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
 NAME = "innerq"
 
 
+_mask_seen = [None, False]  # (mask tensor of the current forward, its verdict)
+
+
 def _trivial_mask(mask) -> bool:
+    """True when the mask hides nothing.  Decode without padding gets no mask
+    at all (the sdpa mask builder skips it after its own check of the padding
+    mask), which costs nothing here.  A mask tensor (padding, or a sliding
+    window the builder could not skip) is read once per forward: every layer
+    of one forward receives the same tensor, so the host synchronises at most
+    once per decode step, not once per layer."""
     if mask is None:
         return True
-    if mask.dtype == torch.bool:
-        return bool(mask.all())
-    return bool((mask == 0).all())
+    if _mask_seen[0] is mask:
+        return _mask_seen[1]
+    ok = bool(mask.all()) if mask.dtype == torch.bool else bool((mask == 0).all())
+    _mask_seen[0], _mask_seen[1] = mask, ok
+    return ok
 
 
 def innerq_attention_forward(module, query, key, value, attention_mask, dropout: float = 0.0,

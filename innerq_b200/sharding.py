@@ -37,11 +37,36 @@ def chunk_range(n_items: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def gather_heads(out_local: torch.Tensor, group=None) -> torch.Tensor:
-    """[..., Hq_local, D] per rank -> [..., Hq, D] in rank (head) order."""
-    world = dist.get_world_size(group)
-    parts = [torch.empty_like(out_local) for _ in range(world)]
-    dist.all_gather(parts, out_local.contiguous(), group=group)
-    return torch.cat(parts, dim=-2)
+    """[..., Hq_local, D] per rank -> [..., Hq, D] in rank (head) order
+    (allocating; HeadGather is the per-step form)."""
+    return HeadGather(out_local, group)().flatten(-3, -2)
+
+
+class HeadGather:
+    """The per-step all-gather of the KV-head shards' attention outputs,
+    with its buffer allocated once: one all_gather_into_tensor of the local
+    [..., Hq_local, D] block into a [world, ..., Hq_local, D] buffer.
+    ``heads()`` views it as [..., world, Hq_local, D] (query head
+    r * Hq_local + j at [..., r, j, :]), with no copy."""
+
+    def __init__(self, out_local: torch.Tensor, group=None):
+        self.src = out_local
+        self.group = group
+        self.world = dist.get_world_size(group)
+        # concatenated along dim 0 (the form every backend takes), viewed as
+        # [world, ...]
+        shape = tuple(out_local.shape)
+        self.flat = out_local.new_empty((self.world * shape[0],) + shape[1:])
+        self.buf = self.flat.view((self.world,) + shape)
+
+    def __call__(self) -> torch.Tensor:
+        """Gather; returns the [..., world, Hq_local, D] view of the buffer."""
+        dist.all_gather_into_tensor(self.flat, self.src.contiguous(), group=self.group)
+        return self.heads()
+
+    def heads(self) -> torch.Tensor:
+        nd = self.buf.dim()
+        return self.buf.permute(*range(1, nd - 2), 0, nd - 2, nd - 1)
 
 
 def merge_context_partials(po: torch.Tensor, pm: torch.Tensor, pl: torch.Tensor, dtype,

@@ -285,6 +285,7 @@ class PackedSide:
                 buf[:, :, :self._rn].copy_(self.recent)
             self._rbuf, self._r0 = buf, 0
         self._g0 = (self.n_q, self._rn, self._r0)
+        self._g_max = max_steps
         self._g_args = _lib.AppendArgs()
         self._g_args.struct_size = C.sizeof(_lib.AppendArgs)
 
@@ -306,6 +307,7 @@ class PackedSide:
         a.group, a.mode, a.role, a.over_token = self.group, self.mode, self.role, int(self.over_token)
         a.flush = self.flush
         a.n_q, a.n_recent, a.r0 = nq0, rn0, r00
+        a.max_steps = self._g_max
         _lib.call("innerq_append_step", C.byref(a), step.data_ptr(), stream_ptr(self.device))
 
     def state_after(self, n_steps: int) -> tuple[int, int]:
@@ -316,7 +318,13 @@ class PackedSide:
         return nq0 + f * k, rn0 + n_steps - f * k
 
     def graph_end(self, n_steps: int):
-        """Bring the host-side state up to date after n_steps replayed steps."""
+        """Bring the host-side state up to date after n_steps replayed steps.
+        More steps than graph_begin reserved raise: the kernels stopped at the
+        reservation (appends write nothing past it), so the cache no longer
+        holds every token."""
+        if n_steps > self._g_max:
+            raise RuntimeError(f"{n_steps} graph-mode steps replayed, {self._g_max} reserved by "
+                               "graph_begin: the steps past the reservation were not appended")
         nq0, rn0, r00 = self._g0
         f = self.flush if self.quantize else 0
         k = min(n_steps, (rn0 + n_steps) // f) if f else 0
@@ -342,10 +350,11 @@ class PackedSide:
             s.recent = rb.data_ptr()
             s.rec_sb, s.rec_sh, s.rec_st = rb.stride()[:3]
             s.n_q, s.n_recent, s.r0 = nq0, rn0, r00
+            s.max_steps = self._g_max
             s.flush = self.flush if self.quantize else 0
             s.bits, s.group, s.mode, s.over_token = self.bits, self.group, self.mode, int(self.over_token)
             return s
-        s.r0, s.flush = 0, 0
+        s.r0, s.flush, s.max_steps = 0, 0, 0
         nq = self.n_q
         s.codes = self.codes.data_ptr() if nq else None
         s.scale = self.scale.data_ptr() if nq else None

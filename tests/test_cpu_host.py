@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
         assert n in _lib.EXPORTS, f"{n} has no ctypes signature"
-    assert lib.innerq_abi_version() == 3
+    assert lib.innerq_abi_version() == 4
     assert lib.innerq_tile_bytes(4) == 2048 and lib.innerq_tile_bytes(3) == 1536
     assert lib.innerq_tile_bytes(2) == 1024 and lib.innerq_tile_bytes(5) == -1 and lib.innerq_tile_bytes(1) == 512
 
@@ -139,3 +139,22 @@ def test_layer_config_surface_matches_reference_defaults():
                     num_key_value_heads=1, intermediate_size=64, vocab_size=32)
     cache = DynamicCache(config=c)
     assert len(cache.layers) == 3 and all(isinstance(l, InnerqDynamicLayer) for l in cache.layers)
+
+
+def test_noalloc_returns_the_plan_status_without_a_gpu():
+    """Argument errors are found before any device work: the allocation-free
+    entry point returns the same status as innerq_decode_attn (here
+    INNERQ_ERR_UNSUPPORTED for a GQA ratio of 3, INNERQ_ERR_ARG for a bad
+    struct size) and touches no device."""
+    from innerq_b200 import _lib
+    lib = _lib.load()
+    a = _lib.AttnArgs()
+    a.struct_size = ctypes.sizeof(_lib.AttnArgs)
+    a.dtype, a.B, a.Hq, a.Hkv, a.D = _lib.DT_F16, 1, 24, 8, 128
+    a.q = 16  # never dereferenced: the plan rejects the arguments first
+    for expect in (-2, -1):
+        if expect == -1:
+            a.struct_size = 8
+        r1 = lib.innerq_decode_attn(ctypes.byref(a), None, 0, None, 0, 0, None, None)
+        r2 = lib.innerq_decode_attn_noalloc(ctypes.byref(a), None, 0, 0, None, None)
+        assert r1 == r2 == expect, (r1, r2)

@@ -118,3 +118,29 @@ def test_lse_merge_matches_full_softmax():
         ls.append(p.sum(-1))
     o = C.lse_merge(np.stack(os_, -2), np.stack(ms, -1), np.stack(ls, -1))
     np.testing.assert_allclose(o, full, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", list(PRESET_KW))
+def test_torch_baseline_layer_bit_exact(cache_golden, name):
+    """The torch CPU restatement timed as the CPU baseline returns the
+    reference's K/V bit for bit after prefill + 40 decode steps."""
+    import torch
+
+    from oracle.torch_ref import TorchRefLayer, consumer_attention
+    g = cache_golden
+    p = f"cache/{name}"
+    dtype = str(g[p + "/dtype"])
+    tdt = torch.float16 if dtype == "fp16" else torch.bfloat16
+    kin = torch.from_numpy(golden_to_f32(g[p + "/k_in"], dtype)).to(tdt)
+    vin = torch.from_numpy(golden_to_f32(g[p + "/v_in"], dtype)).to(tdt)
+    layer = TorchRefLayer(**PRESET_KW[name])
+    T0 = kin.shape[2] - 40
+    layer.update(kin[:, :, :T0], vin[:, :, :T0])
+    for t in range(T0, kin.shape[2]):
+        K, V = layer.update(kin[:, :, t:t + 1], vin[:, :, t:t + 1])
+    np.testing.assert_array_equal(K.float().numpy(), golden_to_f32(g[p + "/K"], dtype))
+    np.testing.assert_array_equal(V.float().numpy(), golden_to_f32(g[p + "/V"], dtype))
+    q = torch.from_numpy(golden_to_f32(g[p + "/q"], dtype)).to(tdt)
+    o = consumer_attention(q, K, V).float().numpy()
+    ref = g[p + "/o"]
+    assert np.abs(o - ref).max() <= 2e-2 * np.abs(ref).max()
