@@ -44,13 +44,17 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=32)
-    ap.add_argument("--ctx", type=int, default=32768)
-    ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--hq", type=int, default=32)
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--ctx", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--hq", type=int, default=None)
     ap.add_argument("--hkv", type=int, default=8)
-    ap.add_argument("--kbits", type=int, default=4)
-    ap.add_argument("--vbits", type=int, default=4)
+    ap.add_argument("--kbits", type=int, default=None)
+    ap.add_argument("--vbits", type=int, default=None)
+    ap.add_argument("--ctx-shards", type=int, default=1,
+                    help="context chunks per KV-head shard (N GPUs = head shards x ctx shards): "
+                         "each rank stores one chunk of the context, the split partials are "
+                         "all-gathered within the chunk group and log-sum-exp merged per layer")
     ap.add_argument("--group", type=int, default=32)
     ap.add_argument("--v-layout", default="tokens", choices=["tokens", "channels"],
                     help="value groups over tokens (InnerQ default) or over channels "
@@ -62,12 +66,30 @@ def parse():
                          "recorded decode step (CUDA graph, cache graph mode)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", default="c1", choices=["c1", "c3", "sweep"],
+    ap.add_argument("--workload", default="c1", choices=["c1", "c3", "c4", "sweep"],
                     help="c1: decode attention over a 32-layer cache (default); "
+                         "c4: the same over the 70B-shaped 80-layer 2-bit cache (B 8, Hq 64, "
+                         "131072 tokens); "
                          "c3: full decode step of a random-init Llama-3-8B-shaped model; "
                          "sweep: the C1/C2/C4 attention and append grid, one JSON line per "
                          "configuration (not the one-line bench contract)")
-    return ap.parse_args()
+    a = ap.parse_args()
+    # BASELINE config 1 (C1) and config 4 (C4); C3 keeps its own defaults
+    defaults = {"c4": dict(batch=8, ctx=131072, layers=80, hq=64, kbits=2, vbits=2)}.get(
+        a.workload, dict(batch=32, ctx=32768, layers=32, hq=32, kbits=4, vbits=4))
+    for k_, v_ in defaults.items():
+        if getattr(a, k_) is None:
+            setattr(a, k_, v_)
+    return a
+
+
+def metric_name(a):
+    """The C1 line keeps BASELINE's metric name; other workloads say their shape."""
+    if a.workload == "c4":
+        return f"decode attn HBM GB/s ({a.kbits}/{a.vbits}-bit QK^T+AV, 70B attention shape)"
+    if (a.kbits, a.vbits) != (4, 4):
+        return f"decode attn HBM GB/s ({a.kbits}/{a.vbits}-bit QK^T+AV, Llama-3-8B attention shape)"
+    return METRIC
 
 
 def cache_kw(a):
@@ -256,13 +278,16 @@ def run_reference(a):
         return
     gbs, cores, sample, t = cpu_reference_sample(a, steps=a.steps, warmup=a.warmup)
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s",
+        "impl": "reference", "metric": metric_name(a), "value": round(gbs, 4), "unit": "GB/s",
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic",
-        "config": {"workload": "C1: Llama-3-8B attention shape, 4-bit InnerQ cache, decode step",
-                   "batch": a.batch, "context": a.ctx, "layers": a.layers,
-                   "reference_sample": sample},
+        "config": {"workload": (f"C4: 70B attention shape, {a.kbits}/{a.vbits}-bit InnerQ cache, "
+                                "decode step" if a.workload == "c4" else
+                                f"C1: Llama-3-8B attention shape, {a.kbits}/{a.vbits}-bit InnerQ "
+                                "cache, decode step"),
+                   "batch": a.batch, "context": a.ctx, "layers": a.layers, "q_heads": a.hq,
+                   "kv_heads": a.hkv, "reference_sample": sample},
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -286,22 +311,48 @@ def run_ours(a):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-    from innerq_b200.sharding import HeadGather, head_shard
-    h_lo, h_hi = head_shard(a.hkv, world, rank)
+    from innerq_b200.sharding import ContextMerge, HeadGather, head_shard
+    from innerq_b200.attention import build_args, plan
+    CS = a.ctx_shards
+    if CS < 1 or world % CS:
+        raise SystemExit(f"--ctx-shards {CS} does not divide {world} ranks")
+    HS = world // CS
+    hs, cs = divmod(rank, CS)     # this rank: KV-head shard hs, context chunk cs
+    last = cs == CS - 1           # the chunk that holds the recent window and takes the appends
+    h_lo, h_hi = head_shard(a.hkv, HS, hs)
     hkv, hq = h_hi - h_lo, (h_hi - h_lo) * (a.hq // a.hkv)
     B, L = a.batch, a.layers
     kw = cache_kw(a)
+    ctx_group = None
+    if CS > 1:
+        for i in range(HS):  # every rank takes part in creating every group
+            grp = dist.new_group(list(range(i * CS, (i + 1) * CS)))
+            if i == hs:
+                ctx_group = grp
+        # chunk cs of the T = ctx-1 prefill tokens: the sink on chunk 0, the
+        # recent window on the last chunk, the packed part of every chunk a
+        # whole number of value groups
+        T, G = a.ctx - 1, max(32, a.group)
+        ns = kw["key_w_sink"]
+        cuts = [0] + [ns + ((T - ns) * c // CS) // G * G for c in range(1, CS)] + [T]
+        t_lo, t_hi = cuts[cs], cuts[cs + 1]
+        if cs > 0:
+            kw.update(key_w_sink=0, value_w_sink=0)
+        if not last:
+            kw.update(key_w_recent=0, value_w_recent=0)
+    else:
+        t_lo, t_hi = 0, a.ctx - 1
     conf = types.SimpleNamespace(_attn_implementation="innerq", **kw)
 
-    # ---- build the resident cache: prefill ctx-1 tokens per layer
+    # ---- build the resident cache: prefill this rank's tokens per layer
     layers = []
     g = torch.Generator(device=dev)
     for li in range(L):
         g.manual_seed(1000 * li + rank)
-        k = torch.randn((B, hkv, a.ctx - 1, D), device=dev, generator=g)
+        k = torch.randn((B, hkv, t_hi - t_lo, D), device=dev, generator=g)
         k *= torch.exp(torch.randn(D, device=dev, generator=g))
         k = k.half()
-        v = torch.randn((B, hkv, a.ctx - 1, D), device=dev, generator=g).half()
+        v = torch.randn((B, hkv, t_hi - t_lo, D), device=dev, generator=g).half()
         layer = InnerqDynamicLayer(conf, li)
         layer.update(k, v)
         del k, v
@@ -316,23 +367,47 @@ def run_ours(a):
     out = torch.empty((L, B, hq, D), device=dev, dtype=torch.float16)
     # the one collective per step: the KV-head shards' outputs gathered into a
     # buffer allocated here, once
-    gather = HeadGather(out) if world > 1 else None
+    head_group = None
+    if HS > 1 and CS > 1:
+        for j in range(CS):
+            grp = dist.new_group(list(range(j, world, CS)))
+            if j == cs:
+                head_group = grp
+    gather = HeadGather(out, head_group) if HS > 1 else None
+    merges = None
+    if CS > 1:
+        # the same split count on every rank of a chunk group (the largest any
+        # rank's planner picks), so the gathered partials blocks line up
+        ns_loc = plan(build_args(qs[0][0], layers[0].key_side, layers[0].value_side))[1]
+        t_ = torch.tensor([ns_loc], device=dev)
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        n_splits_ctx = int(t_.item())
+        merges = [ContextMerge(B, hq, n_splits_ctx, dev, ctx_group) for _ in range(L)]
+
+    def attend(li, layer, q):
+        if merges is None:
+            layer.attend(q, out=out[li])
+        else:  # this chunk's partials, one all-gather in the chunk group, one merge
+            mg = merges[li]
+            layer.attend_partials(q, mg.po, mg.pm, mg.pl)
+            mg(out[li])
 
     def step(i, q=None, k=None, v=None):
         q = qs[i % NPOOL] if q is None else q
         k = ks[i % NPOOL] if k is None else k
         v = vs[i % NPOOL] if v is None else v
         for li, layer in enumerate(layers):
-            layer.update(k[li], v[li])
-            layer.attend(q[li], out=out[li])
+            if last:
+                layer.update(k[li], v[li])
+            attend(li, layer, q[li])
         if gather is not None:
             gather()  # [L, B, Hq, D] across the KV-head shards
 
     gsteps = [None]  # graph-mode steps replayed so far (None: eager)
 
     def bytes_now():
-        # the step about to run: appends one token, then attends
-        n = None if gsteps[0] is None else gsteps[0] + 1
+        # the step about to run: appends one token (last chunk), then attends
+        n = None if (gsteps[0] is None or not last) else gsteps[0] + 1
         return sum(layer_bytes(l, B, hkv, hq, n) for l in layers)
 
     def sync_all():
@@ -348,6 +423,13 @@ def run_ours(a):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
+    def sum_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return t.item()
+
     for i in range(max(3, a.warmup)):
         step(i)
     stream = torch.cuda.current_stream()
@@ -360,7 +442,10 @@ def run_ours(a):
     reps = 3
     for r in range(reps):
         for li, layer in enumerate(layers):
-            layer.attend(qs[0][li], out=out[li])
+            if merges is None:
+                layer.attend(qs[0][li], out=out[li])
+            else:
+                layer.attend_partials(qs[0][li], merges[li].po, merges[li].pm, merges[li].pl)
     ev1.record(stream)
     torch.cuda.synchronize()
     per_launch_ms = ev0.elapsed_time(ev1) / (reps * L)
@@ -391,7 +476,7 @@ def run_ours(a):
     eager_step = step
     if not a.no_graph:
         gstep = torch.zeros(1, dtype=torch.int64, device=dev)
-        for layer in layers:
+        for layer in layers if last else ():  # the other chunks do not change
             layer.graph_begin(gstep, 2 * max(3, a.warmup) + 2 * a.steps + 2 * trial + 4)
         n0 = _lib.launch_count[0]
         cs = torch.cuda.Stream(dev)
@@ -401,8 +486,9 @@ def run_ours(a):
             with torch.cuda.graph(graph, stream=cs):
                 gstep.add_(1)
                 for li, layer in enumerate(layers):
-                    layer.update(k_in[li], v_in[li])
-                    layer.attend(q_in[li], out=out[li])
+                    if last:
+                        layer.update(k_in[li], v_in[li])
+                    attend(li, layer, q_in[li])
         torch.cuda.current_stream().wait_stream(cs)
         per_step_launches = _lib.launch_count[0] - n0
         gsteps[0] = 0
@@ -423,7 +509,7 @@ def run_ours(a):
             step = graph_step
         else:  # leave graph mode: the host takes the state back
             torch.cuda.synchronize()
-            for layer in layers:
+            for layer in layers if last else ():
                 layer.graph_end(gsteps[0])
             graph, gsteps[0], per_step_launches = None, None, None
             step = eager_step
@@ -443,7 +529,7 @@ def run_ours(a):
     clocks = sampler.stop()
     launches = _lib.launch_count[0] - launches0 if graph is None else per_step_launches * a.steps
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / a.steps
-    total_bytes = max_over_ranks(nbytes / a.steps) * world  # ranks hold equal shares
+    total_bytes = sum_over_ranks(nbytes / a.steps)
     value = total_bytes / (ms * 1e-3) / 1e9
 
     # ---- the per-step all-gather alone (its share of the step)
@@ -476,7 +562,7 @@ def run_ours(a):
     ev1.record(stream)
     sync_all()
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / a.steps
-    e2e_value = max_over_ranks(e2e_bytes / a.steps) * world / (e2e_ms * 1e-3) / 1e9
+    e2e_value = sum_over_ranks(e2e_bytes / a.steps) / (e2e_ms * 1e-3) / 1e9
     h2d = (qh.numel() + kh.numel() + vh.numel()) * 2 * world
     d2h = outh.numel() * 2 * world
 
@@ -494,23 +580,34 @@ def run_ours(a):
     peak = float(peaks.get("hbm_gbs", 6650.0))
     traffic = None
     try:
+        # DRAM bytes per algorithmic byte from an ncu capture of the same
+        # kernel configuration (keyed by workload), scaled to this launch
         tr = json.load(open(os.path.join(ROOT, "profiles", "decode_attn_traffic.json")))
-        traffic = round(tr["dram_bytes_per_algorithmic_byte"] * per_launch_bytes)
+        key = a.workload if (a.kbits, a.vbits, a.v_layout, a.mode) == (
+            (2, 2) if a.workload == "c4" else (4, 4)) + ("tokens", "symmetric") else None
+        ratio = tr.get("by_workload", {}).get(key) if key else None
+        if ratio is None and key == "c1":
+            ratio = tr["dram_bytes_per_algorithmic_byte"]
+        traffic = None if ratio is None else round(ratio * per_launch_bytes)
     except (OSError, KeyError, ValueError):
         pass
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "metric": metric_name(a), "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded N(0,1) K with exp(N(0,1)) channel outliers, N(0,1) V and q)",
             "config": {
-                "workload": "C1: decode step over a 32-layer Llama-3-8B-shaped 4-bit InnerQ cache",
+                "workload": ("C4: decode step over an 80-layer 70B-shaped (64 q / 8 kv heads) "
+                             f"{a.kbits}/{a.vbits}-bit InnerQ cache" if a.workload == "c4" else
+                             "C1: decode step over a 32-layer Llama-3-8B-shaped "
+                             f"{a.kbits}/{a.vbits}-bit InnerQ cache"),
                 "batch": B, "context": a.ctx, "layers": L, "q_heads": a.hq, "kv_heads": a.hkv,
                 "head_dim": D, "k_bits": a.kbits, "v_bits": a.vbits, "group": a.group,
                 "v_groups_over": a.v_layout, "mode": a.mode,
-                "parallelism": f"kv-head shards x{world}",
+                "parallelism": (f"kv-head shards x{HS}" + (f", context chunks x{CS} (split partials "
+                                "all-gathered and merged per layer)" if CS > 1 else "")),
                 "step": "eager launches" if graph is None else "recorded once (CUDA graph), replayed",
                 "step_trial_ms": {k_: round(v_, 3) for k_, v_ in mode_ms.items()},
                 "l2": f"inputs larger than L2 ({total_bytes / 1e9:.1f} GB of cache read per step)",

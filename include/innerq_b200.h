@@ -154,7 +154,8 @@ typedef struct {
   const void* key_norm;/* [B][Hkv][D] contiguous normalisation factor, or NULL */
   innerq_side k, v;
   float softmax_scale; /* the reference consumer uses head_dim^-0.5 */
-  int32_t n_splits;    /* 0 = choose for the GPU; else the split-KV count */
+  int32_t n_splits;    /* 0 = choose for the GPU; else exactly this split-KV count (splits
+                        * past the last tile publish m = -inf, l = 0) */
   int32_t tile_lo, tile_hi; /* 0,0 = all tiles; else a sub-range (context sharding) */
   /* Graph mode: device counter of decode steps appended since the state in k
    * and v (innerq_append_step advances the cache, the caller the counter), so
@@ -231,6 +232,22 @@ int innerq_append_step(const innerq_append_args* args, const int64_t* step, void
 int innerq_lse_merge(const float* part_o, const float* part_m, const float* part_l, int B,
                      int rows_per_b, int n_splits, int D, int dtype, void* out, int64_t o_sb,
                      int64_t o_sh, float* lse, void* stream);
+
+/*
+ * Context sharding across ranks (no counterpart in the reference, which is
+ * single-GPU): each rank computes the split partials of its own context chunk
+ * into one block of innerq_partials_rank_floats(B, rows_per_b, n_splits, D)
+ * floats laid out as [o: rows][n_splits][D] | [m: rows][n_splits] |
+ * [l: rows][n_splits] (rows = B * rows_per_b; pass the three parts to
+ * innerq_decode_attn_partials), the blocks of all ranks are gathered
+ * rank_stride floats apart (one all-gather), and innerq_lse_merge_ranks
+ * merges every rank's splits into out exactly as innerq_lse_merge merges one
+ * rank's.  Returns -1 for bad sizes.
+ */
+int64_t innerq_partials_rank_floats(int B, int rows_per_b, int n_splits, int D);
+int innerq_lse_merge_ranks(const float* parts, int n_ranks, int64_t rank_stride, int B,
+                           int rows_per_b, int n_splits, int D, int dtype, void* out, int64_t o_sb,
+                           int64_t o_sh, float* lse, void* stream);
 
 /*
  * innerq_decode_attn without a caller workspace, for callers that cannot

@@ -22,6 +22,7 @@ EXPORTS = (
     "innerq_quant_pack", "innerq_unpack_ref", "innerq_dequant", "innerq_attn_plan",
     "innerq_decode_attn_workspace", "innerq_decode_attn", "innerq_decode_attn_partials",
     "innerq_lse_merge", "innerq_dequant_ref", "innerq_decode_attn_noalloc", "innerq_append_step",
+    "innerq_partials_rank_floats", "innerq_lse_merge_ranks",
 )
 
 
@@ -107,6 +108,8 @@ def load() -> C.CDLL:
         "innerq_decode_attn_noalloc": (i32, [C.POINTER(AttnArgs), vp, i64, i64, vp, vp]),
         "innerq_append_step": (i32, [C.POINTER(AppendArgs), vp, vp]),
         "innerq_lse_merge": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp, i64, i64, vp, vp]),
+        "innerq_partials_rank_floats": (i64, [i32, i32, i32, i32]),
+        "innerq_lse_merge_ranks": (i32, [vp, i32, i64, i32, i32, i32, i32, i32, vp, i64, i64, vp, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)
@@ -123,6 +126,7 @@ KERNELS_PER_CALL = {
     "innerq_norm_factor": 1, "innerq_quant_pack": 1, "innerq_unpack_ref": 1, "innerq_dequant": 1,
     "innerq_dequant_ref": 1, "innerq_decode_attn": 3, "innerq_decode_attn_partials": 2,
     "innerq_lse_merge": 1, "innerq_decode_attn_noalloc": 3, "innerq_append_step": 1,
+    "innerq_lse_merge_ranks": 1,
 }
 launch_count = [0]
 

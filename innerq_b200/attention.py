@@ -75,10 +75,7 @@ class DecodeAttention:
         self.out = None
         self._lib = _lib.load()
 
-    def __call__(self, q: torch.Tensor, k: PackedSide, v: PackedSide, scale: float | None = None,
-                 out: torch.Tensor | None = None, step: torch.Tensor | None = None) -> torch.Tensor:
-        """step: graph mode (the stores' step-0 state plus the device step
-        counter; the launch can be recorded in a CUDA graph and replayed)."""
+    def _fill(self, q, k, v, scale, step):
         if not q.is_cuda or q.dtype != k.dtype:
             require_cuda(q, "query")
             raise TypeError(f"query dtype {q.dtype} != cache dtype {k.dtype}")
@@ -98,18 +95,41 @@ class DecodeAttention:
         v.fill_side(a.v, graph)
         a.step = step.data_ptr() if graph else None
         a.softmax_scale = float(scale if scale is not None else 1.0 / math.sqrt(D))
-        ref = C.byref(a)
-        ws_bytes = self._lib.innerq_decode_attn_workspace(ref)
+        return a, q
+
+    def _ws(self, a, device):
+        ws_bytes = self._lib.innerq_decode_attn_workspace(C.byref(a))
         if ws_bytes < 0:
             raise _lib.InnerqError("innerq_decode_attn_workspace", -1, _lib.last_error())
-        ws = _workspace(q.device, ws_bytes)
+        return _workspace(device, ws_bytes)
+
+    def __call__(self, q: torch.Tensor, k: PackedSide, v: PackedSide, scale: float | None = None,
+                 out: torch.Tensor | None = None, step: torch.Tensor | None = None) -> torch.Tensor:
+        """step: graph mode (the stores' step-0 state plus the device step
+        counter; the launch can be recorded in a CUDA graph and replayed)."""
+        a, q = self._fill(q, k, v, scale, step)
+        a.n_splits = 0
+        ws = self._ws(a, q.device)
+        B, Hq, D = a.B, a.Hq, a.D
         if out is None:
             if self.out is None or self.out.shape != (B, Hq, D) or self.out.dtype != q.dtype:
                 self.out = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
             out = self.out
-        _lib.call("innerq_decode_attn", ref, ws.data_ptr(), ws.numel(), out.data_ptr(),
+        _lib.call("innerq_decode_attn", C.byref(a), ws.data_ptr(), ws.numel(), out.data_ptr(),
                   out.stride(0), out.stride(1), None, stream_ptr(q.device))
         return out
+
+    def partials(self, q: torch.Tensor, k: PackedSide, v: PackedSide, po: torch.Tensor,
+                 pm: torch.Tensor, pl: torch.Tensor, scale: float | None = None,
+                 step: torch.Tensor | None = None) -> None:
+        """Exactly po.shape[2] split partials of this store into po
+        [B, Hq, s, D], pm / pl [B, Hq, s] (fp32, contiguous; e.g. the send
+        block of a sharding.ContextMerge)."""
+        a, q = self._fill(q, k, v, scale, step)
+        a.n_splits = po.shape[2]
+        ws = self._ws(a, q.device)
+        _lib.call("innerq_decode_attn_partials", C.byref(a), po.data_ptr(), pm.data_ptr(),
+                  pl.data_ptr(), ws.data_ptr(), ws.numel(), stream_ptr(q.device))
 
 
 def plan(args: _lib.AttnArgs) -> tuple[int, int]:

@@ -219,6 +219,16 @@ class InnerqDynamicLayer(CacheLayerMixin):
         # view only when the caller gave the destination
         return out_ if (out is not None or reuse) else out_.clone()
 
+    def attend_partials(self, query: torch.Tensor, po: torch.Tensor, pm: torch.Tensor,
+                        pl: torch.Tensor, scaling: float | None = None) -> None:
+        """Split partials of this layer's tokens (a context chunk when the
+        layer is one rank's share of a sharded cache) into po / pm / pl; see
+        DecodeAttention.partials."""
+        if self._attn is None:
+            from .attention import DecodeAttention
+            self._attn = DecodeAttention()
+        self._attn.partials(query, self._k, self._v, po, pm, pl, scaling, step=self._gstep)
+
     def get_mask_sizes(self, cache_position) -> tuple[int, int]:
         """cache.py:398-402; also takes the int query_length of transformers >= 5.5."""
         kv_offset = 0

@@ -159,7 +159,10 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   }
   if (splits > 65535) splits = 65535;
   p.tps = ntr > 0 ? (ntr + splits - 1) / splits : 1;
-  p.n_splits = ntr > 0 ? (ntr + p.tps - 1) / p.tps : 1;
+  // a chosen count drops the splits that would get no tile; a requested one
+  // is kept exactly (its trailing splits may be empty and publish m = -inf),
+  // so every rank of a context-sharded layer has the same partials layout
+  p.n_splits = a->n_splits > 0 ? splits : (ntr > 0 ? (ntr + p.tps - 1) / p.tps : 1);
   p.bk = packed(a->k) ? a->k.bits : 4;
   p.bv = packed(a->v) ? a->v.bits : 4;
   return INNERQ_OK;
@@ -444,6 +447,30 @@ int innerq_lse_merge(const float* part_o, const float* part_m, const float* part
   return cuda_status(launch_lse_merge(part_o, part_m, part_l, B * rows_per_b, rows_per_b, n_splits,
                                       dtype, out, o_sb, o_sh, lse, (cudaStream_t)stream),
                      "lse_merge");
+}
+
+int64_t innerq_partials_rank_floats(int B, int rows_per_b, int n_splits, int D) {
+  if (B < 0 || rows_per_b < 0 || n_splits <= 0 || D != kD) return -1;
+  const int64_t rows = (int64_t)B * rows_per_b * n_splits;
+  return rows * (kD + 2);
+}
+
+int innerq_lse_merge_ranks(const float* parts, int n_ranks, int64_t rank_stride, int B,
+                           int rows_per_b, int n_splits, int D, int dtype, void* out, int64_t o_sb,
+                           int64_t o_sh, float* lse, void* stream) {
+  if (D != kD) return fail(INNERQ_ERR_UNSUPPORTED, "head_dim %d", D);
+  if (dtype != INNERQ_DT_F16 && dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype");
+  if (B < 0 || rows_per_b < 0 || n_splits <= 0 || n_ranks <= 0) return fail(INNERQ_ERR_ARG, "sizes");
+  if (!parts || !out) return fail(INNERQ_ERR_ARG, "null pointer");
+  const int64_t block = innerq_partials_rank_floats(B, rows_per_b, n_splits, D);
+  if (n_ranks > 1 && rank_stride < block)
+    return fail(INNERQ_ERR_ARG, "rank stride %lld floats < the %lld of one rank's partials",
+                (long long)rank_stride, (long long)block);
+  const int64_t rs = (int64_t)B * rows_per_b * n_splits;
+  return cuda_status(launch_lse_merge(parts, parts + rs * kD, parts + rs * kD + rs, B * rows_per_b,
+                                      rows_per_b, n_splits, dtype, out, o_sb, o_sh, lse,
+                                      (cudaStream_t)stream, n_ranks, rank_stride),
+                     "lse_merge_ranks");
 }
 
 }  // extern "C"

@@ -23,7 +23,8 @@ cudaError_t launch_dequant(const void* codes, const void* scale, const void* zer
                            void* out, int64_t ob, int64_t oh, int64_t ot, cudaStream_t s);
 cudaError_t launch_lse_merge(const float* po, const float* pm, const float* pl, int rows,
                              int rows_per_b, int n_splits, int dt, void* out, int64_t o_b,
-                             int64_t o_h, float* lse, cudaStream_t s);
+                             int64_t o_h, float* lse, cudaStream_t s, int n_ranks = 1,
+                             int64_t rank_stride = 0);
 cudaError_t launch_dequant_ref(const int32_t* c, const void* s, const void* zs, int dt, int64_t n_outer,
                                int T, int D, int group, int asym, int over_token, float* out,
                                cudaStream_t st);

@@ -524,20 +524,30 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ codes, const uint16_t
 template <int DT>
 __global__ void lse_merge_kernel(const float* __restrict__ po, const float* __restrict__ pm,
                                  const float* __restrict__ pl, int n_splits, int rows_per_b,
+                                 int n_ranks, int64_t rank_stride,
                                  uint16_t* __restrict__ out, int64_t o_b, int64_t o_h,
                                  float* __restrict__ lse_out) {
+  // n_ranks blocks of partials, rank_stride floats apart (one block per rank
+  // of a context-sharded layer, gathered; 1 block otherwise), each with
+  // n_splits partials per row
   const int row = blockIdx.x, d = threadIdx.x;
-  const float* m = pm + (int64_t)row * n_splits;
-  const float* l = pl + (int64_t)row * n_splits;
   float M = -INFINITY;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, m[s]);
+  for (int w = 0; w < n_ranks; ++w) {
+    const float* m = pm + w * rank_stride + (int64_t)row * n_splits;
+    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, m[s]);
+  }
   float num = 0.f, den = 0.f;
   if (M != -INFINITY) {
-    for (int s = 0; s < n_splits; ++s) {
-      if (m[s] == -INFINITY) continue;  // an empty split contributes nothing
-      const float w = exp2f(m[s] - M);
-      num += w * po[((int64_t)row * n_splits + s) * kD + d];
-      den += w * l[s];
+    for (int w = 0; w < n_ranks; ++w) {
+      const float* m = pm + w * rank_stride + (int64_t)row * n_splits;
+      const float* l = pl + w * rank_stride + (int64_t)row * n_splits;
+      const float* o = po + w * rank_stride + (int64_t)row * n_splits * kD + d;
+      for (int s = 0; s < n_splits; ++s) {
+        if (m[s] == -INFINITY) continue;  // an empty split contributes nothing
+        const float wt = exp2f(m[s] - M);
+        num += wt * o[(int64_t)s * kD];
+        den += wt * l[s];
+      }
     }
   }
   const int b = row / rows_per_b, h = row % rows_per_b;
@@ -679,10 +689,11 @@ cudaError_t launch_dequant(const void* codes, const void* scale, const void* zer
 
 cudaError_t launch_lse_merge(const float* po, const float* pm, const float* pl, int rows,
                              int rows_per_b, int n_splits, int dt, void* out, int64_t o_b,
-                             int64_t o_h, float* lse, cudaStream_t s) {
+                             int64_t o_h, float* lse, cudaStream_t s, int n_ranks,
+                             int64_t rank_stride) {
   if (rows == 0) return cudaSuccess;
-  DT_DISPATCH(dt, lse_merge_kernel<DTC><<<rows, kD, 0, s>>>(po, pm, pl, n_splits, rows_per_b,
-                                                            (uint16_t*)out, o_b, o_h, lse));
+  DT_DISPATCH(dt, lse_merge_kernel<DTC><<<rows, kD, 0, s>>>(po, pm, pl, n_splits, rows_per_b, n_ranks,
+                                                            rank_stride, (uint16_t*)out, o_b, o_h, lse));
   return cudaGetLastError();
 }
 

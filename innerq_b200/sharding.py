@@ -69,30 +69,65 @@ class HeadGather:
         return self.buf.permute(*range(1, nd - 2), 0, nd - 2, nd - 1)
 
 
+def _pack(po, pm, pl):
+    return torch.cat([po.reshape(-1), pm.reshape(-1), pl.reshape(-1)])
+
+
+def _unpack(block, B, Hq, s, D):
+    rows = B * Hq * s
+    return (block[:rows * D].view(B, Hq, s, D), block[rows * D:rows * (D + 1)].view(B, Hq, s),
+            block[rows * (D + 1):rows * (D + 2)].view(B, Hq, s))
+
+
 def merge_context_partials(po: torch.Tensor, pm: torch.Tensor, pl: torch.Tensor, dtype,
                            group=None, merge_fn=None) -> torch.Tensor:
-    """All-gather each rank's split partials (po [B,Hq,s,D], pm/pl [B,Hq,s];
-    the split count may differ per rank) and merge them into [B, Hq, D]."""
+    """Gather every rank's split partials (po [B,Hq,s,D], pm/pl [B,Hq,s], the
+    same split count s on every rank: pass n_splits explicitly) with ONE
+    all-gather of a packed block per rank, then merge them into [B, Hq, D]:
+    by merge_fn(po_all, pm_all, pl_all, dtype) when given (CPU ranks), else
+    by the CUDA rank-block merge, which reads the gathered blocks in place."""
     world = dist.get_world_size(group)
-    s_local = torch.tensor([po.shape[2]], dtype=torch.int64, device=po.device)
-    sizes = [torch.zeros_like(s_local) for _ in range(world)]
-    dist.all_gather(sizes, s_local, group=group)
-    smax = int(max(x.item() for x in sizes))
     B, Hq, s, D = po.shape
-    pad_o = po.new_zeros((B, Hq, smax, D))
-    pad_m = pm.new_full((B, Hq, smax), float("-inf"))
-    pad_l = pl.new_zeros((B, Hq, smax))
-    pad_o[:, :, :s] = po
-    pad_m[:, :, :s] = pm
-    pad_l[:, :, :s] = pl
-    go = [torch.empty_like(pad_o) for _ in range(world)]
-    gm = [torch.empty_like(pad_m) for _ in range(world)]
-    gl = [torch.empty_like(pad_l) for _ in range(world)]
-    dist.all_gather(go, pad_o, group=group)
-    dist.all_gather(gm, pad_m, group=group)
-    dist.all_gather(gl, pad_l, group=group)
-    po_all, pm_all, pl_all = torch.cat(go, 2), torch.cat(gm, 2), torch.cat(gl, 2)
-    if merge_fn is None:
-        from .attention import lse_merge
-        merge_fn = lse_merge
-    return merge_fn(po_all, pm_all, pl_all, dtype)
+    send = _pack(po, pm, pl)
+    recv = send.new_empty((world * send.numel(),))
+    dist.all_gather_into_tensor(recv, send, group=group)
+    if merge_fn is not None:
+        parts = [_unpack(recv[w * send.numel():(w + 1) * send.numel()], B, Hq, s, D)
+                 for w in range(world)]
+        return merge_fn(torch.cat([p[0] for p in parts], 2), torch.cat([p[1] for p in parts], 2),
+                        torch.cat([p[2] for p in parts], 2), dtype)
+    out = torch.empty((B, Hq, D), dtype=dtype, device=po.device)
+    merge_rank_blocks(recv, world, send.numel(), B, Hq, s, out)
+    return out
+
+
+def merge_rank_blocks(recv: torch.Tensor, world: int, block: int, B: int, Hq: int, s: int,
+                      out: torch.Tensor) -> torch.Tensor:
+    """innerq_lse_merge_ranks over `world` gathered partials blocks."""
+    from . import _lib
+    from .store import dtype_code, stream_ptr
+    _lib.call("innerq_lse_merge_ranks", recv.data_ptr(), world, block, B, Hq, s, out.shape[-1],
+              dtype_code(out.dtype), out.data_ptr(), out.stride(0), out.stride(1), None,
+              stream_ptr(recv.device))
+    return out
+
+
+class ContextMerge:
+    """The per-layer exchange of a context-sharded layer, buffers allocated
+    once: this rank's attention writes its split partials straight into
+    ``po`` / ``pm`` / ``pl`` (views of one packed send block), ``__call__``
+    gathers the blocks of all ranks of ``group`` with one
+    all_gather_into_tensor and merges them into ``out`` with one launch."""
+
+    def __init__(self, B: int, Hq: int, n_splits: int, device, group=None, D: int = 128):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.B, self.Hq, self.s, self.D = B, Hq, n_splits, D
+        self.block = B * Hq * n_splits * (D + 2)
+        self.send = torch.empty(self.block, dtype=torch.float32, device=device)
+        self.recv = torch.empty(self.world * self.block, dtype=torch.float32, device=device)
+        self.po, self.pm, self.pl = _unpack(self.send, B, Hq, n_splits, D)
+
+    def __call__(self, out: torch.Tensor) -> torch.Tensor:
+        dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        return merge_rank_blocks(self.recv, self.world, self.block, self.B, self.Hq, self.s, out)

@@ -112,7 +112,7 @@ def test_graph_end_rejects_steps_past_the_reservation():
     run) makes graph_end raise instead of handing back a cache that lost
     tokens."""
     from innerq_b200.cache import DynamicCache, InnerqDynamicLayer
-    layer = InnerqDynamicLayer(cfg(**_bench_kw(4, 32)), 0)
+    layer = InnerqDynamicLayer(cfg(_attn_implementation="innerq", **_bench_kw(4, 32)), 0)
     k, v = synth_kv_dev(1, 2, 300, seed=30)
     layer.update(k, v)
     cache = DynamicCache()
