@@ -64,6 +64,12 @@ def parse():
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every kernel from the host each step instead of replaying the "
                          "recorded decode step (CUDA graph, cache graph mode)")
+    ap.add_argument("--only", default=None,
+                    help="sweep: run only the rows whose name contains this text")
+    ap.add_argument("--sweep-ctx", type=int, default=None,
+                    help="sweep: override the context of the selected rows (small profiling cases)")
+    ap.add_argument("--sweep-batch", type=int, default=None,
+                    help="sweep: override the batch of the selected rows")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="c1", choices=["c1", "c3", "c4", "sweep"],
@@ -771,6 +777,10 @@ def run_sweep(a):
     peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("hbm_gbs", 6650.0)) \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
     for name, B, hq, ctx, bits, group, vlay, mode in SWEEP:
+        if a.only is not None and a.only not in name:
+            continue
+        ctx = a.sweep_ctx or ctx
+        B = a.sweep_batch or B
         a2 = types.SimpleNamespace(kbits=bits, vbits=bits, group=group, v_layout=vlay, mode=mode)
         kw = cache_kw(a2)
         hkv = 8
@@ -829,12 +839,28 @@ def run_sweep(a):
         torch.cuda.synchronize()
         us_tok = e0.elapsed_time(e1) * 1e3 / 20
         side.n_q = 0
+        torch.cuda.nvtx.range_push("chunk")  # profiling handle (ncu --nvtx-include chunk/)
         e0.record()
         side._quantize(x)
         e1.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         us_chunk = e0.elapsed_time(e1) * 1e3
-        del side, x
+        # the same chunk as values (token groups, the InnerQ V layout)
+        vside = PackedSide(_lib.ROLE_V, bits, group, _lib.SYM if mode == "symmetric" else _lib.ASYM,
+                           True, 0, 0, max(32, group))
+        vside.prefill(x[:, :, :max(32, group)])
+        vside.reserve(8192)
+        vside.n_q = 0
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("chunk_v")
+        e0.record()
+        vside._quantize(x)
+        e1.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        us_chunk_v = e0.elapsed_time(e1) * 1e3
+        del side, vside, x
         torch.cuda.empty_cache()
         print(json.dumps({
             "config": name, "batch": B, "q_heads": hq, "kv_heads": hkv, "context": ctx,
@@ -842,7 +868,9 @@ def run_sweep(a):
             "attn_us": round(us, 1), "attn_GBs": round(nb / us / 1e3, 1),
             "frac_of_measured_hbm": round(nb / us / 1e3 / peak, 3), "bytes_per_launch": nb,
             "append_1_token_us": round(us_tok, 1), "append_4096_chunk_us": round(us_chunk, 1),
-            "chunk_read_GBs": round(B * hkv * 4096 * D * 2 / us_chunk / 1e3, 1)}), flush=True)
+            "chunk_read_GBs": round(B * hkv * 4096 * D * 2 / us_chunk / 1e3, 1),
+            "append_4096_chunk_v_us": round(us_chunk_v, 1),
+            "chunk_v_read_GBs": round(B * hkv * 4096 * D * 2 / us_chunk_v / 1e3, 1)}), flush=True)
 
 
 def main():

@@ -255,9 +255,12 @@ class InnerqDynamicLayer(CacheLayerMixin):
 
 class InnerqDynamicSlidingWindowLayer(InnerqDynamicLayer):
     """cache.py:421-461.  The reference crops with ``[:, :, -window, :]``
-    (``cache.py:443-444``), which keeps a single token and drops a dim; this
-    layer crops to the last ``window`` tokens, which is what the surrounding
-    code intends.  The fused path is not used for sliding layers."""
+    (``cache.py:443-444``), which keeps a single token and drops a dim, and
+    only once more than ``window`` tokens preceded the step, one step after
+    its own ``get_mask_sizes`` starts sizing the mask for a full window.  This
+    layer returns what that mask describes: once ``window`` tokens preceded
+    the step, the last ``window - 1 + q_len`` tokens.  The fused path is not
+    used for sliding layers."""
     is_sliding = True
 
     def __init__(self, config, layer_idx: int, sliding_window: int):
@@ -273,9 +276,11 @@ class InnerqDynamicSlidingWindowLayer(InnerqDynamicLayer):
 
     def update(self, key_states, value_states, cache_kwargs=None):
         k, v = super().update(key_states, value_states, cache_kwargs)
-        if self.cumulative_length - key_states.shape[-2] > self.sliding_window:
-            k = k[:, :, -self.sliding_window:, :]
-            v = v[:, :, -self.sliding_window:, :]
+        q_len = key_states.shape[-2]
+        if self.cumulative_length - q_len >= self.sliding_window:  # get_mask_sizes' is_full
+            keep = self.sliding_window - 1 + q_len
+            k = k[:, :, -keep:, :]
+            v = v[:, :, -keep:, :]
         return k, v
 
     def get_mask_sizes(self, cache_position) -> tuple[int, int]:

@@ -100,14 +100,14 @@ __device__ __forceinline__ float div_rn(float a, float b, float rb) {
 
 // ------------------------------------------------------------------ mma ---
 __device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], const uint32_t b[2]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 __device__ __forceinline__ void mma_bf16(float c[4], const uint32_t a[4], const uint32_t b[2]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -119,14 +119,14 @@ template <> __device__ __forceinline__ void mma_dt<BF16>(float c[4], const uint3
 
 // integer MMA: u8 codes x s8 / u8 digits, exact int32 accumulation
 __device__ __forceinline__ void mma_u8s8(int c[4], const uint32_t a[4], const uint32_t b[2]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 __device__ __forceinline__ void mma_u8u8(int c[4], const uint32_t a[4], const uint32_t b[2]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
@@ -137,7 +137,7 @@ __device__ __forceinline__ void mma_u8u8(int c[4], const uint32_t a[4], const ui
 // zeros or per-thread constants for c avoids materialising zeroed registers
 __device__ __forceinline__ void imma_u8s8(int d[4], const uint32_t a[4], const uint32_t b[2], int c0,
                                           int c1, int c2, int c3) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
@@ -146,7 +146,7 @@ __device__ __forceinline__ void imma_u8s8(int d[4], const uint32_t a[4], const u
 }
 __device__ __forceinline__ void imma_u8u8(int d[4], const uint32_t a[4], const uint32_t b[2], int c0,
                                           int c1, int c2, int c3) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])

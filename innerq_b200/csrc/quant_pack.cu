@@ -71,6 +71,34 @@ __global__ void norm_factor_kernel(const uint16_t* __restrict__ x, int64_t sb, i
   f[(int64_t)bh * kD + d] = from_f<DT>(sqrtf(mx));
 }
 
+// the same with 1024 threads per (b, h): 16 token rows x 64 dim pairs, each
+// thread keeping 8 four-byte loads in flight, then a shared-memory reduction
+template <int DT>
+__global__ void __launch_bounds__(1024) norm_factor_wide_kernel(const uint16_t* __restrict__ x, int64_t sb,
+                                                                int64_t sh, int64_t st, int H, int T,
+                                                                uint16_t* __restrict__ f) {
+  __shared__ float red[16][kD];
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int dp = threadIdx.x & 63, row = threadIdx.x >> 6;
+  const uint16_t* base = x + b * sb + h * sh + 2 * dp;
+  float m0 = 0.f, m1 = 0.f;
+#pragma unroll 8
+  for (int t = row; t < T; t += 16) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(base + (int64_t)t * st);
+    m0 = fmaxf(m0, fabsf(to_f<DT>((uint16_t)(w & 0xffffu))));
+    m1 = fmaxf(m1, fabsf(to_f<DT>((uint16_t)(w >> 16))));
+  }
+  red[row][2 * dp] = m0;
+  red[row][2 * dp + 1] = m1;
+  __syncthreads();
+  if (threadIdx.x < kD) {
+    float m = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) m = fmaxf(m, red[r][threadIdx.x]);
+    f[(int64_t)bh * kD + threadIdx.x] = from_f<DT>(sqrtf(m));
+  }
+}
+
 // --------------------------------------------------------------------------
 // Channel groups (per-token groups along head_dim): one warp per token row.
 // --------------------------------------------------------------------------
@@ -222,9 +250,217 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
 }
 
 // --------------------------------------------------------------------------
+// Row layout (keys, channel groups), one thread per (token, 32-dim block):
+// a warp covers 8 tokens x 4 blocks, a CTA of 8 warps 64 tokens of one
+// (batch, head).  Each thread reads its 64 bytes with four 16-byte loads,
+// reduces its group without shuffles (groups of 64 / 128 combine 2 / 4
+// threads), and builds whole 32-bit words of the packed tile in registers.
+// --------------------------------------------------------------------------
+
+// rint(clamp(rnd<DT>(a / s), 0, qmax)) for a >= 0, as the reference computes
+// it.  The quotient a * (1/s) in fp32 is within a few fp32 ulps of a / s, and
+// the reference's code differs from rint of that product only when a / s lies
+// within half a dtype ulp (<= 2^-8 for fp16, 2^-5 for bf16, at quotients
+// below 16) of a half-integer; those rare elements, and every element of a
+// group whose scale is 0 or not finite, take the exact division.
+template <int DT>
+__device__ __forceinline__ int fast_code(float a, float s, float rs, float rsf, float qmax, bool fast) {
+  if (fast) {
+    const float q = a * rsf;
+    const float c = rintf(q);
+    constexpr float kMargin = DT == F16 ? 0.015625f : 0.0625f;
+    if (fabsf(fabsf(q - c) - 0.5f) > kMargin) return (int)fminf(c, qmax);
+  }
+  return code_of(rnd<DT>(shared_div<DT>(a, s, rs)), qmax);
+}
+
+template <int DT, int BITS, int ASYM, int NORM>
+__global__ void __launch_bounds__(256)
+pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st, int T,
+                 const uint16_t* __restrict__ nf, int group, uint8_t* __restrict__ codes,
+                 uint16_t* __restrict__ scale, uint16_t* __restrict__ zero, int64_t cap_tiles,
+                 int64_t t_off) {
+  __shared__ float f_s[NORM ? kD : 1], rf_s[NORM ? kD : 1];
+  const int h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
+  const int64_t bh = (int64_t)b * H + h;
+  if constexpr (NORM) {
+    if (threadIdx.x < kD) {
+      const float f = to_f<DT>(nf[bh * kD + threadIdx.x]);
+      f_s[threadIdx.x] = f;
+      rf_s[threadIdx.x] = shared_rcp<DT>(f);
+    }
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31, kb = lane & 3;
+  const int t = blockIdx.x * 64 + (threadIdx.x >> 5) * 8 + (lane >> 2);
+  const bool valid = t < T;  // no early return: the group reductions shuffle
+  float v[32];
+  {
+    uint4 raw[4] = {};
+    if (valid) {
+      const uint4* p = reinterpret_cast<const uint4*>(x + b * sb + h * sh + (int64_t)t * st + kb * 32);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) raw[k] = p[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        v[8 * k + 2 * u] = to_f<DT>((uint16_t)(w[u] & 0xffffu));
+        v[8 * k + 2 * u + 1] = to_f<DT>((uint16_t)(w[u] >> 16));
+      }
+    }
+  }
+  if constexpr (NORM) {  // cache.py:125 key_states / factor, in the dtype
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const float f = f_s[kb * 32 + e];
+      v[e] = rnd<DT>((DT == F16 && f > 0.f && f < INFINITY) ? div_rn(v[e], f, rf_s[kb * 32 + e]) : v[e] / f);
+    }
+  }
+  float s, z = 0.f, qmax;
+  if constexpr (!ASYM) {
+    float mx = 0.f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fabsf(v[e]));
+    if (group >= 64) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    if (group >= 128) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    qmax = (float)qmax_sym<BITS>();
+    s = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx));
+  } else {
+    float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      mn = fminf(mn, v[e]);
+      mx = fmaxf(mx, v[e]);
+    }
+    if (group >= 64) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    }
+    if (group >= 128) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    }
+    qmax = (float)((1 << BITS) - 1);
+    s = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx - mn)));
+    z = mn;
+  }
+  const float rs = shared_rcp<DT>(s);
+  const bool fast = s > 0.f && s < INFINITY;
+  const float rsf = fast ? __frcp_rn(s) : 0.f;
+  // offset-binary codes of the thread's 32 dims: e = half*16 + 4*tq + i
+  int u[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    if constexpr (!ASYM) {
+      const int c = fast_code<DT>(fabsf(v[e]), s, rs, rsf, qmax, fast);
+      u[e] = (v[e] < 0.f ? -c : c) + (1 << (BITS - 1));
+    } else {
+      u[e] = fast_code<DT>(rnd<DT>(v[e] - z), s, rs, rsf, qmax, fast);
+    }
+  }
+  const int64_t p = t_off + t;
+  const int64_t ti = p >> 5;
+  const int r = (int)(p & 31), gid = r & 7, j = r >> 3;
+  uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
+  const int kpg = group >> 5;  // 32-dim blocks per group
+  if (valid && kb % kpg == 0) {
+    const int ng = kD / group, g = kb / kpg;
+    const int64_t si = (bh * cap_tiles + ti) * 32 * ng + row_scale_idx(r, g, ng);
+    scale[si] = from_f<DT>(s);
+    if (ASYM) zero[si] = from_f<DT>(z);
+  }
+  // row layout words (see common.cuh) for each tq: the 8 codes i = 0..3,
+  // half = 0..1 at dims kb*32 + half*16 + 4*tq + i
+#pragma unroll
+  for (int tq = 0; tq < 4; ++tq) {
+    const int lane2 = gid * 4 + tq;
+    if constexpr (BITS == 4) {
+      uint32_t w = 0u;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) w |= (uint32_t)u[hf * 16 + 4 * tq + i] << (4 * (2 * i + hf));
+      if (valid) *reinterpret_cast<uint32_t*>(tb + j * 512 + lane2 * 16 + kb * 4) = w;
+    } else {
+      // low two bits: word kb>>1 of the row's 8 bytes, crumb 4i + (kb&1)*2 + half,
+      // shared with the neighbouring block kb^1
+      uint32_t w = 0u, wh = 0u;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint32_t c = (uint32_t)u[hf * 16 + 4 * tq + i];
+          w |= (c & 3u) << (2 * (4 * i + (kb & 1) * 2 + hf));
+          if (BITS == 3) wh |= ((c >> 2) & 1u) << (8 * i + kb * 2 + hf);
+        }
+      w |= __shfl_xor_sync(0xffffffffu, w, 1);
+      if (valid && !(kb & 1))
+        *reinterpret_cast<uint32_t*>(tb + (j >> 1) * 512 + lane2 * 16 + (j & 1) * 8 + (kb >> 1) * 4) = w;
+      if constexpr (BITS == 3) {
+        wh |= __shfl_xor_sync(0xffffffffu, wh, 1);
+        wh |= __shfl_xor_sync(0xffffffffu, wh, 2);
+        if (valid && kb == 0) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = wh;
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
 // Col layout, token groups (V): one CTA of 128 threads (one per dim) per
 // group of `group` tokens.
 // --------------------------------------------------------------------------
+// The col-layout words of a group's tiles (values, 2-4 bits) from the codes
+// as words of 4 tokens per dim, cbt[dim][token / 4] (the layout map of
+// common.cuh), stored straight to global memory by threads tid of nthr.
+template <int BITS>
+__device__ __forceinline__ void store_col_tiles(const uint32_t (*cbt)[33], uint8_t* __restrict__ codes,
+                                                int64_t bh, int64_t cap_tiles, int64_t t_abs, int n_tiles,
+                                                int tid, int nthr) {
+  constexpr int TW = tile_bytes(BITS) / 4;
+    // every word of the group's tiles from 2-8 word loads of 4 tokens' codes
+    // (the col-layout map of common.cuh); stored straight to global memory
+    const int64_t ti0 = t_abs / 32;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(codes + (bh * cap_tiles + ti0) * tile_bytes(BITS));
+    for (int i = tid; i < n_tiles * TW; i += nthr) {
+      const int k = i / TW, wi = i % TW;
+      uint32_t w = 0u;
+      if (BITS == 4) {
+        const int pc = wi >> 7, L = (wi >> 2) & 31, c = wi & 3;
+        const int hh = c >> 1, hf = c & 1, g8 = L >> 2, tq = L & 3;
+        const int widx = 8 * k + hf * 4 + tq;
+        const int d0 = pc * 16 + hh * 8 + g8;
+        w = cbt[d0][widx] | (cbt[d0 + 64][widx] << 4);
+      } else if (BITS == 2) {
+        const int pc = wi >> 7, L = (wi >> 2) & 31, c = wi & 3;
+        const int hh = c >> 1, hf = c & 1, g8 = L >> 2, tq = L & 3;
+        const int widx = 8 * k + hf * 4 + tq;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w |= cbt[(2 * q + pc) * 16 + hh * 8 + g8][widx] << (2 * q);
+      } else if (wi < 256) {  // 3-bit plane L
+        const int L = (wi >> 2) & 31, mt = (wi >> 7) * 4 + (wi & 3);
+        const int g8 = L >> 2, tq = L & 3;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int hh = c >> 1, hf = c & 1;
+          w |= (cbt[mt * 16 + hh * 8 + g8][8 * k + hf * 4 + tq] & 0x03030303u) << (2 * c);
+        }
+      } else {  // 3-bit plane H
+        const int wj = wi - 256, L = wj >> 2, mq = wj & 3;
+        const int g8 = L >> 2, tq = L & 3;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int m1 = c >> 2, hh = (c >> 1) & 1, hf = c & 1;
+          const int mt = 2 * mq + m1;
+          w |= ((cbt[mt * 16 + hh * 8 + g8][8 * k + hf * 4 + tq] >> 2) & 0x01010101u) << c;
+        }
+      }
+      dst[(int64_t)k * TW + wi] = w;
+    }
+}
+
 // One group of `group` tokens of pair bh (x0: its first token, dim 0; token
 // stride st), stored at packed position t_abs; 128 threads, one per dim.
 template <int DT, int BITS, int ROLEV>
@@ -291,45 +527,7 @@ __device__ __forceinline__ void pack_col_group(const uint16_t* __restrict__ x0, 
   const int n_tiles = group / 32;
   constexpr int TW = tile_bytes(BITS) / 4;
   if constexpr (kWords) {
-    // every word of the group's tiles from 2-8 word loads of 4 tokens' codes
-    // (the col-layout map of common.cuh); stored straight to global memory
-    const int64_t ti0 = t_abs / 32;
-    uint32_t* dst = reinterpret_cast<uint32_t*>(codes + (bh * cap_tiles + ti0) * tile_bytes(BITS));
-    for (int i = threadIdx.x; i < n_tiles * TW; i += blockDim.x) {
-      const int k = i / TW, wi = i % TW;
-      uint32_t w = 0u;
-      if (BITS == 4) {
-        const int pc = wi >> 7, L = (wi >> 2) & 31, c = wi & 3;
-        const int hh = c >> 1, hf = c & 1, g8 = L >> 2, tq = L & 3;
-        const int widx = 8 * k + hf * 4 + tq;
-        const int d0 = pc * 16 + hh * 8 + g8;
-        w = cbt[d0][widx] | (cbt[d0 + 64][widx] << 4);
-      } else if (BITS == 2) {
-        const int pc = wi >> 7, L = (wi >> 2) & 31, c = wi & 3;
-        const int hh = c >> 1, hf = c & 1, g8 = L >> 2, tq = L & 3;
-        const int widx = 8 * k + hf * 4 + tq;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) w |= cbt[(2 * q + pc) * 16 + hh * 8 + g8][widx] << (2 * q);
-      } else if (wi < 256) {  // 3-bit plane L
-        const int L = (wi >> 2) & 31, mt = (wi >> 7) * 4 + (wi & 3);
-        const int g8 = L >> 2, tq = L & 3;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int hh = c >> 1, hf = c & 1;
-          w |= (cbt[mt * 16 + hh * 8 + g8][8 * k + hf * 4 + tq] & 0x03030303u) << (2 * c);
-        }
-      } else {  // 3-bit plane H
-        const int wj = wi - 256, L = wj >> 2, mq = wj & 3;
-        const int g8 = L >> 2, tq = L & 3;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int m1 = c >> 2, hh = (c >> 1) & 1, hf = c & 1;
-          const int mt = 2 * mq + m1;
-          w |= ((cbt[mt * 16 + hh * 8 + g8][8 * k + hf * 4 + tq] >> 2) & 0x01010101u) << c;
-        }
-      }
-      dst[(int64_t)k * TW + wi] = w;
-    }
+    store_col_tiles<BITS>(cbt, codes, bh, cap_tiles, t_abs, n_tiles, threadIdx.x, blockDim.x);
     return;
   }
   // assemble each 32-token tile of the group in shared memory with the layout map
@@ -351,6 +549,100 @@ __device__ __forceinline__ void pack_col_group(const uint16_t* __restrict__ x0, 
   uint4* dst = reinterpret_cast<uint4*>(codes + (bh * cap_tiles + ti0) * tile_bytes(BITS));
   const uint4* src = reinterpret_cast<const uint4*>(tw);
   for (int i = threadIdx.x; i < n_tiles * TW / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+// Values, token groups, 2-4 bits (col layout): one CTA of 64 threads per
+// group, each thread two adjacent dims read as 4-byte words (a warp reads 128
+// contiguous bytes of a token row).  The group is read in chunks of 32 tokens
+// held in registers: once for its max (min) and, for groups above 32 tokens,
+// once more for the codes (from L2).  Codes use fast_code's exact rounding.
+template <int DT, int BITS, int ASYM>
+__global__ void __launch_bounds__(64)
+pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st, int group,
+                 uint8_t* __restrict__ codes, uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
+                 int64_t cap_tiles, int64_t t_off) {
+  __shared__ uint32_t cbt[kD][33];
+  const int gi = blockIdx.x, h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
+  const int64_t bh = (int64_t)b * H + h;
+  const int dp = threadIdx.x;  // dims 2dp, 2dp+1
+  const uint16_t* x0 = x + b * sb + h * sh + (int64_t)gi * group * st + 2 * dp;
+  float2 v[32];
+  auto load = [&](int c0) {
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(x0 + (int64_t)(c0 + t) * st);
+      v[t] = make_float2(to_f<DT>((uint16_t)(w & 0xffffu)), to_f<DT>((uint16_t)(w >> 16)));
+    }
+  };
+  float mx0 = ASYM ? -INFINITY : 0.f, mx1 = mx0, mn0 = INFINITY, mn1 = INFINITY;
+  for (int c0 = 0; c0 < group; c0 += 32) {
+    load(c0);
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
+      if (ASYM) {
+        mx0 = fmaxf(mx0, v[t].x); mx1 = fmaxf(mx1, v[t].y);
+        mn0 = fminf(mn0, v[t].x); mn1 = fminf(mn1, v[t].y);
+      } else {
+        mx0 = fmaxf(mx0, fabsf(v[t].x)); mx1 = fmaxf(mx1, fabsf(v[t].y));
+      }
+    }
+  }
+  float s[2], z[2] = {0.f, 0.f};
+  float qmax;
+  if (ASYM) {
+    qmax = (float)((1 << BITS) - 1);
+    s[0] = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx0 - mn0)));
+    s[1] = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx1 - mn1)));
+    z[0] = mn0; z[1] = mn1;
+  } else {
+    qmax = (float)qmax_sym<BITS>();
+    s[0] = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx0));
+    s[1] = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx1));
+  }
+  float rs[2], rsf[2];
+  bool fast[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    rs[e] = shared_rcp<DT>(s[e]);
+    fast[e] = s[e] > 0.f && s[e] < INFINITY;
+    rsf[e] = fast[e] ? __frcp_rn(s[e]) : 0.f;
+  }
+  for (int c0 = 0; c0 < group; c0 += 32) {
+    if (group > 32) load(c0);
+#pragma unroll
+    for (int t4 = 0; t4 < 8; ++t4) {
+      uint32_t w[2] = {0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 xv = v[4 * t4 + i];
+        const float xe[2] = {xv.x, xv.y};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          uint32_t uc;
+          if (ASYM) {
+            uc = (uint32_t)fast_code<DT>(rnd<DT>(xe[e] - z[e]), s[e], rs[e], rsf[e], qmax, fast[e]);
+          } else {
+            const int c = fast_code<DT>(fabsf(xe[e]), s[e], rs[e], rsf[e], qmax, fast[e]);
+            uc = (uint32_t)((xe[e] < 0.f ? -c : c) + (1 << (BITS - 1)));
+          }
+          w[e] |= uc << (8 * i);
+        }
+      }
+      cbt[2 * dp][(c0 >> 2) + t4] = w[0];
+      cbt[2 * dp + 1][(c0 >> 2) + t4] = w[1];
+    }
+  }
+  const int64_t groups_cap = cap_tiles * 32 / group;
+  const int64_t t_abs = t_off + (int64_t)gi * group;
+  const int64_t gglob = t_abs / group;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int64_t si = (bh * groups_cap + gglob) * kD + col_scale_idx(2 * dp + e);
+    scale[si] = from_f<DT>(s[e]);
+    if (ASYM) zero[si] = from_f<DT>(z[e]);
+  }
+  __syncthreads();
+  store_col_tiles<BITS>(cbt, codes, bh, cap_tiles, t_abs, group / 32, threadIdx.x, 64);
 }
 
 template <int DT, int BITS, int ROLEV>
@@ -601,8 +893,14 @@ __global__ void dequant_ref_kernel(const int32_t* __restrict__ c, const uint16_t
 
 cudaError_t launch_norm_factor(const void* x, int dt, int B, int H, int T, int64_t sb, int64_t sh,
                                int64_t st, void* f, cudaStream_t s) {
-  DT_DISPATCH(dt, norm_factor_kernel<DTC><<<B * H, kD, 0, s>>>(
-                      (const uint16_t*)x, sb, sh, st, H, T, (uint16_t*)f));
+  const bool rows4 = ((uintptr_t)x % 4 == 0) && sb % 2 == 0 && sh % 2 == 0 && st % 2 == 0;
+  if (rows4) {
+    DT_DISPATCH(dt, norm_factor_wide_kernel<DTC><<<B * H, 1024, 0, s>>>(
+                        (const uint16_t*)x, sb, sh, st, H, T, (uint16_t*)f));
+  } else {
+    DT_DISPATCH(dt, norm_factor_kernel<DTC><<<B * H, kD, 0, s>>>(
+                        (const uint16_t*)x, sb, sh, st, H, T, (uint16_t*)f));
+  }
   return cudaGetLastError();
 }
 
@@ -625,11 +923,34 @@ cudaError_t launch_append_step(const AppendArgs& g, const int64_t* step, cudaStr
   return cudaGetLastError();
 }
 
+// rows of 16-byte aligned, 16-byte strided 16-bit values
+static bool rows16(const void* x, int64_t sb, int64_t sh, int64_t st) {
+  return (uintptr_t)x % 16 == 0 && sb % 8 == 0 && sh % 8 == 0 && st % 8 == 0;
+}
+
 cudaError_t launch_pack(const void* x, int dt, int B, int H, int T, int64_t sb, int64_t sh,
                         int64_t st, int bits, int group, int asym, int role_v, int over_token,
                         const void* nf, void* codes, void* scale, void* zero, int64_t cap_tiles,
                         int64_t t_off, cudaStream_t s) {
-  if (!over_token) {
+  if (!over_token && !role_v && bits >= 2 && rows16(x, sb, sh, st)) {
+    // keys, channel groups: one thread per (token, 32-dim block)
+    const dim3 grid((unsigned)((T + 63) / 64), (unsigned)H, (unsigned)B);
+#define PACK_ROWS(A, N)                                                                          \
+  DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_rows_kernel<DTC, (BC < 2 ? 2 : BC), A, N><<<grid, 256, 0, s>>>( \
+                                          (const uint16_t*)x, sb, sh, st, T, (const uint16_t*)nf,   \
+                                          group, (uint8_t*)codes, (uint16_t*)scale, (uint16_t*)zero,  \
+                                          cap_tiles, t_off)))
+    if (asym && nf) {
+      PACK_ROWS(1, 1);
+    } else if (asym) {
+      PACK_ROWS(1, 0);
+    } else if (nf) {
+      PACK_ROWS(0, 1);
+    } else {
+      PACK_ROWS(0, 0);
+    }
+#undef PACK_ROWS
+  } else if (!over_token) {
     const dim3 grid((unsigned)((T + 31) / 32), (unsigned)H, (unsigned)B);
     if (role_v) {
       DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC, 1><<<grid, 256, 0, s>>>(
@@ -640,6 +961,18 @@ cudaError_t launch_pack(const void* x, int dt, int B, int H, int T, int64_t sb, 
       DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_row_channel_kernel<DTC, BC, 0><<<grid, 256, 0, s>>>(
                                               (const uint16_t*)x, sb, sh, st, H, T,
                                               (const uint16_t*)nf, group, asym, (uint8_t*)codes,
+                                              (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off)));
+    }
+  } else if (role_v && bits >= 2 && (uintptr_t)x % 4 == 0 && sb % 2 == 0 && sh % 2 == 0 && st % 2 == 0) {
+    // values, token groups: 64 threads x 2 dims per group
+    dim3 grid(T / group, H, B);
+    if (asym) {
+      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_cols_kernel<DTC, (BC < 2 ? 2 : BC), 1><<<grid, 64, 0, s>>>(
+                                              (const uint16_t*)x, sb, sh, st, group, (uint8_t*)codes,
+                                              (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off)));
+    } else {
+      DT_DISPATCH(dt, BITS_DISPATCH(bits, pack_cols_kernel<DTC, (BC < 2 ? 2 : BC), 0><<<grid, 64, 0, s>>>(
+                                              (const uint16_t*)x, sb, sh, st, group, (uint8_t*)codes,
                                               (uint16_t*)scale, (uint16_t*)zero, cap_tiles, t_off)));
     }
   } else {

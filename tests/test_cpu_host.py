@@ -158,3 +158,19 @@ def test_noalloc_returns_the_plan_status_without_a_gpu():
         r1 = lib.innerq_decode_attn(ctypes.byref(a), None, 0, None, 0, 0, None, None)
         r2 = lib.innerq_decode_attn_noalloc(ctypes.byref(a), None, 0, 0, None, None)
         assert r1 == r2 == expect, (r1, r2)
+
+
+def test_reference_import_names_resolve_to_this_package():
+    """`from innerq.cache import ...` (the reference's import paths) reaches
+    the B200 modules unchanged."""
+    import innerq
+    import innerq.cache
+    import innerq.models.llama_innerq
+    import innerq_b200.cache
+    import innerq_b200.models.llama_innerq
+    from innerq.cache import DynamicCache, InnerqDynamicLayer  # noqa: F401
+    from innerq.models import InnerqLlamaForCausalLM, InnerqMistralForCausalLM  # noqa: F401
+    from innerq.quant import QMode, quantize_channeldim_sym  # noqa: F401
+    assert innerq.cache is innerq_b200.cache
+    assert innerq.models.llama_innerq is innerq_b200.models.llama_innerq
+    assert innerq.quant.QMode is innerq_b200.quant.QMode

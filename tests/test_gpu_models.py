@@ -66,3 +66,46 @@ def test_generate_installs_innerq_cache():
     assert isinstance(out.past_key_values, DynamicCache)
     assert out.sequences.shape[1] == 73
     assert out.past_key_values.layers[0].get_seq_length() == 72
+
+
+def test_sliding_window_layer_returns_the_window():
+    """cache.py:421-461: a sliding layer returns the tail of what a full layer
+    returns for the same tokens, as many tokens as its get_mask_sizes
+    describes (window - 1 + 1 once the window is full; the reference's
+    [:, :, -window, :] at cache.py:443-444 would keep one token)."""
+    from innerq_b200.cache import InnerqDynamicLayer, InnerqDynamicSlidingWindowLayer
+    from tests._util import cfg, synth_kv
+    W = 48
+    full = InnerqDynamicLayer(cfg(**QCFG), 0)
+    sl = InnerqDynamicSlidingWindowLayer(cfg(**QCFG), 0, sliding_window=W)
+    k, v = synth_kv(2, 2, 140, seed=9)
+    for layer in (full, sl):
+        layer.update(k[:, :, :100], v[:, :, :100])
+    for t in range(100, 140):
+        kv_len, kv_off = sl.get_mask_sizes(1)
+        Kf, Vf = full.update(k[:, :, t:t + 1], v[:, :, t:t + 1])
+        Ks, Vs = sl.update(k[:, :, t:t + 1], v[:, :, t:t + 1])
+        assert Ks.shape[2] == kv_len == W and kv_off == t - W + 1
+        torch.testing.assert_close(Ks, Kf[:, :, -W:], rtol=0, atol=0)
+        torch.testing.assert_close(Vs, Vf[:, :, -W:], rtol=0, atol=0)
+    assert sl.get_max_cache_shape() == W and sl.get_seq_length() == 140
+
+
+def test_mistral_sliding_window_decodes():
+    """A Mistral config with a sliding window gets sliding InnerQ layers and
+    decodes through them (HF sliding mask + the cropped dequantized window)."""
+    from transformers import MistralConfig
+    from innerq_b200 import models
+    from innerq_b200.cache import InnerqDynamicSlidingWindowLayer
+    torch.manual_seed(0)
+    c = MistralConfig(num_hidden_layers=2, hidden_size=512, num_attention_heads=8,
+                      num_key_value_heads=2, head_dim=128, intermediate_size=256,
+                      vocab_size=512, sliding_window=64, **QCFG)
+    m = models.InnerqMistralForCausalLM(c).to("cuda", torch.float16).eval()
+    ids = torch.randint(0, 512, (2, 100), device="cuda", generator=torch.Generator("cuda").manual_seed(3))
+    with torch.no_grad():
+        out = m.generate(ids, max_new_tokens=30, do_sample=False, return_dict_in_generate=True)
+    cache = out.past_key_values
+    assert all(isinstance(l, InnerqDynamicSlidingWindowLayer) for l in cache.layers)
+    assert out.sequences.shape[1] == 130
+    assert cache.layers[0].get_seq_length() == 129

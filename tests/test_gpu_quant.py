@@ -101,3 +101,60 @@ def test_bad_inputs_raise():
     with pytest.raises(ValueError):
         M.QMode.from_str("nope")
     assert InnerqError is not None
+
+
+def _boundary_rows(dtype, bits, asym, n_rows=512, seed=0):
+    """Rows of groups of 32 whose elements sit on and a few dtype ulps around
+    the values where |x| / s (or (x - min) / s) crosses a half-integer, the
+    cases where the rounding of the quotient decides the code."""
+    rng = np.random.default_rng(seed)
+    qmax = (1 << bits) - 1 if asym else (1 << (bits - 1)) - 1
+    out = np.zeros((n_rows, 128), np.float32)
+    for r in range(n_rows):
+        for g in range(4):
+            M = float(Q.rnd(np.float32(rng.uniform(0.05, 30.0)), dtype))
+            lo = float(Q.rnd(np.float32(-rng.uniform(0.0, 5.0)), dtype)) if asym else 0.0
+            rng_ = float(Q.rnd(np.float32(M - lo), dtype)) if asym else M
+            s = float(Q.rnd(np.float32(rng_ / qmax), dtype))
+            vals = [M, lo] if asym else [M]
+            while len(vals) < 32:
+                k = rng.integers(0, qmax)
+                base = Q.rnd(np.float32(lo + (k + 0.5) * s), dtype)
+                bits16 = (base.astype(np.float16).view(np.uint16) if dtype == "fp16"
+                          else Q.f32_to_bf16_bits(base))
+                nbi = int(bits16) + int(rng.integers(-3, 4))
+                if not 0 <= nbi <= 0xFFFF:
+                    continue
+                nb = np.uint16(nbi)
+                v = (np.array([nb], np.uint16).view(np.float16).astype(np.float32)[0] if dtype == "fp16"
+                     else Q.bf16_bits_to_f32(np.array([nb]))[0])
+                if not np.isfinite(v) or v > M or v < lo:
+                    continue
+                if not asym and rng.integers(0, 2):
+                    v = -v
+                vals.append(v)
+            out[r, 32 * g:32 * g + 32] = rng.permutation(np.array(vals, np.float32))
+    return out[None, None]
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("asym", [False, True])
+@pytest.mark.parametrize("over", ["channel", "token"])
+def test_quantize_half_integer_boundaries(dtype, bits, asym, over):
+    """Quantizers on inputs built around the rounding boundaries of the
+    quotient (the fast path's fallback cases) vs the oracle; token groups get
+    the same groups transposed onto the token axis."""
+    xo = _boundary_rows(dtype, bits, asym, n_rows=512 if over == "channel" else 128,
+                        seed=bits + 10 * asym)
+    if over == "token":
+        xo = np.ascontiguousarray(xo.swapaxes(-1, -2))
+    x = torch.from_numpy(xo).to(TDT[dtype]).cuda()
+    ours = _ours()[f"{over}_{'asym' if asym else 'sym'}"][0]
+    c, s, z = ours(x, 32, bits)
+    fn = Q.quantize_asym if asym else Q.quantize_sym
+    rc, rs, rz = fn(to_np32(x), 32, bits, 3 if over == "channel" else 2, dtype)
+    rc = np.where(rc == Q.INT32_MIN, 0, rc)
+    np.testing.assert_array_equal(c.cpu().numpy(), rc)
+    np.testing.assert_array_equal(to_np32(s), rs)
+    np.testing.assert_array_equal(to_np32(z), rz)
