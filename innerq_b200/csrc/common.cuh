@@ -98,6 +98,106 @@ __device__ __forceinline__ float div_rn(float a, float b, float rb) {
   return r == 0.f ? q : __fmaf_rn(r, rb, q);
 }
 
+// rint(clamp(q, 0, qmax)) with a NaN quotient (0 / 0 scale) giving code 0:
+// fmaxf returns its non-NaN operand; adding 1.5 * 2^23 rounds to the nearest
+// integer, ties to even, like rintf (q <= 15 here)
+__device__ __forceinline__ int code_of(float q, float qmax) {
+  return __float_as_int(fminf(fmaxf(q, 0.f), qmax) + 12582912.f) - 0x4B400000;
+}
+
+// ------------------------------------------------- codes by thresholds ---
+// The reference's code of a >= 0 in a group of scale s > 0 is
+//   c(a) = rint(clamp(rnd_dt(RN32(a / s)), 0, qmax))          (quant.py:71-72, 107-109)
+// (RN32: the fp32 quotient of a torch half op, rnd_dt: rounding to fp16 /
+// bf16, rint ties to even).  c is non-decreasing in a, so c(a) >= k exactly
+// when a passes a cut that depends only on k, the dtype and s:
+//   * rint(v) >= k for a dtype value v  <=>  v >= H_k, with H_k = k - 1/2 for
+//     even k (the tie rounds up to k) and the next dtype value after k - 1/2
+//     for odd k;
+//   * rnd_dt(y) >= H_k for an fp32 value y  <=>  y >= Y_k, with Y_k the
+//     midpoint between H_k and the dtype value below it, moved up one fp32 ulp
+//     when H_k's significand is odd (a tie then rounds down);
+//   * RN32(a / s) >= Y_k  <=>  a / s > M_k, or a / s == M_k when Y_k's fp32
+//     significand is even (the tie rounds up), M_k the midpoint between Y_k
+//     and the fp32 value below it.
+// M_k * s has at most 25 + 11 significant bits, exact in fp64, and a is an
+// fp32 value, so the cut in a is the fp32 value just at or above M_k * s.
+// Per group: one fp64 product and rounding per k; per element: a comparison
+// tree over the qmax cuts.  Tested against the fp32 division for every pair
+// of non-negative fp16 / bf16 values (tests/cuda/code_check.cu).
+__host__ __device__ constexpr double pow2_floor(double v) {
+  double p = 1.0;
+  while (p * 2.0 <= v) p *= 2.0;
+  while (p > v) p *= 0.5;
+  return p;
+}
+// spacing of a binary float with `mb` fraction bits at v > 0 (normal range)
+__host__ __device__ constexpr double ulp_at(double v, int mb) { return pow2_floor(v) / (double)(1ll << mb); }
+__host__ __device__ constexpr double ulp_below(double v, int mb) {
+  return pow2_floor(v) == v ? 0.5 * ulp_at(v, mb) : ulp_at(v, mb);
+}
+__host__ __device__ constexpr bool odd_at(double v, int mb) { return ((long long)(v / ulp_at(v, mb))) & 1; }
+// dtype fraction bits: fp16 10, bf16 7; fp32 23
+__host__ __device__ constexpr double cut_h(int k, int mb) {
+  return (k & 1) ? (k - 0.5) + ulp_at(k - 0.5, mb) : k - 0.5;
+}
+__host__ __device__ constexpr double cut_y(int k, int mb) {
+  const double h = cut_h(k, mb);
+  const double mid = h - 0.5 * ulp_below(h, mb);
+  return odd_at(h, mb) ? mid + ulp_at(mid, 23) : mid;
+}
+__host__ __device__ constexpr double cut_m(int k, int mb) {
+  const double y = cut_y(k, mb);
+  return y - 0.5 * ulp_below(y, 23);
+}
+__host__ __device__ constexpr bool cut_even(int k, int mb) { return !odd_at(cut_y(k, mb), 23); }
+
+// the fp32 cut of code k for scale s (as fp64): a passes it iff c(a) >= k
+template <int MB, int K>
+__device__ __forceinline__ float code_cut(double sd) {
+  constexpr double m = cut_m(K, MB);
+  constexpr bool even = cut_even(K, MB);
+  const double t = m * sd;
+  float a = __double2float_ru(t);
+  if (!even && (double)a == t) a = __uint_as_float(__float_as_uint(a) + 1u);  // strictly above
+  return a;
+}
+
+template <int MB, int QMAX, int K = 1>
+__device__ __forceinline__ void code_cuts(double sd, float* cut) {
+  if constexpr (K <= QMAX) {
+    cut[K - 1] = code_cut<MB, K>(sd);
+    code_cuts<MB, QMAX, K + 1>(sd, cut);
+  }
+}
+
+// c(a) from the cuts (QMAX = 1, 3, 7, 15): a binary search by selects
+template <int QMAX>
+__device__ __forceinline__ int code_by_cuts(float a, const float* cut) {
+  if constexpr (QMAX == 1) {
+    return a >= cut[0];
+  } else if constexpr (QMAX == 3) {
+    const int b1 = a >= cut[1];
+    const int b0 = a >= (b1 ? cut[2] : cut[0]);
+    return 2 * b1 + b0;
+  } else if constexpr (QMAX == 7) {
+    const int b2 = a >= cut[3];
+    const int b1 = a >= (b2 ? cut[5] : cut[1]);
+    const float c0 = b2 ? (b1 ? cut[6] : cut[4]) : (b1 ? cut[2] : cut[0]);
+    return 4 * b2 + 2 * b1 + (a >= c0);
+  } else {
+    const int b3 = a >= cut[7];
+    const int b2 = a >= (b3 ? cut[11] : cut[3]);
+    const float c1 = b3 ? (b2 ? cut[13] : cut[9]) : (b2 ? cut[5] : cut[1]);
+    const int b1 = a >= c1;
+    const int i0 = 8 * b3 + 4 * b2 + 2 * b1;  // cut index i0 (+1 - 1)
+    float c0 = cut[0];
+#pragma unroll
+    for (int i = 2; i < 16; i += 2) c0 = i0 == i ? cut[i] : c0;
+    return i0 + (a >= c0);
+  }
+}
+
 // ------------------------------------------------------------------ mma ---
 __device__ __forceinline__ void mma_f16(float c[4], const uint32_t a[4], const uint32_t b[2]) {
   asm(

@@ -25,12 +25,6 @@ namespace innerq {
 template <int BITS>
 __device__ __forceinline__ int qmax_sym() { return (1 << (BITS - 1)) - 1; }
 
-// rint(clamp(q, 0, qmax)) with a NaN quotient (0 / 0 scale) giving code 0:
-// fmaxf returns its non-NaN operand; adding 1.5 * 2^23 rounds to the nearest
-// integer, ties to even, like rintf (q <= 15 here)
-__device__ __forceinline__ int code_of(float q, float qmax) {
-  return __float_as_int(fminf(fmaxf(q, 0.f), qmax) + 12582912.f) - 0x4B400000;
-}
 
 // a / b as the IEEE fp32 '/' computes it for a non-negative numerator and a
 // divisor shared by many numerators: fp16 operands take Markstein's sequence
@@ -257,21 +251,20 @@ pack_row_channel_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, 
 // threads), and builds whole 32-bit words of the packed tile in registers.
 // --------------------------------------------------------------------------
 
-// rint(clamp(rnd<DT>(a / s), 0, qmax)) for a >= 0, as the reference computes
-// it.  The quotient a * (1/s) in fp32 is within a few fp32 ulps of a / s, and
-// the reference's code differs from rint of that product only when a / s lies
-// within half a dtype ulp (<= 2^-8 for fp16, 2^-5 for bf16, at quotients
-// below 16) of a half-integer; those rare elements, and every element of a
-// group whose scale is 0 or not finite, take the exact division.
-template <int DT>
-__device__ __forceinline__ int fast_code(float a, float s, float rs, float rsf, float qmax, bool fast) {
-  if (fast) {
-    const float q = a * rsf;
-    const float c = rintf(q);
-    constexpr float kMargin = DT == F16 ? 0.015625f : 0.0625f;
-    if (fabsf(fabsf(q - c) - 0.5f) > kMargin) return (int)fminf(c, qmax);
+// dtype fraction bits (the cuts of common.cuh depend on them)
+template <int DT> constexpr int kMantBits = DT == F16 ? 10 : 7;
+
+// the cuts of a group of scale s >= 0.  The reference divides by a scale of 0
+// too: a / 0 is inf for a > 0 (code qmax) and NaN for a = 0 (code 0), so every
+// cut sits just above 0; a / inf is 0 (code 0), so every cut is inf.
+template <int DT, int QM>
+__device__ __forceinline__ void group_cuts(float s, float* cut) {
+  if (s > 0.f && s < INFINITY) {
+    code_cuts<kMantBits<DT>, QM>((double)s, cut);
+  } else {
+#pragma unroll
+    for (int k = 0; k < QM; ++k) cut[k] = s == 0.f ? __uint_as_float(1u) : INFINITY;
   }
-  return code_of(rnd<DT>(shared_div<DT>(a, s, rs)), qmax);
 }
 
 template <int DT, int BITS, int ASYM, int NORM>
@@ -347,20 +340,24 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
     s = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx - mn)));
     z = mn;
   }
-  const float rs = shared_rcp<DT>(s);
-  const bool fast = s > 0.f && s < INFINITY;
-  const float rsf = fast ? __frcp_rn(s) : 0.f;
-  // offset-binary codes of the thread's 32 dims: e = half*16 + 4*tq + i
+  // offset-binary codes of the thread's 32 dims (e = half*16 + 4*tq + i) by
+  // the group's cuts
   int u[32];
+  auto codes_with = [&](auto code) {
 #pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    if constexpr (!ASYM) {
-      const int c = fast_code<DT>(fabsf(v[e]), s, rs, rsf, qmax, fast);
-      u[e] = (v[e] < 0.f ? -c : c) + (1 << (BITS - 1));
-    } else {
-      u[e] = fast_code<DT>(rnd<DT>(v[e] - z), s, rs, rsf, qmax, fast);
+    for (int e = 0; e < 32; ++e) {
+      if constexpr (!ASYM) {
+        const int c = code(fabsf(v[e]));
+        u[e] = (v[e] < 0.f ? -c : c) + (1 << (BITS - 1));
+      } else {
+        u[e] = code(rnd<DT>(v[e] - z));
+      }
     }
-  }
+  };
+  constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
+  float cut[QM];
+  group_cuts<DT, QM>(s, cut);
+  codes_with([&](float a) { return code_by_cuts<QM>(a, cut); });
   const int64_t p = t_off + t;
   const int64_t ti = p >> 5;
   const int r = (int)(p & 31), gid = r & 7, j = r >> 3;
@@ -599,39 +596,38 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
     s[0] = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx0));
     s[1] = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx1));
   }
-  float rs[2], rsf[2];
-  bool fast[2];
+  constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
+  float cut[2][QM];
+  group_cuts<DT, QM>(s[0], cut[0]);
+  group_cuts<DT, QM>(s[1], cut[1]);
+  auto codes_with = [&](auto code) {
+    for (int c0 = 0; c0 < group; c0 += 32) {
+      if (group > 32) load(c0);
 #pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    rs[e] = shared_rcp<DT>(s[e]);
-    fast[e] = s[e] > 0.f && s[e] < INFINITY;
-    rsf[e] = fast[e] ? __frcp_rn(s[e]) : 0.f;
-  }
-  for (int c0 = 0; c0 < group; c0 += 32) {
-    if (group > 32) load(c0);
+      for (int t4 = 0; t4 < 8; ++t4) {
+        uint32_t w[2] = {0u, 0u};
 #pragma unroll
-    for (int t4 = 0; t4 < 8; ++t4) {
-      uint32_t w[2] = {0u, 0u};
+        for (int i = 0; i < 4; ++i) {
+          const float2 xv = v[4 * t4 + i];
+          const float xe[2] = {xv.x, xv.y};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 xv = v[4 * t4 + i];
-        const float xe[2] = {xv.x, xv.y};
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          uint32_t uc;
-          if (ASYM) {
-            uc = (uint32_t)fast_code<DT>(rnd<DT>(xe[e] - z[e]), s[e], rs[e], rsf[e], qmax, fast[e]);
-          } else {
-            const int c = fast_code<DT>(fabsf(xe[e]), s[e], rs[e], rsf[e], qmax, fast[e]);
-            uc = (uint32_t)((xe[e] < 0.f ? -c : c) + (1 << (BITS - 1)));
+          for (int e = 0; e < 2; ++e) {
+            uint32_t uc;
+            if (ASYM) {
+              uc = (uint32_t)code(rnd<DT>(xe[e] - z[e]), e);
+            } else {
+              const int c = code(fabsf(xe[e]), e);
+              uc = (uint32_t)((xe[e] < 0.f ? -c : c) + (1 << (BITS - 1)));
+            }
+            w[e] |= uc << (8 * i);
           }
-          w[e] |= uc << (8 * i);
         }
+        cbt[2 * dp][(c0 >> 2) + t4] = w[0];
+        cbt[2 * dp + 1][(c0 >> 2) + t4] = w[1];
       }
-      cbt[2 * dp][(c0 >> 2) + t4] = w[0];
-      cbt[2 * dp + 1][(c0 >> 2) + t4] = w[1];
     }
-  }
+  };
+  codes_with([&](float a, int e) { return code_by_cuts<QM>(a, cut[e]); });
   const int64_t groups_cap = cap_tiles * 32 / group;
   const int64_t t_abs = t_off + (int64_t)gi * group;
   const int64_t gglob = t_abs / group;

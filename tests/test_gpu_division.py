@@ -30,3 +30,21 @@ def test_markstein_division_matches_ieee_for_all_fp16_pairs():
         n_bad, first = ctypes.c_ulonglong(0), ctypes.c_uint(0)
         assert lib.div_check(ctypes.byref(n_bad), ctypes.byref(first)) == 0
     assert n_bad.value == 0, f"{n_bad.value} mismatches, first a/b bits {first.value:#010x}"
+
+
+@pytest.mark.parametrize("dtype", [0, 1], ids=["fp16", "bf16"])
+def test_code_cuts_match_division_for_all_pairs(dtype):
+    """The packers compute codes from per-group cuts instead of dividing each
+    element (csrc/common.cuh, code_cuts): checked against rint(clamp(rnd(a/s)))
+    with the IEEE quotient for every non-negative a and positive s of the dtype
+    (~10^9 pairs), qmax 1, 3, 7, 15."""
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    with tempfile.TemporaryDirectory() as d:
+        so = os.path.join(d, "code_check.so")
+        subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-shared",
+                        "-Xcompiler", "-fPIC", "-I", CSRC, "-o", so,
+                        os.path.join(HERE, "cuda", "code_check.cu")], check=True)
+        lib = ctypes.CDLL(so)
+        n_bad, first = ctypes.c_ulonglong(0), ctypes.c_uint(0)
+        assert lib.code_check(dtype, ctypes.byref(n_bad), ctypes.byref(first)) == 0
+    assert n_bad.value == 0, f"{n_bad.value} mismatches, first a/s bits {first.value:#010x}"
