@@ -65,11 +65,16 @@ def parse():
                     help="launch every kernel from the host each step instead of replaying the "
                          "recorded decode step (CUDA graph, cache graph mode)")
     ap.add_argument("--only", default=None,
-                    help="sweep: run only the rows whose name contains this text")
+                    help="sweep: run only the rows whose name contains this text (=NAME: exactly)")
     ap.add_argument("--sweep-ctx", type=int, default=None,
                     help="sweep: override the context of the selected rows (small profiling cases)")
     ap.add_argument("--sweep-batch", type=int, default=None,
                     help="sweep: override the batch of the selected rows")
+    ap.add_argument("--sweep-hkv", type=int, default=None,
+                    help="sweep: KV heads of the selected rows (a KV-head shard of a larger model)")
+    ap.add_argument("--split-scan", default=None,
+                    help="sweep: comma-separated split counts to time (0 = the planner's), "
+                         "attention only, one JSON line per count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="c1", choices=["c1", "c3", "c4", "sweep"],
@@ -138,20 +143,24 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, period_ms=20, enabled=True):
         self.gpu = gpu_index
+        self.period = period_ms
+        self.enabled = enabled
         self.proc = None
         self.f = None
         self.skip = 0
 
     def start(self):
-        """Start sampling every 20 ms and return once the first sample is in,
-        so that a short timed region that follows is covered."""
+        """Start sampling every `period_ms` and return once the first sample is
+        in, so that a short timed region that follows is covered."""
+        if not self.enabled:
+            return
         try:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "20"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.period)],
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -520,8 +529,9 @@ def run_ours(a):
             graph, gsteps[0], per_step_launches = None, None, None
             step = eager_step
 
-    # ---- device-resident timed region
-    sampler = ClockSampler(local)
+    # ---- device-resident timed region (rank 0 samples its GPU's clocks: one
+    #      nvidia-smi per rank at a short period slowed the host's launches)
+    sampler = ClockSampler(local, period_ms=20 if world == 1 else 100, enabled=rank == 0)
     nbytes = 0
     sync_all()
     sampler.start()
@@ -776,14 +786,20 @@ def run_sweep(a):
     dev = torch.device("cuda", 0)
     peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("hbm_gbs", 6650.0)) \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
+    done = set()
     for name, B, hq, ctx, bits, group, vlay, mode in SWEEP:
-        if a.only is not None and a.only not in name:
+        if a.only is not None and (name != a.only[1:] if a.only.startswith("=") else a.only not in name):
             continue
         ctx = a.sweep_ctx or ctx
         B = a.sweep_batch or B
+        key = (name, B, hq, ctx, bits, group, vlay, mode)
+        if key in done:
+            continue
+        done.add(key)
         a2 = types.SimpleNamespace(kbits=bits, vbits=bits, group=group, v_layout=vlay, mode=mode)
         kw = cache_kw(a2)
-        hkv = 8
+        hkv = a.sweep_hkv or 8
+        hq = hq * hkv // 8
         per_layer = B * hkv * ctx * (bits * 32 + 16)
         nl = max(4, min(8, int(1.2e9 // per_layer) + 1))
         g = torch.Generator(device=dev)
@@ -800,30 +816,46 @@ def run_sweep(a):
             layers.append(layer)
         q = torch.randn((B, hq, 1, D), device=dev, generator=g).half()
         outs = [torch.empty((B, hq, D), dtype=q.dtype, device=dev) for _ in layers]
-        for l, o in zip(layers, outs):
-            decode_attention(q, l.key_side, l.value_side, out=o)
-        torch.cuda.synchronize()
-        reps = 4
-        st = torch.cuda.Stream(dev)
-        with torch.cuda.stream(st):
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=st):
-                for _ in range(reps):
-                    for l, o in zip(layers, outs):
-                        decode_attention(q, l.key_side, l.value_side, out=o)
-        torch.cuda.synchronize()
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(5):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (5 * reps * nl)
         nb = layer_bytes(layers[0], B, hkv, hq)
-        del graph, layers, outs
+
+        def time_attn(n_splits):
+            for l, o in zip(layers, outs):
+                decode_attention(q, l.key_side, l.value_side, out=o, n_splits=n_splits)
+            torch.cuda.synchronize()
+            reps = 4
+            st = torch.cuda.Stream(dev)
+            with torch.cuda.stream(st):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=st):
+                    for _ in range(reps):
+                        for l, o in zip(layers, outs):
+                            decode_attention(q, l.key_side, l.value_side, out=o, n_splits=n_splits)
+            torch.cuda.synchronize()
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(5):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) * 1e3 / (5 * reps * nl)
+
+        if a.split_scan:
+            from innerq_b200.attention import build_args, plan
+            for ns in [int(x) for x in a.split_scan.split(",")]:
+                eff = plan(build_args(q, layers[0].key_side, layers[0].value_side, n_splits=ns))[1]
+                us = time_attn(ns)
+                print(json.dumps({"config": name, "batch": B, "q_heads": hq, "kv_heads": hkv,
+                                  "context": ctx, "bits": bits, "n_splits": ns, "splits_used": eff,
+                                  "attn_us": round(us, 2), "attn_GBs": round(nb / us / 1e3, 1)}),
+                      flush=True)
+            del layers, outs
+            torch.cuda.empty_cache()
+            continue
+        us = time_attn(0)
+        del layers, outs
         torch.cuda.empty_cache()
         # append: one K token (channel groups) and one 4096-token chunk
         side = PackedSide(_lib.ROLE_K, bits, group, _lib.SYM if mode == "symmetric" else _lib.ASYM,

@@ -261,6 +261,7 @@ int innerq_norm_factor(const void* x, int dtype, int B, int H, int T, int D, int
   if (dtype != INNERQ_DT_F16 && dtype != INNERQ_DT_BF16) return fail(INNERQ_ERR_ARG, "dtype");
   if (D != kD) return fail(INNERQ_ERR_UNSUPPORTED, "head_dim %d", D);
   if (B <= 0 || H <= 0 || T <= 0 || !x || !out_f) return fail(INNERQ_ERR_ARG, "empty input");
+  if (B > 65535 || H > 65535) return fail(INNERQ_ERR_ARG, "B and H must be <= 65535 (grid limits)");
   return cuda_status(launch_norm_factor(x, dtype, B, H, T, sb, sh, st, out_f, (cudaStream_t)stream),
                      "norm_factor");
 }

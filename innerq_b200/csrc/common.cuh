@@ -44,7 +44,10 @@
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <utility>
 
 namespace innerq {
 
@@ -196,6 +199,38 @@ __device__ __forceinline__ int code_by_cuts(float a, const float* cut) {
     for (int i = 2; i < 16; i += 2) c0 = i0 == i ? cut[i] : c0;
     return i0 + (a >= c0);
   }
+}
+
+// ------------------------------------------- programmatic dependent launch ---
+// Every kernel of the decode step is launched as the programmatic dependent of
+// the previous kernel on its stream (launch_pdl), so its launch and prologue
+// overlap the tail of that kernel.  The rules that keep stream order:
+//   * each kernel calls griddep_wait() before it reads or writes memory that
+//     an earlier kernel on the stream produces or reads, and before it ends;
+//     the wait returns once the previous grid has completed and its memory is
+//     visible, so by induction every earlier kernel has completed too;
+//   * griddep_launch_dependents() lets the next grid start early; a kernel
+//     calls it only after its own wait.
+// Without a programmatic predecessor the wait returns at once.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ------------------------------------------------------------------ mma ---

@@ -143,12 +143,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
-// programmatic dependent launch: the prep kernel lets the attention grid start
-// early; the attention grid waits for the prep grid (and its memory) here
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-}
 // plain (non-multicast) bulk copy global -> this CTA's shared memory
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -493,7 +487,7 @@ __device__ __forceinline__ void load_kscales(float2 out[2][NG], const uint16_t* 
 // separate instantiation, because carrying that path costs the argument-fed
 // kernel ~10% through register allocation)
 template <int BK, int BV, int RP, int DT, int NG, int VCH, int GM>
-__global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 3)
+__global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 4)
 decode_attn_kernel(const DevArgs a) {
   constexpr int NT = RP / 4;
   constexpr int kStages = stages_for(RP);
@@ -1024,6 +1018,11 @@ decode_attn_kernel(const DevArgs a) {
     }
   }
 
+  // the tiles are done: the merge grid (launched as this grid's programmatic
+  // dependent) may be scheduled as CTAs finish; it waits for this grid's
+  // completion before reading the partials
+  griddep_launch_dependents();
+
   if (failed) {
     // a staged tile never arrived: wait (bounded) for this warp's copies still
     // in flight, then publish NaN so the caller sees the failure
@@ -1078,7 +1077,11 @@ decode_attn_kernel(const DevArgs a) {
 // fragments of the dense (sink / recent) rows.
 template <int DT, int RP, int NG>
 __global__ void __launch_bounds__(kWarps * 32) qprep_kernel(const DevArgs a) {
-  griddep_launch_dependents();  // the attention grid may start its KV copies now
+  // the previous kernel on the stream (an append of this layer's token, a
+  // merge) has completed and its memory is visible once this returns; only
+  // then may the attention grid start its KV copies
+  griddep_wait();
+  griddep_launch_dependents();
   constexpr int NT = RP / 4;
   constexpr int KPG = 4 / NG;                                // 32-dim k-blocks per channel group
   constexpr int QBITS = NG == 4 ? 22 : (NG == 2 ? 21 : 20);  // |q int| < 2^QBITS: a group sum fits int32
@@ -1190,17 +1193,7 @@ __global__ void __launch_bounds__(kWarps * 32) qprep_kernel(const DevArgs a) {
 // launched just before it on the same stream.
 template <typename K>
 inline cudaError_t launch_after_prep(K kern, dim3 grid, int smem, cudaStream_t s, const DevArgs& a) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kWarps * 32, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a);
+  return launch_pdl(kern, grid, dim3(kWarps * 32, 1, 1), smem, s, a);
 }
 
 }  // namespace innerq

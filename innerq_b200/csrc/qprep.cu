@@ -12,12 +12,11 @@ template <int DT, int RP>
 cudaError_t go(const DevArgs& a, int ng, cudaStream_t s) {
   const dim3 grid(a.Hkv, a.B, 1);
   switch (ng) {
-    case 4: qprep_kernel<DT, RP, 4><<<grid, kWarps * 32, 0, s>>>(a); break;
-    case 2: qprep_kernel<DT, RP, 2><<<grid, kWarps * 32, 0, s>>>(a); break;
-    case 1: qprep_kernel<DT, RP, 1><<<grid, kWarps * 32, 0, s>>>(a); break;
+    case 4: return launch_pdl(qprep_kernel<DT, RP, 4>, grid, dim3(kWarps * 32), 0, s, a);
+    case 2: return launch_pdl(qprep_kernel<DT, RP, 2>, grid, dim3(kWarps * 32), 0, s, a);
+    case 1: return launch_pdl(qprep_kernel<DT, RP, 1>, grid, dim3(kWarps * 32), 0, s, a);
     default: return cudaErrorNotSupported;
   }
-  return cudaGetLastError();
 }
 }  // namespace
 

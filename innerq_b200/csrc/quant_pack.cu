@@ -65,32 +65,53 @@ __global__ void norm_factor_kernel(const uint16_t* __restrict__ x, int64_t sb, i
   f[(int64_t)bh * kD + d] = from_f<DT>(sqrtf(mx));
 }
 
-// the same with 1024 threads per (b, h): 16 token rows x 64 dim pairs, each
-// thread keeping 8 four-byte loads in flight, then a shared-memory reduction
+// The same over chunks of 512 tokens: grid (chunks, H, B), 256 threads = 4 token
+// rows x 64 dim pairs.  |x| >= 0 in fp16 / bf16 orders like its 16-bit
+// pattern, so each chunk's maxima are combined as bit patterns in the output
+// itself (zeroed first) with a compare-and-swap on the 32-bit word holding two
+// adjacent dims; norm_sqrt_kernel then replaces each max m by rnd(sqrt(m)).
 template <int DT>
-__global__ void __launch_bounds__(1024) norm_factor_wide_kernel(const uint16_t* __restrict__ x, int64_t sb,
-                                                                int64_t sh, int64_t st, int H, int T,
-                                                                uint16_t* __restrict__ f) {
-  __shared__ float red[16][kD];
-  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+__global__ void __launch_bounds__(256) norm_absmax_kernel(const uint16_t* __restrict__ x, int64_t sb,
+                                                          int64_t sh, int64_t st, int T,
+                                                          uint32_t* __restrict__ f_words) {
+  __shared__ uint32_t red[4][64];
+  const int h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
   const int dp = threadIdx.x & 63, row = threadIdx.x >> 6;
+  const int t0 = blockIdx.x * 512;
   const uint16_t* base = x + b * sb + h * sh + 2 * dp;
-  float m0 = 0.f, m1 = 0.f;
+  uint32_t m0 = 0u, m1 = 0u;  // max |x| as 15-bit magnitude patterns
 #pragma unroll 8
-  for (int t = row; t < T; t += 16) {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(base + (int64_t)t * st);
-    m0 = fmaxf(m0, fabsf(to_f<DT>((uint16_t)(w & 0xffffu))));
-    m1 = fmaxf(m1, fabsf(to_f<DT>((uint16_t)(w >> 16))));
+  for (int k = row; k < 512; k += 4) {
+    if (t0 + k < T) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(base + (int64_t)(t0 + k) * st);
+      m0 = max(m0, w & 0x7fffu);
+      m1 = max(m1, (w >> 16) & 0x7fffu);
+    }
   }
-  red[row][2 * dp] = m0;
-  red[row][2 * dp + 1] = m1;
+  red[row][dp] = m0 | (m1 << 16);
   __syncthreads();
-  if (threadIdx.x < kD) {
-    float m = 0.f;
+  if (row == 0) {
+    uint32_t lo = 0u, hi = 0u;
 #pragma unroll
-    for (int r = 0; r < 16; ++r) m = fmaxf(m, red[r][threadIdx.x]);
-    f[(int64_t)bh * kD + threadIdx.x] = from_f<DT>(sqrtf(m));
+    for (int r = 0; r < 4; ++r) {
+      lo = max(lo, red[r][dp] & 0xffffu);
+      hi = max(hi, red[r][dp] >> 16);
+    }
+    uint32_t* word = f_words + ((int64_t)b * H + h) * (kD / 2) + dp;
+    uint32_t old = *word, assumed;
+    do {
+      assumed = old;
+      const uint32_t nw = max(assumed & 0xffffu, lo) | (max(assumed >> 16, hi) << 16);
+      if (nw == assumed) break;
+      old = atomicCAS(word, assumed, nw);
+    } while (old != assumed);
   }
+}
+
+template <int DT>
+__global__ void norm_sqrt_kernel(uint16_t* __restrict__ f, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) f[i] = from_f<DT>(sqrtf(to_f<DT>(f[i])));
 }
 
 // --------------------------------------------------------------------------
@@ -268,7 +289,7 @@ __device__ __forceinline__ void group_cuts(float s, float* cut) {
 }
 
 template <int DT, int BITS, int ASYM, int NORM>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
 pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st, int T,
                  const uint16_t* __restrict__ nf, int group, uint8_t* __restrict__ codes,
                  uint16_t* __restrict__ scale, uint16_t* __restrict__ zero, int64_t cap_tiles,
@@ -287,46 +308,53 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
   const int lane = threadIdx.x & 31, kb = lane & 3;
   const int t = blockIdx.x * 64 + (threadIdx.x >> 5) * 8 + (lane >> 2);
   const bool valid = t < T;  // no early return: the group reductions shuffle
-  float v[32];
+  // the thread's 32 values as 16 words of two 16-bit dtype values (element e
+  // in half e & 1 of word e >> 1); converted where used to keep registers low
+  uint32_t raw[16];
   {
-    uint4 raw[4] = {};
+    uint4 r4[4] = {};
     if (valid) {
       const uint4* p = reinterpret_cast<const uint4*>(x + b * sb + h * sh + (int64_t)t * st + kb * 32);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) raw[k] = p[k];
+      for (int k = 0; k < 4; ++k) r4[k] = p[k];
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+      raw[4 * k] = r4[k].x; raw[4 * k + 1] = r4[k].y; raw[4 * k + 2] = r4[k].z; raw[4 * k + 3] = r4[k].w;
+    }
+  }
+  auto val = [&](int e) -> float {
+    return to_f<DT>((uint16_t)((e & 1) ? (raw[e >> 1] >> 16) : (raw[e >> 1] & 0xffffu)));
+  };
+  if constexpr (NORM) {  // cache.py:125 key_states / factor, in the dtype (stored back as dtype bits)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        v[8 * k + 2 * u] = to_f<DT>((uint16_t)(w[u] & 0xffffu));
-        v[8 * k + 2 * u + 1] = to_f<DT>((uint16_t)(w[u] >> 16));
+    for (int w = 0; w < 16; ++w) {
+      uint32_t nw = 0u;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int e = 2 * w + hf;
+        const float f = f_s[kb * 32 + e];
+        const float q = (DT == F16 && f > 0.f && f < INFINITY) ? div_rn(val(e), f, rf_s[kb * 32 + e])
+                                                               : val(e) / f;
+        nw |= (uint32_t)from_f<DT>(q) << (16 * hf);
       }
+      raw[w] = nw;
     }
   }
-  if constexpr (NORM) {  // cache.py:125 key_states / factor, in the dtype
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const float f = f_s[kb * 32 + e];
-      v[e] = rnd<DT>((DT == F16 && f > 0.f && f < INFINITY) ? div_rn(v[e], f, rf_s[kb * 32 + e]) : v[e] / f);
-    }
-  }
-  float s, z = 0.f, qmax;
+  float s, z = 0.f;
   if constexpr (!ASYM) {
     float mx = 0.f;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fabsf(v[e]));
+    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fabsf(val(e)));
     if (group >= 64) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     if (group >= 128) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    qmax = (float)qmax_sym<BITS>();
     s = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx));
   } else {
     float mn = INFINITY, mx = -INFINITY;
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
-      mn = fminf(mn, v[e]);
-      mx = fmaxf(mx, v[e]);
+      mn = fminf(mn, val(e));
+      mx = fmaxf(mx, val(e));
     }
     if (group >= 64) {
       mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
@@ -336,28 +364,22 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
       mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     }
-    qmax = (float)((1 << BITS) - 1);
     s = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx - mn)));
     z = mn;
   }
-  // offset-binary codes of the thread's 32 dims (e = half*16 + 4*tq + i) by
-  // the group's cuts
-  int u[32];
-  auto codes_with = [&](auto code) {
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      if constexpr (!ASYM) {
-        const int c = code(fabsf(v[e]));
-        u[e] = (v[e] < 0.f ? -c : c) + (1 << (BITS - 1));
-      } else {
-        u[e] = code(rnd<DT>(v[e] - z));
-      }
-    }
-  };
   constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
   float cut[QM];
   group_cuts<DT, QM>(s, cut);
-  codes_with([&](float a) { return code_by_cuts<QM>(a, cut); });
+  // offset-binary code of element e (dim kb*32 + e, e = half*16 + 4*tq + i)
+  auto code = [&](int e) -> uint32_t {
+    const float v = val(e);
+    if constexpr (!ASYM) {
+      const int c = code_by_cuts<QM>(fabsf(v), cut);
+      return (uint32_t)((v < 0.f ? -c : c) + (1 << (BITS - 1)));
+    } else {
+      return (uint32_t)code_by_cuts<QM>(rnd<DT>(v - z), cut);
+    }
+  };
   const int64_t p = t_off + t;
   const int64_t ti = p >> 5;
   const int r = (int)(p & 31), gid = r & 7, j = r >> 3;
@@ -379,7 +401,7 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) w |= (uint32_t)u[hf * 16 + 4 * tq + i] << (4 * (2 * i + hf));
+        for (int hf = 0; hf < 2; ++hf) w |= code(hf * 16 + 4 * tq + i) << (4 * (2 * i + hf));
       if (valid) *reinterpret_cast<uint32_t*>(tb + j * 512 + lane2 * 16 + kb * 4) = w;
     } else {
       // low two bits: word kb>>1 of the row's 8 bytes, crumb 4i + (kb&1)*2 + half,
@@ -389,7 +411,7 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          const uint32_t c = (uint32_t)u[hf * 16 + 4 * tq + i];
+          const uint32_t c = code(hf * 16 + 4 * tq + i);
           w |= (c & 3u) << (2 * (4 * i + (kb & 1) * 2 + hf));
           if (BITS == 3) wh |= ((c >> 2) & 1u) << (8 * i + kb * 2 + hf);
         }
@@ -563,13 +585,15 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
   const int64_t bh = (int64_t)b * H + h;
   const int dp = threadIdx.x;  // dims 2dp, 2dp+1
   const uint16_t* x0 = x + b * sb + h * sh + (int64_t)gi * group * st + 2 * dp;
-  float2 v[32];
+  // a chunk of 32 tokens as words of the two dims' 16-bit values, converted
+  // where used (keeps the registers, and so the occupancy, of the 4-bit codes)
+  uint32_t raw[32];
   auto load = [&](int c0) {
 #pragma unroll
-    for (int t = 0; t < 32; ++t) {
-      const uint32_t w = *reinterpret_cast<const uint32_t*>(x0 + (int64_t)(c0 + t) * st);
-      v[t] = make_float2(to_f<DT>((uint16_t)(w & 0xffffu)), to_f<DT>((uint16_t)(w >> 16)));
-    }
+    for (int t = 0; t < 32; ++t) raw[t] = *reinterpret_cast<const uint32_t*>(x0 + (int64_t)(c0 + t) * st);
+  };
+  auto val = [&](int t, int e) -> float {
+    return to_f<DT>((uint16_t)(e ? (raw[t] >> 16) : (raw[t] & 0xffffu)));
   };
   float mx0 = ASYM ? -INFINITY : 0.f, mx1 = mx0, mn0 = INFINITY, mn1 = INFINITY;
   for (int c0 = 0; c0 < group; c0 += 32) {
@@ -577,22 +601,19 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
       if (ASYM) {
-        mx0 = fmaxf(mx0, v[t].x); mx1 = fmaxf(mx1, v[t].y);
-        mn0 = fminf(mn0, v[t].x); mn1 = fminf(mn1, v[t].y);
+        mx0 = fmaxf(mx0, val(t, 0)); mx1 = fmaxf(mx1, val(t, 1));
+        mn0 = fminf(mn0, val(t, 0)); mn1 = fminf(mn1, val(t, 1));
       } else {
-        mx0 = fmaxf(mx0, fabsf(v[t].x)); mx1 = fmaxf(mx1, fabsf(v[t].y));
+        mx0 = fmaxf(mx0, fabsf(val(t, 0))); mx1 = fmaxf(mx1, fabsf(val(t, 1)));
       }
     }
   }
   float s[2], z[2] = {0.f, 0.f};
-  float qmax;
   if (ASYM) {
-    qmax = (float)((1 << BITS) - 1);
     s[0] = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx0 - mn0)));
     s[1] = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx1 - mn1)));
     z[0] = mn0; z[1] = mn1;
   } else {
-    qmax = (float)qmax_sym<BITS>();
     s[0] = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx0));
     s[1] = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx1));
   }
@@ -600,34 +621,30 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
   float cut[2][QM];
   group_cuts<DT, QM>(s[0], cut[0]);
   group_cuts<DT, QM>(s[1], cut[1]);
-  auto codes_with = [&](auto code) {
-    for (int c0 = 0; c0 < group; c0 += 32) {
-      if (group > 32) load(c0);
+  for (int c0 = 0; c0 < group; c0 += 32) {
+    if (group > 32) load(c0);
 #pragma unroll
-      for (int t4 = 0; t4 < 8; ++t4) {
-        uint32_t w[2] = {0u, 0u};
+    for (int t4 = 0; t4 < 8; ++t4) {
+      uint32_t w[2] = {0u, 0u};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 xv = v[4 * t4 + i];
-          const float xe[2] = {xv.x, xv.y};
+      for (int i = 0; i < 4; ++i) {
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            uint32_t uc;
-            if (ASYM) {
-              uc = (uint32_t)code(rnd<DT>(xe[e] - z[e]), e);
-            } else {
-              const int c = code(fabsf(xe[e]), e);
-              uc = (uint32_t)((xe[e] < 0.f ? -c : c) + (1 << (BITS - 1)));
-            }
-            w[e] |= uc << (8 * i);
+        for (int e = 0; e < 2; ++e) {
+          const float xe = val(4 * t4 + i, e);
+          uint32_t uc;
+          if (ASYM) {
+            uc = (uint32_t)code_by_cuts<QM>(rnd<DT>(xe - z[e]), cut[e]);
+          } else {
+            const int c = code_by_cuts<QM>(fabsf(xe), cut[e]);
+            uc = (uint32_t)((xe < 0.f ? -c : c) + (1 << (BITS - 1)));
           }
+          w[e] |= uc << (8 * i);
         }
-        cbt[2 * dp][(c0 >> 2) + t4] = w[0];
-        cbt[2 * dp + 1][(c0 >> 2) + t4] = w[1];
       }
+      cbt[2 * dp][(c0 >> 2) + t4] = w[0];
+      cbt[2 * dp + 1][(c0 >> 2) + t4] = w[1];
     }
-  };
-  codes_with([&](float a, int e) { return code_by_cuts<QM>(a, cut[e]); });
+  }
   const int64_t groups_cap = cap_tiles * 32 / group;
   const int64_t t_abs = t_off + (int64_t)gi * group;
   const int64_t gglob = t_abs / group;
@@ -680,6 +697,8 @@ __global__ void __launch_bounds__(128) append_step_kernel(const AppendDev a, con
   __shared__ uint32_t seg_unused[16];
   const int h = blockIdx.x, b = blockIdx.y, H = gridDim.x, d = threadIdx.x;
   const int64_t bh = (int64_t)b * H + h;
+  griddep_wait();  // earlier kernels on the stream (the step counter's update) are done
+  griddep_launch_dependents();
   if (*step < 1 || *step > a.max_steps) return;  // outside the reserved steps: write nothing
   const int n1 = (int)*step, n0 = n1 - 1;
   uint16_t* fifo = a.fifo + b * a.f_b + h * a.f_h;
@@ -810,32 +829,73 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ codes, const uint16_t
 // Split-KV log-sum-exp merge: out = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s
 // --------------------------------------------------------------------------
 template <int DT>
-__global__ void lse_merge_kernel(const float* __restrict__ po, const float* __restrict__ pm,
-                                 const float* __restrict__ pl, int n_splits, int rows_per_b,
-                                 int n_ranks, int64_t rank_stride,
-                                 uint16_t* __restrict__ out, int64_t o_b, int64_t o_h,
-                                 float* __restrict__ lse_out) {
+__global__ void __launch_bounds__(kD) lse_merge_kernel(const float* __restrict__ po, const float* __restrict__ pm,
+                                                       const float* __restrict__ pl, int n_splits, int rows_per_b,
+                                                       int n_ranks, int64_t rank_stride,
+                                                       uint16_t* __restrict__ out, int64_t o_b, int64_t o_h,
+                                                       float* __restrict__ lse_out) {
   // n_ranks blocks of partials, rank_stride floats apart (one block per rank
   // of a context-sharded layer, gathered; 1 block otherwise), each with
-  // n_splits partials per row
-  const int row = blockIdx.x, d = threadIdx.x;
+  // n_splits partials per row.  The split maxima and sums of the row are read
+  // by all threads at once (in chunks of kChunk), their weights 2^(m - M)
+  // kept in shared memory, then each thread (one dim) sums its column with
+  // its loads in flight together.
+  constexpr int kChunk = 1024;
+  __shared__ float w_s[kChunk];
+  __shared__ float red_s[kD / 32];
+  griddep_wait();  // the attention grid's partials are complete and visible
+  griddep_launch_dependents();
+  const int row = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  const int total = n_ranks * n_splits;
+  auto part = [&](const float* base, int j) -> const float* {  // split j = (rank, split)
+    const int w = j / n_splits, s = j - w * n_splits;
+    return base + w * rank_stride + (int64_t)row * n_splits + s;
+  };
+  auto block_max = [&](float v) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red_s[warp] = v;
+    __syncthreads();
+    v = fmaxf(fmaxf(red_s[0], red_s[1]), fmaxf(red_s[2], red_s[3]));
+    __syncthreads();
+    return v;
+  };
+  auto block_sum = [&](float v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red_s[warp] = v;
+    __syncthreads();
+    v = (red_s[0] + red_s[1]) + (red_s[2] + red_s[3]);
+    __syncthreads();
+    return v;
+  };
   float M = -INFINITY;
-  for (int w = 0; w < n_ranks; ++w) {
-    const float* m = pm + w * rank_stride + (int64_t)row * n_splits;
-    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, m[s]);
-  }
+  for (int j = d; j < total; j += kD) M = fmaxf(M, *part(pm, j));
+  M = block_max(M);
   float num = 0.f, den = 0.f;
   if (M != -INFINITY) {
-    for (int w = 0; w < n_ranks; ++w) {
-      const float* m = pm + w * rank_stride + (int64_t)row * n_splits;
-      const float* l = pl + w * rank_stride + (int64_t)row * n_splits;
-      const float* o = po + w * rank_stride + (int64_t)row * n_splits * kD + d;
-      for (int s = 0; s < n_splits; ++s) {
-        if (m[s] == -INFINITY) continue;  // an empty split contributes nothing
-        const float wt = exp2f(m[s] - M);
-        num += wt * o[(int64_t)s * kD];
-        den += wt * l[s];
+    for (int c0 = 0; c0 < total; c0 += kChunk) {
+      const int cn = min(kChunk, total - c0);
+      float dl = 0.f;
+      for (int j = d; j < cn; j += kD) {
+        const float m = *part(pm, c0 + j);
+        // an empty split contributes nothing
+        const float wt = m == -INFINITY ? 0.f : exp2f(m - M);
+        w_s[j] = wt;
+        dl += wt * *part(pl, c0 + j);
       }
+      den += block_sum(dl);  // (its barrier also publishes w_s)
+      int w = c0 / n_splits, sp = c0 - w * n_splits;
+      const float* op = po + w * rank_stride + ((int64_t)row * n_splits + sp) * kD + d;
+#pragma unroll 8
+      for (int j = 0; j < cn; ++j) {
+        num += w_s[j] * *op;
+        op += kD;
+        if (++sp == n_splits) {  // next rank's block
+          sp = 0;
+          ++w;
+          op = po + w * rank_stride + (int64_t)row * n_splits * kD + d;
+        }
+      }
+      __syncthreads();
     }
   }
   const int b = row / rows_per_b, h = row % rows_per_b;
@@ -889,14 +949,19 @@ __global__ void dequant_ref_kernel(const int32_t* __restrict__ c, const uint16_t
 
 cudaError_t launch_norm_factor(const void* x, int dt, int B, int H, int T, int64_t sb, int64_t sh,
                                int64_t st, void* f, cudaStream_t s) {
-  const bool rows4 = ((uintptr_t)x % 4 == 0) && sb % 2 == 0 && sh % 2 == 0 && st % 2 == 0;
-  if (rows4) {
-    DT_DISPATCH(dt, norm_factor_wide_kernel<DTC><<<B * H, 1024, 0, s>>>(
-                        (const uint16_t*)x, sb, sh, st, H, T, (uint16_t*)f));
-  } else {
+  const bool pairs = ((uintptr_t)x % 4 == 0) && sb % 2 == 0 && sh % 2 == 0 && st % 2 == 0 &&
+                     (uintptr_t)f % 4 == 0;
+  if (!pairs) {
     DT_DISPATCH(dt, norm_factor_kernel<DTC><<<B * H, kD, 0, s>>>(
                         (const uint16_t*)x, sb, sh, st, H, T, (uint16_t*)f));
+    return cudaGetLastError();
   }
+  const int64_t n = (int64_t)B * H * kD;
+  cudaError_t e = cudaMemsetAsync(f, 0, n * sizeof(uint16_t), s);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((T + 511) / 512), (unsigned)H, (unsigned)B);
+  DT_DISPATCH(dt, norm_absmax_kernel<DTC><<<grid, 256, 0, s>>>((const uint16_t*)x, sb, sh, st, T, (uint32_t*)f));
+  DT_DISPATCH(dt, norm_sqrt_kernel<DTC><<<(unsigned)((n + 255) / 256), 256, 0, s>>>((uint16_t*)f, n));
   return cudaGetLastError();
 }
 
@@ -910,13 +975,14 @@ cudaError_t launch_append_step(const AppendArgs& g, const int64_t* step, cudaStr
   a.max_steps = g.max_steps;
   const dim3 grid((unsigned)g.H, (unsigned)g.B, 1);
   const int dt = g.dt, bits = g.bits;
+  cudaError_t e = cudaSuccess;
   switch (g.mode) {
-    case 0: DT_DISPATCH(dt, BITS_DISPATCH(bits, append_step_kernel<DTC, BC, 0><<<grid, 128, 0, s>>>(a, step))); break;
-    case 1: DT_DISPATCH(dt, BITS_DISPATCH(bits, append_step_kernel<DTC, BC, 1><<<grid, 128, 0, s>>>(a, step))); break;
-    case 2: DT_DISPATCH(dt, BITS_DISPATCH(bits, append_step_kernel<DTC, BC, 2><<<grid, 128, 0, s>>>(a, step))); break;
-    default: DT_DISPATCH(dt, (append_step_kernel<DTC, 4, 3><<<grid, 128, 0, s>>>(a, step))); break;
+    case 0: DT_DISPATCH(dt, BITS_DISPATCH(bits, e = launch_pdl(append_step_kernel<DTC, BC, 0>, grid, dim3(128), 0, s, a, step))); break;
+    case 1: DT_DISPATCH(dt, BITS_DISPATCH(bits, e = launch_pdl(append_step_kernel<DTC, BC, 1>, grid, dim3(128), 0, s, a, step))); break;
+    case 2: DT_DISPATCH(dt, BITS_DISPATCH(bits, e = launch_pdl(append_step_kernel<DTC, BC, 2>, grid, dim3(128), 0, s, a, step))); break;
+    default: DT_DISPATCH(dt, (e = launch_pdl(append_step_kernel<DTC, 4, 3>, grid, dim3(128), 0, s, a, step))); break;
   }
-  return cudaGetLastError();
+  return e;
 }
 
 // rows of 16-byte aligned, 16-byte strided 16-bit values
@@ -1021,9 +1087,10 @@ cudaError_t launch_lse_merge(const float* po, const float* pm, const float* pl, 
                              int64_t o_h, float* lse, cudaStream_t s, int n_ranks,
                              int64_t rank_stride) {
   if (rows == 0) return cudaSuccess;
-  DT_DISPATCH(dt, lse_merge_kernel<DTC><<<rows, kD, 0, s>>>(po, pm, pl, n_splits, rows_per_b, n_ranks,
-                                                            rank_stride, (uint16_t*)out, o_b, o_h, lse));
-  return cudaGetLastError();
+  cudaError_t e = cudaSuccess;
+  DT_DISPATCH(dt, e = launch_pdl(lse_merge_kernel<DTC>, dim3(rows), dim3(kD), 0, s, po, pm, pl, n_splits,
+                                 rows_per_b, n_ranks, rank_stride, (uint16_t*)out, o_b, o_h, lse));
+  return e;
 }
 
 cudaError_t launch_dequant_ref(const int32_t* c, const void* s, const void* zs, int dt, int64_t n_outer,

@@ -201,7 +201,9 @@ class PackedSide:
         self.B, self.H, T, self.D = x.shape
         self._check_supported()
         n_sink = min(self.w_sink, T) if self.quantize else 0
-        self.sink = x[:, :, :n_sink].contiguous()
+        # a copy, never a view: even an empty slice would keep the whole
+        # prefill tensor alive for the life of the cache
+        self.sink = x[:, :, :n_sink].clone(memory_format=torch.contiguous_format)
         x = x[:, :, n_sink:]
         T = x.shape[2]
         if self.quantize:

@@ -235,3 +235,20 @@ def test_full_size_context_32k(B):
     r = to_np32(ref[:, :, 0])
     err = np.abs(to_np32(out) - r)
     assert (err <= 1e-3 * np.abs(r).max() + 2.0 ** -11 * np.abs(r)).all(), err.max()
+
+
+def test_prefill_states_are_not_retained():
+    """A layer without sink tokens keeps no view of the prefill tensors: after
+    the caller drops them their memory is free again (a zero-size slice kept
+    as the sink would hold the whole prefill K/V alive)."""
+    from innerq_b200.cache import InnerqDynamicLayer
+    layer = InnerqDynamicLayer(cfg(k_bits=4, v_bits=4, key_w_sink=0, value_w_sink=0), 0)
+    k, v = synth_kv(4, 8, 8192, seed=31)
+    torch.cuda.synchronize()
+    layer.update(k, v)
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    nbytes = k.numel() * k.element_size() + v.numel() * v.element_size()
+    del k, v
+    torch.cuda.synchronize()
+    assert before - torch.cuda.memory_allocated() >= nbytes
