@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define INNERQ_ABI_VERSION 4
+#define INNERQ_ABI_VERSION 5
 
 enum {
   INNERQ_OK = 0,
@@ -49,7 +49,7 @@ enum {
   INNERQ_ERR_CUDA = -3         /* a CUDA launch or runtime call failed */
 };
 enum { INNERQ_DT_F16 = 0, INNERQ_DT_BF16 = 1 };
-enum { INNERQ_SYM = 0, INNERQ_ASYM = 1 };         /* quant.py:43-46 QMode */
+enum { INNERQ_SYM = 0, INNERQ_ASYM = 1, INNERQ_HYBRID = 2 };  /* quant.py:43-56 QMode */
 enum { INNERQ_ROLE_K = 0, INNERQ_ROLE_V = 1 };
 
 /* Version of this ABI (INNERQ_ABI_VERSION). */
@@ -143,6 +143,18 @@ typedef struct {
    * state after min(*step, max_steps) steps, so a counter run past the
    * reservation never reads outside the buffers (the caller checks the count). */
   int32_t r0, flush, max_steps;
+  /* Hybrid values (mode INNERQ_HYBRID, quant.py:133-176; values grouped over
+   * tokens, read by innerq_decode_attn only): codes / scale above hold the
+   * symmetric `bits`-bit set, codes2 / scale2 / zero2 the asymmetric
+   * (bits - 1)-bit set in a store of cap_tiles2 tiles, and mask one bit per
+   * (token group, dim), 16 bytes per group ([B][H][cap_tiles2 * 32 / group]),
+   * bit col_scale_idx(dim) (the dim order of the value scales) set where the
+   * group keeps its symmetric codes.  Unused (NULL, 0) otherwise. */
+  const void* codes2;
+  const void* scale2;
+  const void* zero2;
+  const void* mask;
+  int64_t cap_tiles2;
 } innerq_side;
 
 typedef struct {

@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libinnerq_b
 
 INNERQ_OK = 0
 DT_F16, DT_BF16 = 0, 1
-SYM, ASYM = 0, 1
+SYM, ASYM, HYBRID = 0, 1, 2
 ROLE_K, ROLE_V = 0, 1
 
 EXPORTS = (
@@ -43,6 +43,8 @@ class Side(C.Structure):
         ("n_sink", C.c_int32), ("n_q", C.c_int32), ("n_recent", C.c_int32),
         ("bits", C.c_int32), ("group", C.c_int32), ("mode", C.c_int32), ("over_token", C.c_int32),
         ("r0", C.c_int32), ("flush", C.c_int32), ("max_steps", C.c_int32),
+        ("codes2", C.c_void_p), ("scale2", C.c_void_p), ("zero2", C.c_void_p), ("mask", C.c_void_p),
+        ("cap_tiles2", C.c_int64),
     ]
 
 
@@ -115,7 +117,7 @@ def load() -> C.CDLL:
         f = getattr(lib, name)
         f.restype = res
         f.argtypes = args
-    if lib.innerq_abi_version() != 4:
+    if lib.innerq_abi_version() != 5:
         raise ImportError("libinnerq_b200.so ABI version mismatch; rebuild it")
     _lib = lib
     return lib

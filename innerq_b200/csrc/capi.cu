@@ -67,8 +67,17 @@ struct Plan {
 int check_side(const innerq_side& s, int dtype, int role, const char* name) {
   if (s.n_sink < 0 || s.n_q < 0 || s.n_recent < 0) return fail(INNERQ_ERR_ARG, "%s: negative count", name);
   if (packed(s)) {
-    int rc = check_common(dtype, kD, s.bits, s.group, s.mode, role, s.over_token);
+    const bool hyb = s.mode == INNERQ_HYBRID;
+    int rc = check_common(dtype, kD, s.bits, s.group, hyb ? INNERQ_SYM : s.mode, role, s.over_token);
     if (rc) return rc;
+    if (hyb) {
+      if (role != INNERQ_ROLE_V || !s.over_token)
+        return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: hybrid %s must be values grouped over tokens", name);
+      if (!s.codes2 || !s.scale2 || !s.zero2 || !s.mask || !aligned(s.codes2, 16) || !aligned(s.scale2, 16) ||
+          !aligned(s.zero2, 16) || !aligned(s.mask, 16))
+        return fail(INNERQ_ERR_ARG, "%s: hybrid stores missing or not 16-byte aligned", name);
+      if ((int64_t)s.n_q > s.cap_tiles2 * 32) return fail(INNERQ_ERR_ARG, "%s: n_q beyond the asymmetric store", name);
+    }
     if (s.bits < 2) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: %s bits %d (2, 3, 4)", name, s.bits);
     // the fused kernel reads the InnerQ layouts (cache.py:87-88 defaults)
     if (role == INNERQ_ROLE_K && s.over_token)
@@ -122,6 +131,11 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
   if (a->step) {
     if ((rc = check_graph_side(a->k, "k"))) return rc;
     if ((rc = check_graph_side(a->v, "v"))) return rc;
+  }
+  if (packed(a->v) && a->v.mode == INNERQ_HYBRID) {
+    if (a->step) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: hybrid values in graph mode");
+    if (packed(a->k) && a->k.group != 32)
+      return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: hybrid values need keys in groups of 32 (use innerq_dequant)");
   }
   // values grouped over channels share the keys' channel-group count
   if (packed(a->v) && !a->v.over_token && packed(a->k) && a->v.group != a->k.group)
@@ -180,11 +194,17 @@ DevSide dev_side(const innerq_side& s) {
   d.rc_b = s.rec_sb; d.rc_h = s.rec_sh; d.rc_t = s.rec_st;
   d.n_sink = s.n_sink; d.n_q = s.n_q; d.n_rec = s.n_recent;
   d.group = packed(s) ? s.group : 32;
-  d.asym = packed(s) && s.mode == INNERQ_ASYM;
+  d.asym = packed(s) && s.mode == INNERQ_ASYM;  // hybrid: the symmetric set
   d.chan = 0;
   d.r0 = s.r0;
   d.flush = s.flush;
   d.max_steps = s.max_steps;
+  d.hyb = packed(s) && s.mode == INNERQ_HYBRID;
+  d.codes2 = (const uint8_t*)s.codes2;
+  d.scale2 = (const uint16_t*)s.scale2;
+  d.zero2 = (const uint16_t*)s.zero2;
+  d.mask = (const uint16_t*)s.mask;
+  d.cap_tiles2 = s.cap_tiles2;
   return d;
 }
 

@@ -60,6 +60,16 @@ struct DevSide {
   // the FIFO base, r0 the window's FIFO offset at step 0, flush the flush size,
   // max_steps the steps its buffers were reserved for
   int r0, flush, max_steps;
+  // hybrid values (token groups): codes / scale are the symmetric set;
+  // codes2 / scale2 / zero2 the asymmetric (bits - 1)-bit set (cap_tiles2),
+  // mask 8 16-bit words per group, bit col_scale_idx(dim) set where the group
+  // keeps its symmetric codes
+  int hyb;
+  const uint8_t* codes2;
+  const uint16_t* scale2;
+  const uint16_t* zero2;
+  const uint16_t* mask;
+  int64_t cap_tiles2;
 };
 
 // A side's geometry after n decode steps of graph mode: each step appends one
@@ -100,12 +110,14 @@ __host__ __device__ constexpr int stages_for(int rp) { return 2; }
 // in ns) instead of spinning; 1 << 16 tries bound the wait to seconds
 constexpr uint32_t kWaitLimit = 1u << 16;
 
-// bytes of one staged tile (K codes, K scales [, K zeros], V codes, V scales [, V zeros])
-__host__ __device__ inline int stage_bytes(int bk, int bv, int ng, int kasym, int vasym) {
-  return tile_bytes(bk) + 64 * ng * (1 + kasym) + tile_bytes(bv) + 256 * (1 + vasym);
+// bytes of one staged tile (K codes, K scales [, K zeros], V codes, V scales
+// [, V zeros] [, hybrid: asymmetric V codes, their scales and zeros, the mask])
+__host__ __device__ inline int stage_bytes(int bk, int bv, int ng, int kasym, int vasym, int hyb = 0) {
+  return tile_bytes(bk) + 64 * ng * (1 + kasym) + tile_bytes(bv) + 256 * (1 + vasym) +
+         (hyb ? tile_bytes(bv - 1) + 256 + 256 + 16 : 0);
 }
-__host__ __device__ inline int attn_dyn_smem(int bk, int bv, int ng, int kasym, int vasym, int rp) {
-  return kWarps * stages_for(rp) * stage_bytes(bk, bv, ng, kasym, vasym);
+__host__ __device__ inline int attn_dyn_smem(int bk, int bv, int ng, int kasym, int vasym, int rp, int hyb = 0) {
+  return kWarps * stages_for(rp) * stage_bytes(bk, bv, ng, kasym, vasym, hyb);
 }
 
 // ------------------------------------------------------------ PTX helpers ---
@@ -225,11 +237,14 @@ __device__ __forceinline__ void load_krow(KRow<BITS>& r, const uint8_t* tb, int 
   }
 }
 
-template <int BITS> struct VChunk { uint32_t w[BITS == 4 ? 16 : (BITS == 2 ? 8 : 12)]; };
+template <int BITS> struct VChunk { uint32_t w[BITS == 4 ? 16 : (BITS == 2 ? 8 : (BITS == 3 ? 12 : 4))]; };
 
 template <int BITS>
 __device__ __forceinline__ void load_vchunk(VChunk<BITS>& c, const uint8_t* tb, int lane) {
-  if constexpr (BITS == 4) {
+  if constexpr (BITS == 1) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tb + lane * 16);
+    c.w[0] = v.x; c.w[1] = v.y; c.w[2] = v.z; c.w[3] = v.w;
+  } else if constexpr (BITS == 4) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint4 v = *reinterpret_cast<const uint4*>(tb + i * 512 + lane * 16);
@@ -459,6 +474,52 @@ __device__ __forceinline__ void v_packed_accumulate(const VChunk<BV>& vc, const 
   }
 }
 
+// A fragment of the asymmetric (BV - 1)-bit set of a hybrid V tile, scaled
+// like the symmetric BV-bit fragment of the same m-tile (col_scale<BV>(mt)),
+// so one fp32 scale per dim undoes either
+template <int BV>
+__device__ __forceinline__ uint32_t asym_frag(const uint32_t* w, int mt, int h, int half) {
+  if constexpr (BV == 2) {  // 1-bit plane: bit (mt&1)*4 + h*2 + half of word mt>>1
+    return ((w[mt >> 1] >> ((mt & 1) * 4 + h * 2 + half)) & 0x01010101u) << (2 * (mt >> 1));
+  } else if constexpr (BV == 3) {  // 2-bit set, crumb position mt>>1, moved to bit 0
+    return (w[(mt & 1) * 4 + h * 2 + half] >> (2 * (mt >> 1))) & 0x03030303u;
+  } else {  // 3-bit set (factor 1) under a 4-bit layout (factor 16 for m-tiles 4-7)
+    return col_frag<3>(w, mt, h, half) << (mt < 4 ? 0 : 4);
+  }
+}
+
+// PV of one packed tile of hybrid values (quant.py:133-176): per dim the
+// group's mask picks the symmetric codes (scale s, offset 2^(BV-1)) or the
+// asymmetric ones (scale s2, zero z2):
+//   O[nt][mt][h] += fv * (S * sum_t u p + Cz * sum_t p),
+//   (S, Cz) = mask ? (s, -2^(BV-1) s) : (s2, z2)
+template <int BV, int NT>
+__device__ __forceinline__ void v_hybrid_accumulate(const VChunk<BV>& vc, const VChunk<BV - 1>& va,
+                                                    const float2 sv[8], const float2 sa[8],
+                                                    const float2 za[8], uint32_t mk,
+                                                    const uint32_t pb[NT][2], const int psum[NT],
+                                                    const float fv[NT], float2 o[NT][8]) {
+  constexpr float kOff = (float)(1 << (BV - 1));
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const bool s0 = (mk >> (2 * mt)) & 1u, s1 = (mk >> (2 * mt + 1)) & 1u;  // dims (mt, h 0 / 1)
+    const float2 S = make_float2(s0 ? sv[mt].x : sa[mt].x, s1 ? sv[mt].y : sa[mt].y);
+    const float2 Cz = make_float2(s0 ? -kOff * sv[mt].x : za[mt].x, s1 ? -kOff * sv[mt].y : za[mt].y);
+    const uint32_t af[4] = {s0 ? col_frag<BV>(vc.w, mt, 0, 0) : asym_frag<BV>(va.w, mt, 0, 0),
+                            s1 ? col_frag<BV>(vc.w, mt, 1, 0) : asym_frag<BV>(va.w, mt, 1, 0),
+                            s0 ? col_frag<BV>(vc.w, mt, 0, 1) : asym_frag<BV>(va.w, mt, 0, 1),
+                            s1 ? col_frag<BV>(vc.w, mt, 1, 1) : asym_frag<BV>(va.w, mt, 1, 1)};
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      int acc[4];
+      imma_u8u8(acc, af, pb[nt], 0, 0, 0, 0);
+      const float2 t = make_float2((float)(acc[0] * 256 + acc[1]), (float)(acc[2] * 256 + acc[3]));
+      o[nt][mt] = __ffma2_rn(__fmul2_rn(S, f2(fv[nt] * (1.f / col_scale<BV>(mt)))), t, o[nt][mt]);
+      o[nt][mt] = __ffma2_rn(Cz, f2((float)psum[nt] * fv[nt]), o[nt][mt]);
+    }
+  }
+}
+
 // scales / zero points of the lane's 4 rows (row layout, [g][j]), 8*NG bytes at
 // p, as pairs of rows: out[m][g] = (row 2m, row 2m+1)
 template <int DT, int NG>
@@ -486,7 +547,7 @@ __device__ __forceinline__ void load_kscales(float2 out[2][NG], const uint16_t* 
 // over tokens; GM: graph mode (geometry from the device step counter; a
 // separate instantiation, because carrying that path costs the argument-fed
 // kernel ~10% through register allocation)
-template <int BK, int BV, int RP, int DT, int NG, int VCH, int GM>
+template <int BK, int BV, int RP, int DT, int NG, int VCH, int GM, int VHY = 0>
 __global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 4)
 decode_attn_kernel(const DevArgs a) {
   constexpr int NT = RP / 4;
@@ -518,7 +579,7 @@ decode_attn_kernel(const DevArgs a) {
   const int ks = a.k.n_sink;
   const int vs = a.v.n_sink;
   const int kasym = a.k.asym, vasym = a.v.asym;
-  const int SB = stage_bytes(BK, BV, NG, kasym, vasym);
+  const int SB = stage_bytes(BK, BV, NG, kasym, vasym, VHY);
   const int koff = kasym ? 0 : (1 << (BK - 1));
   const int voff = vasym ? 0 : (1 << (BV - 1));
 
@@ -535,6 +596,13 @@ decode_attn_kernel(const DevArgs a) {
   const int64_t vsc_pair = VCH ? a.v.cap_tiles * 32 * NG : vgroups_cap * kD;
   const uint16_t* vscale = a.v.scale ? a.v.scale + kbh * vsc_pair : nullptr;
   const uint16_t* vzero = a.v.zero ? a.v.zero + kbh * vsc_pair : nullptr;
+  // hybrid values: the asymmetric set and the per-(group, dim) mask
+  constexpr int TBV2 = VHY ? tile_bytes(BV - 1) : 0;
+  const int64_t vgroups_cap2 = VHY ? (a.v.cap_tiles2 * 32) >> vgs : 0;
+  const uint8_t* vcodes2 = VHY ? a.v.codes2 + kbh * a.v.cap_tiles2 * TBV2 : nullptr;
+  const uint16_t* vscale2 = VHY ? a.v.scale2 + kbh * vgroups_cap2 * kD : nullptr;
+  const uint16_t* vzero2 = VHY ? a.v.zero2 + kbh * vgroups_cap2 * kD : nullptr;
+  const uint16_t* vmask = VHY ? a.v.mask + kbh * vgroups_cap2 * 8 : nullptr;
 
   // One ring per CTA: stage i holds the kWarps consecutive tiles
   // tile_beg + kWarps*i + w (warp w takes tile w).  Layout of a stage:
@@ -545,6 +613,10 @@ decode_attn_kernel(const DevArgs a) {
   const int o_vc = o_kz + (kasym ? kWarps * 64 * NG : 0);
   const int o_vs = o_vc + kWarps * TBV;
   const int o_vz = o_vs + kWarps * 256;
+  const int o_vc2 = o_vz + (vasym ? kWarps * 256 : 0);  // hybrid regions
+  const int o_vs2 = o_vc2 + kWarps * TBV2;
+  const int o_vz2 = o_vs2 + kWarps * 256;
+  const int o_vm = o_vz2 + kWarps * 256;
   const int SBC = kWarps * SB;  // bytes of a stage (same total as kWarps per-tile slots)
   uint8_t* ring = dyn;
 
@@ -589,7 +661,8 @@ decode_attn_kernel(const DevArgs a) {
     const uint32_t nvg = (uint32_t)(g1 - g0 + 1);
     uint8_t* st = ring + slot * SBC;
     const uint32_t kb = n_in * (TBK + 64 * NG * (1 + kasym));
-    const uint32_t vb = n_in * TBV + (VCH ? n_in * 64 * NG : nvg * 256) * (1 + vasym);
+    const uint32_t vb = n_in * TBV + (VCH ? n_in * 64 * NG : nvg * 256) * (1 + vasym) +
+                        (VHY ? n_in * TBV2 + nvg * (256 + 256 + 16) : 0);
     fence_proxy_async();
     mbar_arrive_tx(bar, kb + vb);
     bulk_g2s(st, kcodes + tk * TBK, n_in * TBK, bar);
@@ -602,6 +675,12 @@ decode_attn_kernel(const DevArgs a) {
     } else {
       bulk_g2s(st + o_vs, vscale + g0 * kD, nvg * 256, bar);
       if (vasym) bulk_g2s(st + o_vz, vzero + g0 * kD, nvg * 256, bar);
+    }
+    if constexpr (VHY) {
+      bulk_g2s(st + o_vc2, vcodes2 + tv * TBV2, n_in * TBV2, bar);
+      bulk_g2s(st + o_vs2, vscale2 + g0 * kD, nvg * 256, bar);
+      bulk_g2s(st + o_vz2, vzero2 + g0 * kD, nvg * 256, bar);
+      bulk_g2s(st + o_vm, vmask + g0 * 8, nvg * 16, bar);
     }
   };
 
@@ -934,6 +1013,32 @@ decode_attn_kernel(const DevArgs a) {
       }
       VChunk<BV> vc;
       float2 sv[8], zv[8];
+      if constexpr (VHY) {
+        VChunk<BV - 1> va;
+        uint32_t mk;
+        if (fast) {
+          const int gi = ((t0 - vs) >> vgs) - ((a.t_first + (tile - warp) * kTile - vs) >> vgs);
+          load_vchunk<BV>(vc, sg + o_vc + warp * TBV, lane);
+          load_vchunk<BV - 1>(va, sg + o_vc2 + warp * TBV2, lane);
+          load16<DT>(sv, reinterpret_cast<const uint16_t*>(sg + o_vs + gi * 256) + gid * 16);
+          load16<DT>(zv, reinterpret_cast<const uint16_t*>(sg + o_vs2 + gi * 256) + gid * 16);
+          float2 z2[8];
+          load16<DT>(z2, reinterpret_cast<const uint16_t*>(sg + o_vz2 + gi * 256) + gid * 16);
+          mk = reinterpret_cast<const uint16_t*>(sg + o_vm + gi * 16)[gid];
+          v_hybrid_accumulate<BV, NT>(vc, va, sv, zv, z2, mk, pb, psum, fv, o);
+        } else {
+          const int pv = t0 - vs;
+          load_vchunk<BV>(vc, vcodes + (int64_t)(pv >> 5) * tile_bytes(BV), lane);
+          load_vchunk<BV - 1>(va, vcodes2 + (int64_t)(pv >> 5) * TBV2, lane);
+          const int64_t gg = pv >> vgs;
+          load16<DT>(sv, vscale + gg * kD + gid * 16);
+          load16<DT>(zv, vscale2 + gg * kD + gid * 16);
+          float2 z2[8];
+          load16<DT>(z2, vzero2 + gg * kD + gid * 16);
+          mk = vmask[gg * 8 + gid];
+          v_hybrid_accumulate<BV, NT>(vc, va, sv, zv, z2, mk, pb, psum, fv, o);
+        }
+      } else {
       if (fast) {
         const int gofs = (((t0 - vs) >> vgs) - ((a.t_first + (tile - warp) * kTile - vs) >> vgs)) * 256;
         load_vchunk<BV>(vc, sg + o_vc + warp * TBV, lane);
@@ -948,6 +1053,7 @@ decode_attn_kernel(const DevArgs a) {
       }
       if (vasym) v_packed_accumulate<BV, NT, true>(vc, sv, zv, pb, offp, fv, zf, o);
       else v_packed_accumulate<BV, NT, false>(vc, sv, zv, pb, offp, fv, zf, o);
+      }
     }
     if (!vpacked) {
       // dense V rows (sink / recent / masked rows), probabilities as dtype hi/lo

@@ -9,10 +9,10 @@
 
 namespace innerq {
 
-template <int BK, int DT, int BV, int RP, int NG, int VCH, int GM>
+template <int BK, int DT, int BV, int RP, int NG, int VCH, int GM, int VHY = 0>
 cudaError_t attn_go(const DevArgs& a, dim3 grid, cudaStream_t s) {
-  auto kern = decode_attn_kernel<BK, BV, RP, DT, NG, VCH, GM>;
-  const int smem = attn_dyn_smem(BK, BV, NG, a.k.asym, a.v.asym, RP);
+  auto kern = decode_attn_kernel<BK, BV, RP, DT, NG, VCH, GM, VHY>;
+  const int smem = attn_dyn_smem(BK, BV, NG, a.k.asym, a.v.asym, RP, VHY);
   int dev = 0;
   cudaGetDevice(&dev);
   static int set_bytes[64] = {0};
@@ -26,6 +26,13 @@ cudaError_t attn_go(const DevArgs& a, dim3 grid, cudaStream_t s) {
 
 template <int BK, int DT, int BV, int RP, int GM>
 cudaError_t attn_go_ng(const DevArgs& a, int ng, dim3 grid, cudaStream_t s) {
+  // hybrid values (token groups; keys in groups of 32, argument-fed geometry)
+  if (a.v.hyb) {
+    if constexpr (GM == 0) {
+      if (ng == 4 && !a.v.chan) return attn_go<BK, DT, BV, RP, 4, 0, 0, 1>(a, grid, s);
+    }
+    return cudaErrorNotSupported;
+  }
   // value groups over tokens (VCH 0) or channels (VCH 1)
   switch (ng) {
     case 4: return a.v.chan ? attn_go<BK, DT, BV, RP, 4, 1, GM>(a, grid, s) : attn_go<BK, DT, BV, RP, 4, 0, GM>(a, grid, s);

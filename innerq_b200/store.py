@@ -357,6 +357,8 @@ class PackedSide:
             s.bits, s.group, s.mode, s.over_token = self.bits, self.group, self.mode, int(self.over_token)
             return s
         s.r0, s.flush, s.max_steps = 0, 0, 0
+        s.codes2 = s.scale2 = s.zero2 = s.mask = None
+        s.cap_tiles2 = 0
         nq = self.n_q
         s.codes = self.codes.data_ptr() if nq else None
         s.scale = self.scale.data_ptr() if nq else None
@@ -388,7 +390,11 @@ class HybridSide(PackedSide):
     symmetric at ``bits`` (kept in this store) and asymmetric at ``bits - 1``
     (kept in ``self.zp``) — and a per-group mask chooses the symmetric one
     where its fp32 L1 error is lower.  Materialised through the dequant
-    kernels; the fused attention kernel does not read hybrid stores.
+    kernels, or, for values grouped over tokens, read by the fused attention
+    kernel directly: ``self.mask_bits`` keeps the mask on the device as one
+    bit per (group, dim), 16 bytes per group, bit ``col_scale_idx(dim)`` (the
+    dims' order in the value scales) set where the group keeps its symmetric
+    codes.
 
     The mask is computed from the GPU dequantization with torch sums, so on an
     exact tie of the two fp32 error sums (summation order differs from the
@@ -399,10 +405,28 @@ class HybridSide(PackedSide):
         super().__init__(role, bits, group, _lib.SYM, over_token, w_sink, w_recent, flush, normalize)
         self.zp = PackedSide(role, bits - 1, group, _lib.ASYM, over_token, 0, 0, flush)
         self.masks = []
+        self.mask_bits = None  # [B, H, groups of zp's capacity, 16] uint8
 
     @property
     def fusable(self) -> bool:
-        return not self.quantize
+        return not self.quantize or (self.role == _lib.ROLE_V and self.over_token)
+
+    # dims in the order of the value scales: bit (2 * (d >> 4) + ((d >> 3) & 1))
+    # of 16-bit word d & 7 of a group's mask
+    def _store_mask_bits(self, m: torch.Tensor, g0: int):
+        """Pack the bool mask m [B, H, n_groups, D] of the groups from g0 on."""
+        B, H, n, D = m.shape
+        cap_groups = self.zp.cap_tiles * 32 // self.group
+        if self.mask_bits is None or self.mask_bits.shape[2] < cap_groups:
+            buf = torch.zeros((B, H, cap_groups, 16), dtype=torch.uint8, device=m.device)
+            if self.mask_bits is not None:
+                buf[:, :, :self.mask_bits.shape[2]].copy_(self.mask_bits)
+            self.mask_bits = buf
+        # d = mt*16 + h*8 + gid -> [gid][mt][h], 16 bits per gid
+        bits = m.view(B, H, n, 8, 2, 8).permute(0, 1, 2, 5, 3, 4).reshape(B, H, n, 8, 16)
+        w = (bits.to(torch.int32) << torch.arange(16, device=m.device, dtype=torch.int32)).sum(-1)
+        by = torch.stack([(w & 0xFF), (w >> 8) & 0xFF], dim=-1).to(torch.uint8)  # little-endian words
+        self.mask_bits[:, :, g0:g0 + n] = by.view(B, H, n, 16)
 
     def _check_supported(self):
         super()._check_supported()
@@ -433,9 +457,13 @@ class HybridSide(PackedSide):
         xf = x.float()
         err_a = (da - xf).view(shp).abs().sum(red)
         err_s = (ds - xf).view(shp).abs().sum(red)
-        self.masks.append(err_a > err_s)
+        m = err_a > err_s
+        self.masks.append(m)
+        g0 = self.n_q // self.group
         self.zp._quantize(x)
         PackedSide._quantize(self, x)
+        if self.over_token:
+            self._store_mask_bits(m, g0)
 
     def mask(self):
         return torch.cat(self.masks, dim=2) if self.masks else None
@@ -456,6 +484,22 @@ class HybridSide(PackedSide):
         mid = out[:, :, ns:ns + nq]
         mid.copy_(torch.where(m, mid, zp_mid))
         return out
+
+    def fill_side(self, s: _lib.Side, graph: bool = False) -> _lib.Side:
+        """The symmetric set as the side's store, plus the asymmetric set and
+        the mask (mode INNERQ_HYBRID) once something is packed."""
+        if graph:
+            raise NotImplementedError("graph mode does not cover hybrid stores")
+        super().fill_side(s)
+        if self.n_q:
+            zp = self.zp
+            s.mode = _lib.HYBRID
+            s.codes2, s.scale2, s.zero2 = zp.codes.data_ptr(), zp.scale.data_ptr(), zp.zero.data_ptr()
+            s.mask, s.cap_tiles2 = self.mask_bits.data_ptr(), zp.cap_tiles
+        else:
+            s.codes2 = s.scale2 = s.zero2 = s.mask = None
+            s.cap_tiles2 = 0
+        return s
 
     def ref_views(self):
         if self.n_q == 0:

@@ -119,3 +119,24 @@ def assert_attn_close(out, ref, dtype="fp16"):
     err = np.abs(o - r)
     bound = 1e-3 * np.abs(r).max() + ulp * np.abs(r)
     assert (err <= bound).all(), f"max err {err.max():.3e}, bound at argmax {bound.flat[err.argmax()]:.3e}"
+
+
+def hybrid_side_fp32(side):
+    """[sink | fp32 hybrid dequantization | recent] of a HybridSide: both code
+    sets dequantized by the reference-format kernels and combined with the
+    mask as quant.py:159-176 does (symmetric where the mask is set)."""
+    from innerq_b200 import quant as M
+    parts = []
+    if side.sink is not None and side.sink.shape[2]:
+        parts.append(side.sink.float())
+    codes, scale, zs = side.ref_views()
+    if codes is not None:
+        sym = M._dequantize(codes["nozp"], scale["nozp"], zs["nozp"], side.group, torch.float32,
+                            side.mode, side.over_token)
+        asym = M._dequantize(codes["zp"], scale["zp"], zs["zp"], side.group, torch.float32, 1,
+                             side.over_token)
+        m = scale["mask"].repeat_interleave(side.group, dim=2 if side.over_token else 3)
+        parts.append(torch.where(m, sym, asym))
+    if side.n_recent:
+        parts.append(side.recent.float())
+    return torch.cat(parts, dim=2)

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
         assert n in _lib.EXPORTS, f"{n} has no ctypes signature"
-    assert lib.innerq_abi_version() == 4
+    assert lib.innerq_abi_version() == 5
     assert lib.innerq_tile_bytes(4) == 2048 and lib.innerq_tile_bytes(3) == 1536
     assert lib.innerq_tile_bytes(2) == 1024 and lib.innerq_tile_bytes(5) == -1 and lib.innerq_tile_bytes(1) == 512
 

@@ -252,3 +252,49 @@ def test_prefill_states_are_not_retained():
     del k, v
     torch.cuda.synchronize()
     assert before - torch.cuda.memory_allocated() >= nbytes
+
+
+HYBRID_CASES = [
+    # (k_bits, v_bits, R, dtype, v_group, T0, steps)
+    (3, 2, 4, "fp16", 32, 700, 40),   # the innerq_hybrid preset (scripts/run_lmeval.sh:133-151)
+    (3, 2, 8, "bf16", 32, 517, 33),
+    (4, 3, 4, "fp16", 64, 900, 5),
+    (2, 4, 2, "fp16", 32, 640, 70),
+]
+
+
+@pytest.mark.parametrize("case", HYBRID_CASES, ids=[f"h{i}" for i in range(len(HYBRID_CASES))])
+def test_hybrid_values_fused_vs_reference(case):
+    """Hybrid values (quant.py:133-176) read by the fused kernel: symmetric or
+    asymmetric codes per (group, dim) by the stored mask, against an fp64
+    attention over the reference's fp32 hybrid dequantization."""
+    from innerq_b200.cache import InnerqDynamicLayer
+    from tests._util import gpu_ref_attention, hybrid_side_fp32, side_fp32
+    bk, bv, R, dtype, gv, T0, steps = case
+    kw = dict(k_bits=bk, v_bits=bv, key_flush_size=1, value_flush_size=gv, key_w_sink=32,
+              value_w_sink=32, key_w_recent=96, value_w_recent=96, key_normalize=True,
+              value_group_size=gv, value_quantize_mode="hybrid", _attn_implementation="innerq")
+    Hkv, B = 2, 2
+    k, v = synth_kv(B, Hkv, T0 + steps, dtype=dtype, seed=T0 + bv)
+    layer = InnerqDynamicLayer(cfg(**kw), 0)
+    layer.update(k[:, :, :T0], v[:, :, :T0])
+    for t in range(T0, T0 + steps):
+        layer.update(k[:, :, t:t + 1], v[:, :, t:t + 1])
+    assert layer._fusable()
+    q = synth_q(B, Hkv * R, dtype=dtype, seed=T0 + 1)
+    out = layer.attend(q)
+    ks = layer.key_side
+    K = side_fp32(ks, ks.norm_f if ks.normalize else None).double()
+    V = hybrid_side_fp32(layer.value_side).double()
+    S = K.shape[2]
+    qd = q[:, :, 0].double().view(B, Hkv, R, 128)
+    ref = torch.softmax((qd @ K.transpose(-1, -2)) / math.sqrt(128), dim=-1) @ V
+    r = to_np32(ref.reshape(B, Hkv * R, 128))
+    ulp = 2.0 ** -8 if dtype == "bf16" else 2.0 ** -11
+    err = np.abs(to_np32(out) - r)
+    assert (err <= 1e-3 * np.abs(r).max() + ulp * np.abs(r)).all(), err.max()
+    # and the materialised path agrees with the reference's own get_deq_tensors
+    layer.fused = False
+    Kd, Vd = layer.get_deq_tensors()
+    np.testing.assert_array_equal(to_np32(Vd), to_np32(V.to(Vd.dtype)))
+    assert S == T0 + steps
