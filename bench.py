@@ -134,6 +134,9 @@ def layer_bytes(layer, B, Hkv, Hq, graph_steps=None):
         (k.state_after(graph_steps), v.state_after(graph_steps))
     per_bh = side_bytes(knq, k.n_sink, knr, k.bits, k.group, False, k.mode == 1, k.normalize) \
         + side_bytes(vnq, v.n_sink, vnr, v.bits, v.group, v.over_token, v.mode == 1)
+    if getattr(v, "zp", None) is not None and v.over_token:
+        # hybrid values: the asymmetric (bits-1)-bit set, its scales and zeros, the mask
+        per_bh += vnq * (v.bits - 1) * D // 8 + (vnq // v.group) * (D * 2 * 2 + 16)
     return B * Hkv * per_bh + 2 * B * Hq * D * 2
 
 
@@ -768,6 +771,8 @@ SWEEP = [
     ("C2 BASELINE-literal", 16, 32, 16384, 3, 32, "channels", "symmetric"),
     ("C2 asym", 16, 32, 16384, 2, 32, "tokens", "asymmetric"),
     ("C4 (1 GPU, 4 layers)", 8, 64, 131072, 2, 32, "tokens", "symmetric"),
+    # the innerq_hybrid preset (scripts/run_lmeval.sh:133-151): 3-bit K, 2-bit hybrid V
+    ("C1 innerq_hybrid", 32, 32, 32768, (3, 2), 32, "tokens", "hybrid"),
 ]
 
 
@@ -796,11 +801,16 @@ def run_sweep(a):
         if key in done:
             continue
         done.add(key)
-        a2 = types.SimpleNamespace(kbits=bits, vbits=bits, group=group, v_layout=vlay, mode=mode)
+        kb_, vb_ = bits if isinstance(bits, tuple) else (bits, bits)
+        a2 = types.SimpleNamespace(kbits=kb_, vbits=vb_, group=group, v_layout=vlay,
+                                   mode="symmetric" if mode == "hybrid" else mode)
         kw = cache_kw(a2)
+        if mode == "hybrid":
+            kw["value_quantize_mode"] = "hybrid"
+        bits = kb_
         hkv = a.sweep_hkv or 8
         hq = hq * hkv // 8
-        per_layer = B * hkv * ctx * (bits * 32 + 16)
+        per_layer = B * hkv * ctx * ((kb_ + vb_) * 16 + 16)
         nl = max(4, min(8, int(1.2e9 // per_layer) + 1))
         g = torch.Generator(device=dev)
         g.manual_seed(0)
