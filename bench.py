@@ -745,6 +745,11 @@ def run_c3(a):
         clocks = sampler.stop()
         ours = _lib.launch_count[0] - n0 if per_step_launches is None else per_step_launches * a.steps
     ms = e0.elapsed_time(e1) / a.steps
+    cpu = None
+    if not a.no_cpu_baseline:
+        del model, cache
+        torch.cuda.empty_cache()
+        cpu = c3_cpu_baseline(a, B, S, qcfg)
     line = {
         "metric": "decode tokens/s (Llama-3-8B-shaped, 4-bit InnerQ cache)", "value": round(B / (ms * 1e-3), 1),
         "unit": "tokens/s", "n_gpus": 1, "steps": a.steps, "warmup": max(3, a.warmup),
@@ -753,9 +758,58 @@ def run_c3(a):
         "config": {"workload": "C3: full decode step, random-init Llama-3-8B shape", "batch": B,
                    "context": S, "layers": 32, "k_bits": a.kbits, "v_bits": a.vbits,
                    "step": "eager" if a.no_graph else "recorded once (CUDA graph), replayed"},
-        "gpu_launches": ours, "clocks": clocks,
+        "gpu_launches": ours, "clocks": clocks, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
+
+
+def c3_cpu_baseline(a, B, S, qcfg, steps=2):
+    """C3 on the host cores: the same random-init model shape decoding through
+    the reference's cache restated in torch (oracle/torch_ref.py, dequantize
+    of the whole cache every layer) and Hugging Face sdpa, torch on every
+    core.  A 32-layer step does not fit the time budget, so 1- and 2-layer
+    models are timed and the step is extrapolated: t(32) = t(1) + 31 (t(2) - t(1))."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from oracle.torch_ref import ref_cache
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(1)
+    t = {}
+    for L in (1, 2):
+        cfg = LlamaConfig(num_hidden_layers=L, hidden_size=4096, intermediate_size=14336,
+                          num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                          vocab_size=128256, max_position_embeddings=S + 1024, rope_theta=500000.0)
+        torch.manual_seed(0)
+        model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+        with torch.no_grad():
+            for p in model.parameters():
+                p.normal_(0.0, 0.02)
+        cache = ref_cache(L, **qcfg)
+        for layer in cache.layers:
+            k = (torch.randn((B, 8, S - 1, 128), generator=g)
+                 * torch.exp(torch.randn(128, generator=g))).bfloat16()
+            v = torch.randn((B, 8, S - 1, 128), generator=g).bfloat16()
+            layer.update(k, v)
+            del k, v
+        ids = torch.randint(0, cfg.vocab_size, (steps + 1, B, 1), generator=g)
+        times = []
+        with torch.no_grad():
+            for i in range(steps + 1):
+                pos = torch.full((B, 1), S - 1 + i, dtype=torch.long)
+                t0 = time.perf_counter()
+                model(input_ids=ids[i], past_key_values=cache, position_ids=pos, use_cache=True)
+                if i:  # the first step warms up
+                    times.append(time.perf_counter() - t0)
+        t[L] = statistics.median(times)
+        del model, cache
+    t32 = t[1] + 31 * (t[2] - t[1])
+    return {"value": round(B / t32, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": (f"random-init Llama-3-8B-shaped model, batch {B}, context {S}, bf16, the "
+                       "reference cache restated in torch (oracle/torch_ref.py) + HF sdpa; 1- and "
+                       f"2-layer models timed ({t[1]:.2f} s, {t[2]:.2f} s per step, {steps} steps "
+                       f"each), 32-layer step extrapolated as t1 + 31 (t2 - t1); torch on {cores} threads")}
 
 
 SWEEP = [

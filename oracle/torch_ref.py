@@ -158,3 +158,39 @@ def consumer_attention(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor) -> tor
         K = K[:, :, None].expand(B, H, rep, S, D).reshape(B, H * rep, S, D)
         V = V[:, :, None].expand(B, H, rep, S, D).reshape(B, H * rep, S, D)
     return F.scaled_dot_product_attention(q, K, V)
+
+
+def ref_cache(n_layers: int, **kw):
+    """A Hugging Face cache whose layers are TorchRefLayer (the reference's
+    cache on CPU), for timing a full model's decode step on the host."""
+    from transformers.cache_utils import Cache, CacheLayerMixin
+
+    class _Layer(CacheLayerMixin):
+        is_sliding = False
+
+        def __init__(self):
+            super().__init__()
+            self.ref = TorchRefLayer(**kw)
+            self.n = 0
+
+        def lazy_initialization(self, key_states, value_states):
+            self.dtype, self.device = key_states.dtype, key_states.device
+            self.is_initialized = True
+
+        def update(self, key_states, value_states, *args, **kwargs):
+            if not self.is_initialized:
+                self.lazy_initialization(key_states, value_states)
+            self.n += key_states.shape[-2]
+            return self.ref.update(key_states, value_states)
+
+        def get_mask_sizes(self, query_length):
+            q = query_length if isinstance(query_length, int) else query_length.shape[0]
+            return self.n + q, 0
+
+        def get_seq_length(self):
+            return self.n
+
+        def get_max_cache_shape(self):
+            return -1
+
+    return Cache(layers=[_Layer() for _ in range(n_layers)])
