@@ -141,6 +141,74 @@ def layer_bytes(layer, B, Hkv, Hq, graph_steps=None):
 
 
 # --------------------------------------------------------------- clocks ---
+class NvmlClockSampler:
+    """SM clock and clock-event reasons of one GPU read through NVML, in a
+    burst taken while the GPU executes the timed region: the host enqueues
+    every step of the region first and samples afterwards, so no launch waits
+    behind an NVML call (polling during the launches, from nvidia-smi or from
+    a thread, delayed the ranks' launches by milliseconds per sample on
+    multi-GPU boxes)."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, torch_device, enabled=True):
+        self.dev = torch_device
+        self.enabled = enabled
+        self.samples = []
+        self.h = None
+
+    def _handle(self, N):
+        import torch
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+            return N.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return N.nvmlDeviceGetHandleByIndex(self.dev.index or 0)
+
+    def start(self):
+        """Before the region: open NVML (nothing is sampled yet)."""
+        if not self.enabled:
+            return
+        import pynvml as N
+        N.nvmlInit()
+        self.N = N
+        self.h = self._handle(N)
+        self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM))
+
+    def burst(self, region_ms_estimate, n=5):
+        """After the region's launches are enqueued: n samples spread over the
+        first 60% of the region's expected duration."""
+        if self.h is None:
+            return
+        N = self.N
+        gap = max(0.5, 0.6 * region_ms_estimate / n) / 1000.0
+        for _ in range(n):
+            sm = float(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+            r = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            self.samples.append((sm, [name for name, attr in self.REASONS if r & getattr(N, attr)]))
+            time.sleep(gap)
+
+    def stop(self):
+        if not self.samples:
+            return None
+        reasons = sorted({n for _, rs in self.samples for n in rs})
+        return {"sm_mhz": statistics.median([s for s, _ in self.samples]), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples),
+                "source": "NVML, sampled while the GPU ran the enqueued timed region"}
+
+
+def clock_sampler(torch_device, local, period_ms=20, enabled=True):
+    """NVML bursts when pynvml is importable, else nvidia-smi polling."""
+    try:
+        import pynvml  # noqa: F401
+        return NvmlClockSampler(torch_device, enabled)
+    except ImportError:
+        return ClockSampler(local, period_ms, enabled)
+
+
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -172,6 +240,9 @@ class ClockSampler:
         while time.time() < t_end and os.path.getsize(self.f.name) == 0 and self.proc.poll() is None:
             time.sleep(0.01)
         self.skip = sum(1 for _ in open(self.f.name))  # samples taken before the region
+
+    def burst(self, region_ms_estimate, n=5):
+        """Polling runs on its own; nothing to do after the enqueue."""
 
     def stop(self):
         if self.proc is None:
@@ -532,9 +603,9 @@ def run_ours(a):
             graph, gsteps[0], per_step_launches = None, None, None
             step = eager_step
 
-    # ---- device-resident timed region (rank 0 samples its GPU's clocks: one
-    #      nvidia-smi per rank at a short period slowed the host's launches)
-    sampler = ClockSampler(local, period_ms=20 if world == 1 else 100, enabled=rank == 0)
+    # ---- device-resident timed region (rank 0 samples its GPU's clocks)
+    sampler = clock_sampler(dev, local, period_ms=20, enabled=rank == 0 and
+                            os.environ.get("INNERQ_BENCH_CLOCKS", "1") != "0")
     nbytes = 0
     sync_all()
     sampler.start()
@@ -544,6 +615,8 @@ def run_ours(a):
         nbytes += bytes_now()
         step(i)
     ev1.record(stream)
+    # the region is enqueued: sample the clocks while the GPU runs it
+    sampler.burst(a.steps * min(mode_ms.values()))
     sync_all()
     clocks = sampler.stop()
     launches = _lib.launch_count[0] - launches0 if graph is None else per_step_launches * a.steps
@@ -650,7 +723,12 @@ def run_ours(a):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    # release the recorded step (it holds NCCL work in the context-chunk mode)
+    # and the communicator buffers before the process group goes
+    graph = gather = merges = None
+    torch.cuda.synchronize()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -733,7 +811,7 @@ def run_c3(a):
                 step(max(3, a.warmup) + i)
             torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        sampler = ClockSampler(0)
+        sampler = clock_sampler(dev, 0)
         sampler.start()
         n0 = _lib.launch_count[0]
         i0 = max(3, a.warmup) * (1 if per_step_launches is None else 2)
@@ -741,6 +819,7 @@ def run_c3(a):
         for i in range(a.steps):
             step(i0 + i)
         e1.record()
+        sampler.burst(a.steps * 7.0)  # ~7-8 ms per replayed step
         torch.cuda.synchronize()
         clocks = sampler.stop()
         ours = _lib.launch_count[0] - n0 if per_step_launches is None else per_step_launches * a.steps
