@@ -11,8 +11,11 @@ K = N(0,1) x exp(N(0,1)) per channel, V = N(0,1), q = N(0,1), fp16, seeded.
 
 One step = one decode token through all 32 layers: append the new K/V token
 (quantize-and-pack) and run the fused decode attention per layer.  With N
-GPUs the 8 KV heads (and their query heads) are partitioned across ranks and
-the per-layer outputs are all-gathered over NCCL once per step.
+GPUs the 8 KV heads (and their query heads) are partitioned across ranks.  By
+default the scaling is weak: the global batch is 32 x N, so every GPU holds
+the one-GPU workload's 256 (sequence, KV head) pairs and the attention path
+has no exchange; `--scaling strong` splits the 32-sequence workload itself and
+all-gathers the KV-head shards' outputs over NCCL once per step.
 
 `value` is algorithmic HBM bytes per step (packed codes + scales + fp16 sink /
 recent + normalisation factor + q + out, summed over all ranks) / time.
@@ -51,6 +54,12 @@ def parse():
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--kbits", type=int, default=None)
     ap.add_argument("--vbits", type=int, default=None)
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak (default): every GPU keeps the one-GPU workload's (sequence, KV "
+                         "head) pairs, the global batch grows with the GPU count and the KV heads "
+                         "are partitioned (no exchange on the attention path); strong: the "
+                         "one-GPU workload itself is split, and the KV-head shards' outputs are "
+                         "all-gathered once per step")
     ap.add_argument("--ctx-shards", type=int, default=1,
                     help="context chunks per KV-head shard (N GPUs = head shards x ctx shards): "
                          "each rank stores one chunk of the context, the split partials are "
@@ -410,7 +419,10 @@ def run_ours(a):
     last = cs == CS - 1           # the chunk that holds the recent window and takes the appends
     h_lo, h_hi = head_shard(a.hkv, HS, hs)
     hkv, hq = h_hi - h_lo, (h_hi - h_lo) * (a.hq // a.hkv)
-    B, L = a.batch, a.layers
+    # weak scaling: the global batch grows with the head shards, so each rank
+    # holds as many (sequence, KV head) pairs as the one-GPU workload
+    B_global = a.batch * (HS if a.scaling == "weak" else 1)
+    B, L = B_global, a.layers
     kw = cache_kw(a)
     ctx_group = None
     if CS > 1:
@@ -462,7 +474,7 @@ def run_ours(a):
             grp = dist.new_group(list(range(j, world, CS)))
             if j == cs:
                 head_group = grp
-    gather = HeadGather(out, head_group) if HS > 1 else None
+    gather = HeadGather(out, head_group) if (HS > 1 and a.scaling == "strong") else None
     merges = None
     if CS > 1:
         # the same split count on every rank of a chunk group (the largest any
@@ -688,7 +700,7 @@ def run_ours(a):
         line = {
             "metric": metric_name(a), "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "higher_is_better": True, "scaling": a.scaling, "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded N(0,1) K with exp(N(0,1)) channel outliers, N(0,1) V and q)",
             "config": {
                 "workload": ("C4: decode step over an 80-layer 70B-shaped (64 q / 8 kv heads) "
@@ -699,7 +711,12 @@ def run_ours(a):
                 "head_dim": D, "k_bits": a.kbits, "v_bits": a.vbits, "group": a.group,
                 "v_groups_over": a.v_layout, "mode": a.mode,
                 "parallelism": (f"kv-head shards x{HS}" + (f", context chunks x{CS} (split partials "
-                                "all-gathered and merged per layer)" if CS > 1 else "")),
+                                "all-gathered and merged per layer)" if CS > 1 else "")
+                                + (f"; weak scaling: global batch {B} = {a.batch} x {HS} head shards, "
+                                   f"{B * hkv} (sequence, KV head) pairs per GPU"
+                                   if a.scaling == "weak" and HS > 1 else "")
+                                + ("; KV-head outputs all-gathered once per step"
+                                   if gather is not None else "")),
                 "step": "eager launches" if graph is None else "recorded once (CUDA graph), replayed",
                 "step_trial_ms": {k_: round(v_, 3) for k_, v_ in mode_ms.items()},
                 "l2": f"inputs larger than L2 ({total_bytes / 1e9:.1f} GB of cache read per step)",
