@@ -188,12 +188,14 @@ class NvmlClockSampler:
         self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM))
 
     def burst(self, region_ms_estimate, n=5):
-        """After the region's launches are enqueued: n samples spread over the
-        first 60% of the region's expected duration."""
+        """After the region's launches are enqueued: n samples spread over
+        20-60% of the region's expected duration."""
         if self.h is None:
             return
         N = self.N
-        gap = max(0.5, 0.6 * region_ms_estimate / n) / 1000.0
+        # let the other ranks finish enqueueing their steps first
+        time.sleep(0.2 * region_ms_estimate / 1000.0)
+        gap = max(0.5, 0.4 * region_ms_estimate / n) / 1000.0
         for _ in range(n):
             sm = float(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
             r = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
