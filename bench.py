@@ -1024,9 +1024,12 @@ def run_sweep(a):
         # append: one K token (channel groups) and one 4096-token chunk
         side = PackedSide(_lib.ROLE_K, bits, group, _lib.SYM if mode == "symmetric" else _lib.ASYM,
                           False, 0, 0, 1)
-        x = torch.randn((B, hkv, 4096, D), device=dev, generator=g).half()
+        # two chunks used in turn: together larger than L2
+        xs = [torch.randn((B, hkv, 4096, D), device=dev, generator=g).half() for _ in range(2)]
+        x = xs[0]
+        n_rep = 8
         side.prefill(x[:, :, :1])
-        side.reserve(8192)
+        side.reserve(4096 * (n_rep + 2))
         torch.cuda.synchronize()
         e0.record()
         for i in range(20):
@@ -1034,29 +1037,49 @@ def run_sweep(a):
         e1.record()
         torch.cuda.synchronize()
         us_tok = e0.elapsed_time(e1) * 1e3 / 20
+        # chunk launches back to back (the host runs ahead of the GPU, so
+        # launch overhead is not timed); mean per chunk
         side.n_q = 0
+        side._quantize(xs[1])
+        torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("chunk")  # profiling handle (ncu --nvtx-include chunk/)
         e0.record()
-        side._quantize(x)
+        for i in range(n_rep):
+            side._quantize(xs[i % 2])
         e1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
-        us_chunk = e0.elapsed_time(e1) * 1e3
-        # the same chunk as values (token groups, the InnerQ V layout)
+        us_chunk = e0.elapsed_time(e1) * 1e3 / n_rep
+        # keys with the normalisation factor (innerq_base), set by the first chunk
+        nside = PackedSide(_lib.ROLE_K, bits, group, _lib.SYM if mode == "symmetric" else _lib.ASYM,
+                           False, 0, 0, 1, normalize=True)
+        nside.prefill(xs[1])
+        nside.reserve(4096 * (n_rep + 2))
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(n_rep):
+            nside._quantize(xs[i % 2])
+        e1.record()
+        torch.cuda.synchronize()
+        us_chunk_n = e0.elapsed_time(e1) * 1e3 / n_rep
+        del nside
+        # the same chunks as values (token groups, the InnerQ V layout)
         vside = PackedSide(_lib.ROLE_V, bits, group, _lib.SYM if mode == "symmetric" else _lib.ASYM,
                            True, 0, 0, max(32, group))
         vside.prefill(x[:, :, :max(32, group)])
-        vside.reserve(8192)
+        vside.reserve(4096 * (n_rep + 2))
         vside.n_q = 0
+        vside._quantize(xs[1])
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("chunk_v")
         e0.record()
-        vside._quantize(x)
+        for i in range(n_rep):
+            vside._quantize(xs[i % 2])
         e1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
-        us_chunk_v = e0.elapsed_time(e1) * 1e3
-        del side, vside, x
+        us_chunk_v = e0.elapsed_time(e1) * 1e3 / n_rep
+        del side, vside, x, xs
         torch.cuda.empty_cache()
         print(json.dumps({
             "config": name, "batch": B, "q_heads": hq, "kv_heads": hkv, "context": ctx,
@@ -1066,6 +1089,7 @@ def run_sweep(a):
             "append_1_token_us": round(us_tok, 1), "append_4096_chunk_us": round(us_chunk, 1),
             "chunk_read_GBs": round(B * hkv * 4096 * D * 2 / us_chunk / 1e3, 1),
             "append_4096_chunk_v_us": round(us_chunk_v, 1),
+            "append_4096_chunk_knorm_us": round(us_chunk_n, 1),
             "chunk_v_read_GBs": round(B * hkv * 4096 * D * 2 / us_chunk_v / 1e3, 1)}), flush=True)
 
 

@@ -201,6 +201,57 @@ __device__ __forceinline__ int code_by_cuts(float a, const float* cut) {
   }
 }
 
+// --------------------------------- symmetric codes, two elements at a time ---
+// For a dtype value a, a >= cut (fp32) exactly when a >= ru(cut), the
+// smallest dtype value at or above the cut.  So with the cuts rounded up to
+// the dtype, the code magnitude of |a| is the number of cuts it reaches, and
+// both 16-bit elements of a word are coded by packed dtype instructions (on
+// the FMA pipe): per cut, a packed compare giving 1.0 / 0.0 and a packed FMA
+// adding sign(a) * that to an accumulator that starts at BASE + 2^(b-1), with
+// BASE = 1024 (fp16) or 128 (bf16): there consecutive integers are consecutive
+// bit patterns, so the low byte of each half ends up holding the offset-binary
+// code u = 2^(b-1) + sign * c exactly.  A NaN element compares false: code 0.
+template <int DT> __device__ __forceinline__ uint32_t cut_bits(float cut);
+template <> __device__ __forceinline__ uint32_t cut_bits<F16>(float cut) {
+  return __half_as_ushort(__float2half_ru(cut));
+}
+template <> __device__ __forceinline__ uint32_t cut_bits<BF16>(float cut) {
+  return __bfloat16_as_ushort(__float2bfloat16_ru(cut));
+}
+
+template <int DT> struct Pair;
+template <> struct Pair<F16> {
+  using T = __half2;
+  static constexpr uint32_t kOne = 0x3c003c00u, kBase = 0x64006400u;  // 1.0, 1024.0
+};
+template <> struct Pair<BF16> {
+  using T = __nv_bfloat162;
+  static constexpr uint32_t kOne = 0x3f803f80u, kBase = 0x43004300u;  // 1.0, 128.0
+};
+template <int DT> __device__ __forceinline__ typename Pair<DT>::T as_pair(uint32_t w) {
+  return *reinterpret_cast<const typename Pair<DT>::T*>(&w);
+}
+template <int DT> __device__ __forceinline__ uint32_t pair_bits(typename Pair<DT>::T v) {
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+// max(m, |a|) per half, in the dtype (exact)
+template <int DT> __device__ __forceinline__ uint32_t absmax2(uint32_t m, uint32_t a) {
+  return pair_bits<DT>(__hmax2(as_pair<DT>(m), __habs2(as_pair<DT>(a))));
+}
+
+// Offset-binary symmetric codes of the two elements of w in bytes 0 and 2;
+// cb[k]: the cut of code k + 1 rounded up to the dtype, for (half 0, half 1)
+template <int DT, int BITS>
+__device__ __forceinline__ uint32_t sym_codes2(uint32_t w, const uint32_t* cb) {
+  constexpr int QM = (1 << (BITS - 1)) - 1;
+  const auto a = __habs2(as_pair<DT>(w));
+  const auto sg = as_pair<DT>((w & 0x80008000u) | Pair<DT>::kOne);  // +-1.0
+  auto acc = as_pair<DT>(Pair<DT>::kBase + (1u << (BITS - 1)) * 0x00010001u);
+#pragma unroll
+  for (int k = 0; k < QM; ++k) acc = __hfma2(__hge2(a, as_pair<DT>(cb[k])), sg, acc);
+  return pair_bits<DT>(acc);
+}
+
 // ------------------------------------------- programmatic dependent launch ---
 // Every kernel of the decode step is launched as the programmatic dependent of
 // the previous kernel on its stream (launch_pdl), so its launch and prologue

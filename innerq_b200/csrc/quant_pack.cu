@@ -294,16 +294,22 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
                  const uint16_t* __restrict__ nf, int group, uint8_t* __restrict__ codes,
                  uint16_t* __restrict__ scale, uint16_t* __restrict__ zero, int64_t cap_tiles,
                  int64_t t_off) {
-  __shared__ float f_s[NORM ? kD : 1], rf_s[NORM ? kD : 1];
+  __shared__ __align__(8) float f_s[NORM ? kD : 2];
+  __shared__ __align__(8) float rf_s[NORM ? kD : 2];
   const int h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
   const int64_t bh = (int64_t)b * H + h;
+  // fp16 factors that are all positive and finite take the paired division
+  // (Markstein's sequence on float pairs); others take the scalar path
+  bool pair_div = false;
   if constexpr (NORM) {
+    bool ok = true;
     if (threadIdx.x < kD) {
       const float f = to_f<DT>(nf[bh * kD + threadIdx.x]);
       f_s[threadIdx.x] = f;
       rf_s[threadIdx.x] = shared_rcp<DT>(f);
+      ok = f > 0.f && f < INFINITY;
     }
-    __syncthreads();
+    pair_div = __syncthreads_and(ok) && DT == F16;
   }
   const int lane = threadIdx.x & 31, kb = lane & 3;
   const int t = blockIdx.x * 64 + (threadIdx.x >> 5) * 8 + (lane >> 2);
@@ -326,7 +332,23 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
   auto val = [&](int e) -> float {
     return to_f<DT>((uint16_t)((e & 1) ? (raw[e >> 1] >> 16) : (raw[e >> 1] & 0xffffu)));
   };
-  if constexpr (NORM) {  // cache.py:125 key_states / factor, in the dtype (stored back as dtype bits)
+  if (NORM && !ASYM && pair_div) {
+    // cache.py:125 key_states / factor in fp16, two elements at a time: the
+    // magnitude's quotient (Markstein: q = |x| rf, r = |x| - q f exact,
+    // RN(q + r rf) = RN(|x| / f)) rounded to fp16, the sign put back
+    const float2* f2p = reinterpret_cast<const float2*>(f_s + kb * 32);
+    const float2* r2p = reinterpret_cast<const float2*>(rf_s + kb * 32);
+#pragma unroll
+    for (int w = 0; w < 16; ++w) {
+      const uint32_t mag = raw[w] & 0x7fff7fffu;
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&mag));
+      const float2 f = f2p[w], rf = r2p[w];
+      const float2 q = __fmul2_rn(a, rf);
+      const float2 r = __ffma2_rn(make_float2(-q.x, -q.y), f, a);
+      const __half2 h = __float22half2_rn(__ffma2_rn(r, rf, q));
+      raw[w] = *reinterpret_cast<const uint32_t*>(&h) | (raw[w] & 0x80008000u);
+    }
+  } else if constexpr (NORM) {  // cache.py:125 key_states / factor, in the dtype (stored back as dtype bits)
 #pragma unroll
     for (int w = 0; w < 16; ++w) {
       uint32_t nw = 0u;
@@ -340,6 +362,70 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
       }
       raw[w] = nw;
     }
+  }
+  const int64_t p = t_off + t;
+  const int64_t ti = p >> 5;
+  const int r = (int)(p & 31), gid = r & 7, j = r >> 3;
+  uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
+  const int kpg = group >> 5;  // 32-dim blocks per group
+  if constexpr (!ASYM) {
+    // symmetric: the group max in the dtype (exact), codes two elements per
+    // word (sym_codes2), moved into the row-layout words by byte permutes
+    float mx;
+    {
+      uint32_t m2 = 0u;
+#pragma unroll
+      for (int w = 0; w < 16; ++w) m2 = absmax2<DT>(m2, raw[w]);
+      mx = fmaxf(to_f<DT>((uint16_t)(m2 & 0xffffu)), to_f<DT>((uint16_t)(m2 >> 16)));
+    }
+    if (group >= 64) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    if (group >= 128) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float s = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx));
+    constexpr int QM = (1 << (BITS - 1)) - 1;
+    uint32_t cb[QM];
+    {
+      float cut[QM];
+      group_cuts<DT, QM>(s, cut);
+#pragma unroll
+      for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[k]) * 0x00010001u;
+    }
+    if (valid && kb % kpg == 0) {
+      const int ng = kD / group, g = kb / kpg;
+      scale[(bh * cap_tiles + ti) * 32 * ng + row_scale_idx(r, g, ng)] = from_f<DT>(s);
+    }
+    // word w holds elements 2w, 2w+1 = dims kb*32 + hf*16 + 4*tq + i with
+    // hf = w >> 3, tq = (w >> 1) & 3, i = 2*(w & 1) + (half)
+#pragma unroll
+    for (int tq = 0; tq < 4; ++tq) {
+      const int lane2 = gid * 4 + tq;
+      uint32_t P[2];  // hf = 0, 1: the codes of i = 0..3 in bytes 0..3
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int w = hf * 8 + 2 * tq;
+        P[hf] = __byte_perm(sym_codes2<DT, BITS>(raw[w], cb), sym_codes2<DT, BITS>(raw[w + 1], cb), 0x6420);
+      }
+      if constexpr (BITS == 4) {
+        // nibble 2i + hf
+        if (valid) *reinterpret_cast<uint32_t*>(tb + j * 512 + lane2 * 16 + kb * 4) = P[0] | (P[1] << 4);
+      } else {
+        // low two bits: crumb 4i + (kb&1)*2 + hf of word kb>>1, shared with
+        // block kb^1; 3-bit: bit 2 at 8i + kb*2 + hf of plane H
+        const int sh = (kb & 1) * 4;
+        const uint32_t l0 = BITS == 3 ? P[0] & 0x03030303u : P[0];
+        const uint32_t l1 = BITS == 3 ? P[1] & 0x03030303u : P[1];
+        uint32_t w = (l0 << sh) | (l1 << (sh + 2));
+        w |= __shfl_xor_sync(0xffffffffu, w, 1);
+        if (valid && !(kb & 1))
+          *reinterpret_cast<uint32_t*>(tb + (j >> 1) * 512 + lane2 * 16 + (j & 1) * 8 + (kb >> 1) * 4) = w;
+        if constexpr (BITS == 3) {
+          uint32_t wh = (((P[0] >> 2) & 0x01010101u) << (2 * kb)) | (((P[1] >> 2) & 0x01010101u) << (2 * kb + 1));
+          wh |= __shfl_xor_sync(0xffffffffu, wh, 1);
+          wh |= __shfl_xor_sync(0xffffffffu, wh, 2);
+          if (valid && kb == 0) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = wh;
+        }
+      }
+    }
+    return;
   }
   float s, z = 0.f;
   if constexpr (!ASYM) {
@@ -380,11 +466,6 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
       return (uint32_t)code_by_cuts<QM>(rnd<DT>(v - z), cut);
     }
   };
-  const int64_t p = t_off + t;
-  const int64_t ti = p >> 5;
-  const int r = (int)(p & 31), gid = r & 7, j = r >> 3;
-  uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
-  const int kpg = group >> 5;  // 32-dim blocks per group
   if (valid && kb % kpg == 0) {
     const int ng = kD / group, g = kb / kpg;
     const int64_t si = (bh * cap_tiles + ti) * 32 * ng + row_scale_idx(r, g, ng);
@@ -576,7 +657,7 @@ __device__ __forceinline__ void pack_col_group(const uint16_t* __restrict__ x0, 
 // held in registers: once for its max (min) and, for groups above 32 tokens,
 // once more for the codes (from L2).  Codes use fast_code's exact rounding.
 template <int DT, int BITS, int ASYM>
-__global__ void __launch_bounds__(64)
+__global__ void __launch_bounds__(64, 8)
 pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st, int group,
                  uint8_t* __restrict__ codes, uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
                  int64_t cap_tiles, int64_t t_off) {
@@ -595,6 +676,50 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
   auto val = [&](int t, int e) -> float {
     return to_f<DT>((uint16_t)(e ? (raw[t] >> 16) : (raw[t] & 0xffffu)));
   };
+  if constexpr (!ASYM) {
+    // symmetric: per-dim max in the dtype (exact), codes of both dims of a
+    // token word at once (sym_codes2), 4 tokens' codes gathered into the
+    // [dim][token / 4] byte words by byte permutes
+    constexpr int QM = (1 << (BITS - 1)) - 1;
+    uint32_t m2 = 0u;
+    for (int c0 = 0; c0 < group; c0 += 32) {
+      load(c0);
+#pragma unroll
+      for (int t = 0; t < 32; ++t) m2 = absmax2<DT>(m2, raw[t]);
+    }
+    float s[2];
+    s[0] = rnd<DT>(div_qmax<DT, QM>(to_f<DT>((uint16_t)(m2 & 0xffffu))));
+    s[1] = rnd<DT>(div_qmax<DT, QM>(to_f<DT>((uint16_t)(m2 >> 16))));
+    uint32_t cb[QM];
+    {
+      float cut[2][QM];
+      group_cuts<DT, QM>(s[0], cut[0]);
+      group_cuts<DT, QM>(s[1], cut[1]);
+#pragma unroll
+      for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[0][k]) | (cut_bits<DT>(cut[1][k]) << 16);
+    }
+    for (int c0 = 0; c0 < group; c0 += 32) {
+      if (group > 32) load(c0);
+#pragma unroll
+      for (int t4 = 0; t4 < 8; ++t4) {
+        const uint32_t f0 = sym_codes2<DT, BITS>(raw[4 * t4], cb), f1 = sym_codes2<DT, BITS>(raw[4 * t4 + 1], cb);
+        const uint32_t f2 = sym_codes2<DT, BITS>(raw[4 * t4 + 2], cb), f3 = sym_codes2<DT, BITS>(raw[4 * t4 + 3], cb);
+        // [f0.b0, f1.b0, f0.b2, f1.b2], [f2.b0, f3.b0, f2.b2, f3.b2]
+        const uint32_t p01 = __byte_perm(f0, f1, 0x6240), p23 = __byte_perm(f2, f3, 0x6240);
+        cbt[2 * dp][(c0 >> 2) + t4] = __byte_perm(p01, p23, 0x5410);
+        cbt[2 * dp + 1][(c0 >> 2) + t4] = __byte_perm(p01, p23, 0x7632);
+      }
+    }
+    const int64_t groups_cap = cap_tiles * 32 / group;
+    const int64_t t_abs = t_off + (int64_t)gi * group;
+    const int64_t gglob = t_abs / group;
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+      scale[(bh * groups_cap + gglob) * kD + col_scale_idx(2 * dp + e)] = from_f<DT>(s[e]);
+    __syncthreads();
+    store_col_tiles<BITS>(cbt, codes, bh, cap_tiles, t_abs, group / 32, threadIdx.x, 64);
+    return;
+  }
   float mx0 = ASYM ? -INFINITY : 0.f, mx1 = mx0, mn0 = INFINITY, mn1 = INFINITY;
   for (int c0 = 0; c0 < group; c0 += 32) {
     load(c0);
