@@ -296,6 +296,10 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
                  int64_t t_off) {
   __shared__ __align__(8) float f_s[NORM ? kD : 2];
   __shared__ __align__(8) float rf_s[NORM ? kD : 2];
+  // the factor pairs of word w of block kb: {f, f, rf, rf} of dims kb*32 + 2w,
+  // +1; blocks 17 entries apart, so the 4 blocks a warp reads at once sit in
+  // different banks
+  __shared__ float4 fr_s[NORM ? 4 : 1][17];
   const int h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
   const int64_t bh = (int64_t)b * H + h;
   // fp16 factors that are all positive and finite take the paired division
@@ -308,6 +312,9 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
       f_s[threadIdx.x] = f;
       rf_s[threadIdx.x] = shared_rcp<DT>(f);
       ok = f > 0.f && f < INFINITY;
+      float* fr = reinterpret_cast<float*>(&fr_s[threadIdx.x >> 5][(threadIdx.x & 31) >> 1]);
+      fr[threadIdx.x & 1] = f;
+      fr[2 + (threadIdx.x & 1)] = rf_s[threadIdx.x];
     }
     pair_div = __syncthreads_and(ok) && DT == F16;
   }
@@ -336,13 +343,12 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
     // cache.py:125 key_states / factor in fp16, two elements at a time: the
     // magnitude's quotient (Markstein: q = |x| rf, r = |x| - q f exact,
     // RN(q + r rf) = RN(|x| / f)) rounded to fp16, the sign put back
-    const float2* f2p = reinterpret_cast<const float2*>(f_s + kb * 32);
-    const float2* r2p = reinterpret_cast<const float2*>(rf_s + kb * 32);
 #pragma unroll
     for (int w = 0; w < 16; ++w) {
       const uint32_t mag = raw[w] & 0x7fff7fffu;
       const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&mag));
-      const float2 f = f2p[w], rf = r2p[w];
+      const float4 fr = fr_s[kb][w];
+      const float2 f = make_float2(fr.x, fr.y), rf = make_float2(fr.z, fr.w);
       const float2 q = __fmul2_rn(a, rf);
       const float2 r = __ffma2_rn(make_float2(-q.x, -q.y), f, a);
       const __half2 h = __float22half2_rn(__ffma2_rn(r, rf, q));
