@@ -663,7 +663,7 @@ __device__ __forceinline__ void pack_col_group(const uint16_t* __restrict__ x0, 
 // held in registers: once for its max (min) and, for groups above 32 tokens,
 // once more for the codes (from L2).  Codes use fast_code's exact rounding.
 template <int DT, int BITS, int ASYM>
-__global__ void __launch_bounds__(64, 8)
+__global__ void __launch_bounds__(64)
 pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t st, int group,
                  uint8_t* __restrict__ codes, uint16_t* __restrict__ scale, uint16_t* __restrict__ zero,
                  int64_t cap_tiles, int64_t t_off) {
@@ -705,7 +705,9 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
       for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[0][k]) | (cut_bits<DT>(cut[1][k]) << 16);
     }
     for (int c0 = 0; c0 < group; c0 += 32) {
-      if (group > 32) load(c0);
+      // 3 / 4 bits: the chunk is read again (from L2) rather than kept in
+      // registers across the cut computation, which would cost occupancy
+      if (group > 32 || BITS > 2) load(c0);
 #pragma unroll
       for (int t4 = 0; t4 < 8; ++t4) {
         const uint32_t f0 = sym_codes2<DT, BITS>(raw[4 * t4], cb), f1 = sym_codes2<DT, BITS>(raw[4 * t4 + 1], cb);
