@@ -181,6 +181,33 @@ class InnerqDynamicLayer(CacheLayerMixin):
             return key_states, value_states
         return self.get_deq_tensors()
 
+    # --------------------------------------------------------- serialisation
+    def state_dict(self) -> dict:
+        """The layer's cache content as host tensors: both stores
+        (PackedSide.state_dict) and the token count."""
+        if self._gstep is not None:
+            raise RuntimeError("cannot serialise a layer in graph mode (call graph_end first)")
+        return {"cumulative_length": self.cumulative_length, "is_initialized": bool(self.is_initialized),
+                "sliding_window": getattr(self, "sliding_window", None),
+                "k": self._k.state_dict(), "v": self._v.state_dict()}
+
+    def load_state_dict(self, d: dict, device=None) -> None:
+        """Restore what state_dict() wrote, onto `device` (default: the
+        current CUDA device).  The layer must have been built from the same
+        config (bits, groups, windows, modes are checked)."""
+        if d.get("sliding_window") != getattr(self, "sliding_window", None):
+            raise ValueError(f"saved layer has sliding_window={d.get('sliding_window')!r}, "
+                             f"this layer {getattr(self, 'sliding_window', None)!r}")
+        self._k.load_state_dict(d["k"], device)
+        self._v.load_state_dict(d["v"], device)
+        self.cumulative_length = int(d["cumulative_length"])
+        self.is_initialized = bool(d["is_initialized"])
+        self._attn = None
+        if self.is_initialized:
+            self.dtype, self.device = self._k.dtype, self._k.device
+            if hasattr(self, "_sliding_window_tensor"):
+                self._sliding_window_tensor = self._sliding_window_tensor.to(self.device)
+
     # ------------------------------------------------------------ graph mode
     def graph_begin(self, step: torch.Tensor, max_steps: int) -> None:
         """Enter graph mode (see DynamicCache.graph_begin)."""
@@ -321,6 +348,37 @@ class DynamicCache(Cache):
                     layers.append(InnerqDynamicLayer(config=config, layer_idx=layer_idx))
         super().__init__(layers=layers, offloading=offloading,
                          offload_only_non_sliding=offload_only_non_sliding)
+
+    # --------------------------------------------------------- serialisation
+    FORMAT = "innerq_b200.DynamicCache"
+    FORMAT_VERSION = 1
+
+    def state_dict(self) -> dict:
+        """Every layer's packed cache as host tensors and plain values (no
+        pickled objects: loadable with torch.load(weights_only=True))."""
+        return {"format": self.FORMAT, "version": self.FORMAT_VERSION,
+                "layers": [layer.state_dict() for layer in self.layers]}
+
+    def load_state_dict(self, sd: dict, device=None) -> None:
+        if sd.get("format") != self.FORMAT or sd.get("version") != self.FORMAT_VERSION:
+            raise ValueError(f"not a {self.FORMAT} v{self.FORMAT_VERSION} state: "
+                             f"{sd.get('format')!r} v{sd.get('version')!r}")
+        if len(sd["layers"]) != len(self.layers):
+            raise ValueError(f"saved cache has {len(sd['layers'])} layers, this one {len(self.layers)}")
+        for layer, d in zip(self.layers, sd["layers"]):
+            layer.load_state_dict(d, device)
+
+    def save(self, path) -> None:
+        """Write the packed cache to `path` (torch.save of state_dict())."""
+        torch.save(self.state_dict(), path)
+
+    @classmethod
+    def load(cls, path, config, device=None) -> "DynamicCache":
+        """A cache built from `config` (the model config the saved cache was
+        built with) holding the content saved at `path`, on `device`."""
+        cache = cls(config=config)
+        cache.load_state_dict(torch.load(path, map_location="cpu", weights_only=True), device)
+        return cache
 
     # ------------------------------------------------------------ graph mode
     def graph_begin(self, max_steps: int) -> torch.Tensor:

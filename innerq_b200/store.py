@@ -270,6 +270,75 @@ class PackedSide:
                   scale.data_ptr(), _ptr(zs if sign is None else None), stream_ptr(self.device))
         return codes, scale, zs
 
+    # ------------------------------------------------------- serialisation
+    _CONFIG_KEYS = ("role", "bits", "group", "mode", "over_token", "w_sink", "w_recent", "flush",
+                    "normalize")
+
+    def state_dict(self) -> dict:
+        """This side's content as host tensors and plain values: the config it
+        was built with, the sink, the packed tiles and scales / zero points
+        actually in use (not the spare capacity), the normalisation factor and
+        the recent window.  The tiles keep their on-device layout (the packed
+        format of ``csrc/common.cuh``), so a restored side continues bit for
+        bit where this one stopped."""
+        if self._g0 is not None:
+            raise RuntimeError("cannot serialise a store in graph mode (call graph_end first)")
+        d = {k: getattr(self, k) for k in self._CONFIG_KEYS}
+        d["initialized"] = self.dtype is not None
+        if not d["initialized"]:
+            return d
+        d["dtype"] = str(self.dtype).replace("torch.", "")
+        d["shape"] = (self.B, self.H, self.D)
+        d["n_q"] = self.n_q
+        d["sink"] = None if self.sink is None else self.sink.cpu()
+        d["recent"] = self.recent.cpu() if self._rbuf is not None else None
+        d["norm_f"] = None if self.norm_f is None else self.norm_f.cpu()
+        d["codes"] = d["scale"] = d["zero"] = None
+        if self.quantize and self.n_q:
+            nt = (self.n_q + 31) // 32
+            ns = (self.n_q // self.group) if self.over_token else nt * 32
+            d["codes"] = self.codes[:, :, :nt].cpu()
+            d["scale"] = self.scale[:, :, :ns].cpu()
+            d["zero"] = None if self.zero is None else self.zero[:, :, :ns].cpu()
+        return d
+
+    def load_state_dict(self, d: dict, device) -> None:
+        """Restore a side written by state_dict() onto `device` (a CUDA
+        device; None: the current one).  The config must match the one this
+        side was built with."""
+        for k in self._CONFIG_KEYS:
+            if d.get(k) != getattr(self, k):
+                raise ValueError(f"saved cache store has {k}={d.get(k)!r}, this layer {getattr(self, k)!r}")
+        self.codes = self.scale = self.zero = None
+        self.cap_tiles = self.n_q = 0
+        self._rbuf, self._r0, self._rn = None, 0, 0
+        self.norm_f = None
+        if not d["initialized"]:
+            self.dtype = self.device = self.sink = None
+            return
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError("innerq_b200 stores live on a CUDA device: it has no CPU path")
+        self.dtype = getattr(torch, d["dtype"])
+        dtype_code(self.dtype)
+        self.device = device
+        self.B, self.H, self.D = d["shape"]
+        self._check_supported()
+        self.sink = None if d["sink"] is None else d["sink"].to(device=device, dtype=self.dtype).contiguous()
+        if d["norm_f"] is not None:
+            self.norm_f = d["norm_f"].to(device).contiguous()
+        n_q = int(d["n_q"])
+        if self.quantize and n_q:
+            self._alloc_store(n_q + self.headroom)
+            nt, ns = d["codes"].shape[2], d["scale"].shape[2]
+            self.codes[:, :, :nt].copy_(d["codes"])
+            self.scale[:, :, :ns].copy_(d["scale"])
+            if self.zero is not None:
+                self.zero[:, :, :ns].copy_(d["zero"])
+        self.n_q = n_q
+        if d["recent"] is not None:
+            self._push_recent(d["recent"].to(device))
+
     # ---------------------------------------------------------- graph mode
     def graph_begin(self, max_steps: int):
         """Prepare for up to `max_steps` decode steps replayed from a CUDA
@@ -467,6 +536,25 @@ class HybridSide(PackedSide):
 
     def mask(self):
         return torch.cat(self.masks, dim=2) if self.masks else None
+
+    def state_dict(self) -> dict:
+        """The symmetric set (PackedSide.state_dict), the asymmetric set and
+        the per-group masks."""
+        d = super().state_dict()
+        d["zp"] = self.zp.state_dict()
+        m = self.mask()
+        d["mask"] = None if m is None else m.cpu()
+        return d
+
+    def load_state_dict(self, d: dict, device) -> None:
+        super().load_state_dict(d, device)
+        self.zp.load_state_dict(d["zp"], device)
+        self.masks, self.mask_bits = [], None
+        if d["mask"] is not None:
+            m = d["mask"].to(self.device)
+            self.masks = [m]
+            if self.over_token:
+                self._store_mask_bits(m, 0)
 
     def materialize(self) -> torch.Tensor:
         out = super().materialize()

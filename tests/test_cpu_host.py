@@ -174,3 +174,35 @@ def test_reference_import_names_resolve_to_this_package():
     assert innerq.cache is innerq_b200.cache
     assert innerq.models.llama_innerq is innerq_b200.models.llama_innerq
     assert innerq.quant.QMode is innerq_b200.quant.QMode
+
+
+def test_cache_state_format_without_gpu():
+    """An empty cache serialises to plain values (no tensors yet) and loads
+    back; a state of another format or layer count is refused."""
+    import io
+
+    import torch
+
+    from innerq_b200.cache import DynamicCache
+
+    class Cfg:
+        num_hidden_layers = 3
+        k_bits, v_bits = 3, 3
+
+        def get_text_config(self, decoder=True):
+            return self
+
+    c = DynamicCache(config=Cfg())
+    sd = c.state_dict()
+    assert sd["format"] == "innerq_b200.DynamicCache" and len(sd["layers"]) == 3
+    assert not sd["layers"][0]["k"]["initialized"]
+    buf = io.BytesIO()
+    torch.save(sd, buf)
+    buf.seek(0)
+    c2 = DynamicCache(config=Cfg())
+    c2.load_state_dict(torch.load(buf, weights_only=True))
+    assert c2.get_seq_length() == 0
+    with pytest.raises(ValueError):
+        c2.load_state_dict(dict(sd, format="other"))
+    with pytest.raises(ValueError):
+        c2.load_state_dict(dict(sd, layers=sd["layers"][:2]))
