@@ -17,10 +17,15 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "innerq_internal.h"
 
 namespace innerq {
+
+// warps of one split-merge CTA (splits are dealt to them)
+constexpr int kMergeMaxWarps = 16;
 
 template <int BITS>
 __device__ __forceinline__ int qmax_sym() { return (1 << (BITS - 1)) - 1; }
@@ -961,79 +966,80 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ codes, const uint16_t
 // --------------------------------------------------------------------------
 // Split-KV log-sum-exp merge: out = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s
 // --------------------------------------------------------------------------
-template <int DT>
-__global__ void __launch_bounds__(kD) lse_merge_kernel(const float* __restrict__ po, const float* __restrict__ pm,
-                                                       const float* __restrict__ pl, int n_splits, int rows_per_b,
-                                                       int n_ranks, int64_t rank_stride,
-                                                       uint16_t* __restrict__ out, int64_t o_b, int64_t o_h,
-                                                       float* __restrict__ lse_out) {
-  // n_ranks blocks of partials, rank_stride floats apart (one block per rank
-  // of a context-sharded layer, gathered; 1 block otherwise), each with
-  // n_splits partials per row.  The split maxima and sums of the row are read
-  // by all threads at once (in chunks of kChunk), their weights 2^(m - M)
-  // kept in shared memory, then each thread (one dim) sums its column with
-  // its loads in flight together.
-  constexpr int kChunk = 1024;
-  __shared__ float w_s[kChunk];
-  __shared__ float red_s[kD / 32];
+template <int DT, int VEC>
+__global__ void __launch_bounds__(kMergeMaxWarps * 32)
+lse_merge_kernel(const float* __restrict__ po, const float* __restrict__ pm, const float* __restrict__ pl,
+                 int n_splits, int rows_per_b, int n_ranks, int64_t rank_stride, uint16_t* __restrict__ out,
+                 int64_t o_b, int64_t o_h, float* __restrict__ lse_out) {
+  // One CTA per output row; n_ranks blocks of partials, rank_stride floats
+  // apart (one block per rank of a context-sharded layer, gathered; 1 block
+  // otherwise), each with n_splits partials per row.  The splits are dealt
+  // to the CTA's warps (warp w takes splits w, w + nw, ...), a lane holds 4
+  // dims, so a warp reads one split's 128-dim row per (16-byte) load and the
+  // CTA has nw of them in flight; the warps' sums meet in shared memory.
+  __shared__ float4 acc_s[kMergeMaxWarps][32];
+  __shared__ float den_s[kMergeMaxWarps], max_s[kMergeMaxWarps];
   griddep_wait();  // the attention grid's partials are complete and visible
   griddep_launch_dependents();
-  const int row = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int total = n_ranks * n_splits;
-  auto part = [&](const float* base, int j) -> const float* {  // split j = (rank, split)
-    const int w = j / n_splits, s = j - w * n_splits;
-    return base + w * rank_stride + (int64_t)row * n_splits + s;
+  // split j = (rank w, split sp): offset of its (m, l) entry; its o row
+  // starts at w * rank_stride + (row * n_splits + sp) * kD
+  auto at = [&](int j) -> int64_t {
+    const int w = j / n_splits, sp = j - w * n_splits;
+    return w * rank_stride + (int64_t)row * n_splits + sp;
   };
-  auto block_max = [&](float v) {
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) red_s[warp] = v;
-    __syncthreads();
-    v = fmaxf(fmaxf(red_s[0], red_s[1]), fmaxf(red_s[2], red_s[3]));
-    __syncthreads();
-    return v;
+  auto at_o = [&](int j) -> int64_t {
+    const int w = j / n_splits, sp = j - w * n_splits;
+    return w * rank_stride + ((int64_t)row * n_splits + sp) * kD;
   };
-  auto block_sum = [&](float v) {
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red_s[warp] = v;
-    __syncthreads();
-    v = (red_s[0] + red_s[1]) + (red_s[2] + red_s[3]);
-    __syncthreads();
-    return v;
-  };
+  // the row's largest split maximum
   float M = -INFINITY;
-  for (int j = d; j < total; j += kD) M = fmaxf(M, *part(pm, j));
-  M = block_max(M);
-  float num = 0.f, den = 0.f;
+  for (int j = threadIdx.x; j < total; j += blockDim.x) M = fmaxf(M, pm[at(j)]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) max_s[warp] = M;
+  __syncthreads();
+  M = max_s[0];
+  for (int w = 1; w < nw; ++w) M = fmaxf(M, max_s[w]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
   if (M != -INFINITY) {
-    for (int c0 = 0; c0 < total; c0 += kChunk) {
-      const int cn = min(kChunk, total - c0);
-      float dl = 0.f;
-      for (int j = d; j < cn; j += kD) {
-        const float m = *part(pm, c0 + j);
-        // an empty split contributes nothing
-        const float wt = m == -INFINITY ? 0.f : exp2f(m - M);
-        w_s[j] = wt;
-        dl += wt * *part(pl, c0 + j);
+#pragma unroll 4
+    for (int j = warp; j < total; j += nw) {
+      const int64_t r = at(j);
+      const float m = pm[r];
+      // an empty split contributes nothing
+      const float wt = m == -INFINITY ? 0.f : exp2f(m - M);
+      den += wt * pl[r];
+      const float* src = po + at_o(j);
+      float4 v;
+      if constexpr (VEC) {
+        v = *reinterpret_cast<const float4*>(src + 4 * lane);
+      } else {
+        v = make_float4(src[4 * lane], src[4 * lane + 1], src[4 * lane + 2], src[4 * lane + 3]);
       }
-      den += block_sum(dl);  // (its barrier also publishes w_s)
-      int w = c0 / n_splits, sp = c0 - w * n_splits;
-      const float* op = po + w * rank_stride + ((int64_t)row * n_splits + sp) * kD + d;
-#pragma unroll 8
-      for (int j = 0; j < cn; ++j) {
-        num += w_s[j] * *op;
-        op += kD;
-        if (++sp == n_splits) {  // next rank's block
-          sp = 0;
-          ++w;
-          op = po + w * rank_stride + (int64_t)row * n_splits * kD + d;
-        }
-      }
-      __syncthreads();
+      acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
     }
   }
+  acc_s[warp][lane] = acc;
+  if (lane == 0) den_s[warp] = den;
+  __syncthreads();
+  if (warp != 0) return;
+  float4 num = acc_s[0][lane];
+  float dsum = den_s[0];
+  for (int w = 1; w < nw; ++w) {
+    const float4 t = acc_s[w][lane];
+    num.x += t.x; num.y += t.y; num.z += t.z; num.w += t.w;
+    dsum += den_s[w];
+  }
   const int b = row / rows_per_b, h = row % rows_per_b;
-  out[b * o_b + h * o_h + d] = from_f<DT>(den > 0.f ? num / den : 0.f);
-  if (lse_out && d == 0) lse_out[row] = den > 0.f ? M + log2f(den) : -INFINITY;
+  uint16_t* o = out + b * o_b + h * o_h + 4 * lane;
+  o[0] = from_f<DT>(dsum > 0.f ? num.x / dsum : 0.f);
+  o[1] = from_f<DT>(dsum > 0.f ? num.y / dsum : 0.f);
+  o[2] = from_f<DT>(dsum > 0.f ? num.z / dsum : 0.f);
+  o[3] = from_f<DT>(dsum > 0.f ? num.w / dsum : 0.f);
+  if (lse_out && lane == 0) lse_out[row] = dsum > 0.f ? M + log2f(dsum) : -INFINITY;
 }
 
 
@@ -1221,8 +1227,16 @@ cudaError_t launch_lse_merge(const float* po, const float* pm, const float* pl, 
                              int64_t rank_stride) {
   if (rows == 0) return cudaSuccess;
   cudaError_t e = cudaSuccess;
-  DT_DISPATCH(dt, e = launch_pdl(lse_merge_kernel<DTC>, dim3(rows), dim3(kD), 0, s, po, pm, pl, n_splits,
-                                 rows_per_b, n_ranks, rank_stride, (uint16_t*)out, o_b, o_h, lse));
+  // one warp per split up to kMergeMaxWarps; 16-byte loads when aligned
+  const int nw = (int)std::min<int64_t>(kMergeMaxWarps, std::max<int64_t>(1, (int64_t)n_splits * n_ranks));
+  const bool vec = (uintptr_t)po % 16 == 0 && (n_ranks == 1 || rank_stride % 4 == 0);
+  if (vec) {
+    DT_DISPATCH(dt, e = launch_pdl(lse_merge_kernel<DTC, 1>, dim3(rows), dim3(32 * nw), 0, s, po, pm, pl,
+                                   n_splits, rows_per_b, n_ranks, rank_stride, (uint16_t*)out, o_b, o_h, lse));
+  } else {
+    DT_DISPATCH(dt, e = launch_pdl(lse_merge_kernel<DTC, 0>, dim3(rows), dim3(32 * nw), 0, s, po, pm, pl,
+                                   n_splits, rows_per_b, n_ranks, rank_stride, (uint16_t*)out, o_b, o_h, lse));
+  }
   return e;
 }
 
