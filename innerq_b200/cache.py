@@ -46,6 +46,8 @@ class InnerqDynamicLayer(CacheLayerMixin):
         self.fused = bool(getattr(config, "_attn_implementation", None) == "innerq")
         self._attn = None
         self._gstep = None  # graph mode: the cache's device step counter
+        hq, hkv = getattr(config, "num_attention_heads", None), getattr(config, "num_key_value_heads", None)
+        self._gqa = hq // hkv if isinstance(hq, int) and isinstance(hkv, int) and hkv > 0 else None
         super().__init__()
 
     # cache.py:70-119
@@ -215,6 +217,8 @@ class InnerqDynamicLayer(CacheLayerMixin):
             raise NotImplementedError("graph mode needs a prefilled layer on the fused attention path")
         if isinstance(self._k, HybridSide) or isinstance(self._v, HybridSide):
             raise NotImplementedError("graph mode does not cover hybrid stores")
+        if self._k.quantize and self._k.over_token:
+            raise NotImplementedError("graph mode does not cover keys grouped over tokens")
         self._k.graph_begin(max_steps)
         self._v.graph_begin(max_steps)
         self._gstep = step
@@ -231,6 +235,16 @@ class InnerqDynamicLayer(CacheLayerMixin):
         k, v = self._k, self._v
         if not (k.fusable and v.fusable):
             return False
+        if k.quantize and k.over_token:
+            # keys grouped over tokens (KIVI): GQA <= 4, the values' sink
+            # size, non-hybrid values, channel-grouped values in groups of 32
+            if self._gqa is not None and self._gqa > 4:
+                return False
+            if isinstance(k, HybridSide) or isinstance(v, HybridSide):
+                return False
+            if v.quantize and k.w_sink != v.w_sink:
+                return False
+            return not (v.quantize and not v.over_token and v.group != 32)
         return not (v.quantize and not v.over_token and k.quantize and v.group != k.group)
 
     def attend(self, query: torch.Tensor, scaling: float | None = None,

@@ -79,9 +79,8 @@ int check_side(const innerq_side& s, int dtype, int role, const char* name) {
       if ((int64_t)s.n_q > s.cap_tiles2 * 32) return fail(INNERQ_ERR_ARG, "%s: n_q beyond the asymmetric store", name);
     }
     if (s.bits < 2) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: %s bits %d (2, 3, 4)", name, s.bits);
-    // the fused kernel reads the InnerQ layouts (cache.py:87-88 defaults)
-    if (role == INNERQ_ROLE_K && s.over_token)
-      return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens (use innerq_dequant)");
+    // keys grouped over tokens (the KIVI layout) are read too; make_plan
+    // checks the rest of their conditions
     if (!s.codes || !s.scale || (s.mode == INNERQ_ASYM && !s.zero))
       return fail(INNERQ_ERR_ARG, "%s: missing store pointer", name);
     if (!aligned(s.codes, 16) || !aligned(s.scale, 16) || (s.zero && !aligned(s.zero, 16)))
@@ -137,8 +136,23 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
     if (packed(a->k) && a->k.group != 32)
       return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: hybrid values need keys in groups of 32 (use innerq_dequant)");
   }
+  // keys grouped over tokens (KIVI, cache.py:87): the query is scaled per
+  // token group inside the kernel; built for GQA <= 4, eager launches,
+  // unnormalised keys, the values' sink size, non-hybrid values
+  if (packed(a->k) && a->k.over_token) {
+    if (p.R > 4) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens need GQA <= 4");
+    if (a->step) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens in graph mode");
+    if (a->key_norm) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: normalised keys grouped over tokens");
+    if (a->k.n_sink != a->v.n_sink)
+      return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens need the values' sink size");
+    if (packed(a->v) && a->v.mode == INNERQ_HYBRID)
+      return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens with hybrid values");
+    if (packed(a->v) && !a->v.over_token && a->v.group != 32)
+      return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens with values in channel groups of %d (32 is built)", a->v.group);
+    if (a->k.n_q % 32) return fail(INNERQ_ERR_ARG, "k: n_q %% 32");
+  }
   // values grouped over channels share the keys' channel-group count
-  if (packed(a->v) && !a->v.over_token && packed(a->k) && a->v.group != a->k.group)
+  if (packed(a->v) && !a->v.over_token && packed(a->k) && !a->k.over_token && a->v.group != a->k.group)
     return fail(INNERQ_ERR_UNSUPPORTED,
                 "fused attention: channel-grouped values need the keys' group size (%d vs %d; use innerq_dequant)",
                 a->v.group, a->k.group);
@@ -205,6 +219,7 @@ DevSide dev_side(const innerq_side& s) {
   d.zero2 = (const uint16_t*)s.zero2;
   d.mask = (const uint16_t*)s.mask;
   d.cap_tiles2 = s.cap_tiles2;
+  d.otok = packed(s) && s.over_token;
   return d;
 }
 
@@ -240,7 +255,8 @@ int run_partials(const innerq_attn_args* a, const Plan& p, float* po, float* pm,
   d.R = p.R;
   dim3 grid(p.n_splits, a->Hkv, a->B);
   const int rp = p.R <= 4 ? 4 : 8;
-  const int ng = packed(a->k) ? kD / a->k.group : (d.v.chan ? kD / a->v.group : 4);
+  // keys grouped over tokens: the 4-group staging geometry (4 tiles' scales per stage)
+  const int ng = packed(a->k) && !a->k.over_token ? kD / a->k.group : (d.v.chan && !packed(a->k) ? kD / a->v.group : 4);
   const bool bf = a->dtype == INNERQ_DT_BF16;
   cudaError_t e = launch_qprep(d, rp, ng, bf, st);
   if (e != cudaSuccess) return cuda_status(e, "qprep");

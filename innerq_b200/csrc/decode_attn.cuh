@@ -70,6 +70,7 @@ struct DevSide {
   const uint16_t* zero2;
   const uint16_t* mask;
   int64_t cap_tiles2;
+  int otok;  // keys grouped over tokens (scales per (token group, dim))
 };
 
 // A side's geometry after n decode steps of graph mode: each step appends one
@@ -445,6 +446,114 @@ __device__ __forceinline__ void k_packed_logits(const KRow<BK> rw[4], const floa
   }
 }
 
+// Logits (q . k) of the lane's 4 token rows for its head (lane tq) from a
+// packed K tile whose scales / zero points run per (token group, dim), the
+// KIVI layout (cache.py:87, quant.py:58-93): k = s_d u + z_d (asymmetric) or
+// s_d (u - off) (symmetric), so q . k = sum_d (q_d s_d) u + sum_d q_d z_d.
+// The scaled query q_d s_d changes with the tile's group, so its integer
+// digits are built here, per tile: each lane makes the B-fragment bytes of
+// head gid/2 for its 32 dims (kb*32 + 4tq + i, kb*32 + 16 + 4tq + i), scaled
+// by 2^e so the group's largest |q_d s_d| fits QB bits; with codes below
+// 2^BK the 128-dim integer sum stays exact in int32 (QB = 24 - BK).
+// sp / zp: the group's 128 scales / zero points (natural dim order), qk: the
+// pair's query in fp32, [4 heads][128].  Rows j = 2m, 2m+1 as one float pair.
+template <int BK, int DT, bool KASYM>
+__device__ __forceinline__ void k_tok_logits(const KRow<BK> rw[4], const uint16_t* sp, const uint16_t* zp,
+                                             const float (*qk)[kD], int lane, float2 lp[2]) {
+  constexpr int QB = 24 - BK;
+  const int gid = lane >> 2, tq = lane & 3, hb = gid >> 1, plane = gid & 1;
+  float qs[4][8];
+  float mx = 0.f, zs = 0.f;
+#pragma unroll
+  for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int d = kb * 32 + hf * 16 + 4 * tq;
+      const float4 q4 = *reinterpret_cast<const float4*>(&qk[hb][d]);
+      const uint2 s2 = *reinterpret_cast<const uint2*>(sp + d);
+      const float2 sa = pair_to_f2<DT>(s2.x), sb = pair_to_f2<DT>(s2.y);
+      const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, sv[4] = {sa.x, sa.y, sb.x, sb.y};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        qs[kb][hf * 4 + i] = qv[i] * sv[i];
+        mx = fmaxf(mx, fabsf(qs[kb][hf * 4 + i]));
+      }
+      if constexpr (KASYM) {
+        const uint2 z2 = *reinterpret_cast<const uint2*>(zp + d);
+        const float2 za = pair_to_f2<DT>(z2.x), zb = pair_to_f2<DT>(z2.y);
+        zs = fmaf(qv[0], za.x, fmaf(qv[1], za.y, fmaf(qv[2], zb.x, fmaf(qv[3], zb.y, zs))));
+      }
+    }
+  // the head's largest |q s| and sums over its 128 dims: the 4 lanes tq of a gid
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  int e = 0;
+  if (mx > 0.f) {
+    int ex;
+    frexpf(mx, &ex);
+    e = QB - ex;
+  }
+  const float mul = ldexpf(1.f, e);
+  int qsum = 0;
+  uint32_t bA[4][2], bB[4][2];  // n-tile 0: d2 / d1 of head hb; n-tile 1: d0 of head hb / 0
+#pragma unroll
+  for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      int dA[4], dB[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int v = __float2int_rn(qs[kb][hf * 4 + i] * mul);
+        qsum += v;
+        int d0, d1, d2;
+        digits3(v, d0, d1, d2);
+        dA[i] = plane ? d1 : d2;
+        dB[i] = plane ? 0 : d0;
+      }
+      bA[kb][hf] = __byte_perm(__byte_perm(dA[0], dA[1], 0x0040), __byte_perm(dA[2], dA[3], 0x0040), 0x5410);
+      bB[kb][hf] = __byte_perm(__byte_perm(dB[0], dB[1], 0x0040), __byte_perm(dB[2], dB[3], 0x0040), 0x5410);
+    }
+  qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+  qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+  if constexpr (KASYM) {
+    zs += __shfl_xor_sync(0xffffffffu, zs, 1);
+    zs += __shfl_xor_sync(0xffffffffu, zs, 2);
+  }
+  int acc[2][2][4];  // [mt][n-tile][c]
+#pragma unroll
+  for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const uint32_t af[4] = {row_frag<BK>(rw[2 * mt].w, kb, 0), row_frag<BK>(rw[2 * mt + 1].w, kb, 0),
+                              row_frag<BK>(rw[2 * mt].w, kb, 1), row_frag<BK>(rw[2 * mt + 1].w, kb, 1)};
+      if (kb == 0) {
+        imma_u8s8(acc[mt][0], af, bA[kb], 0, 0, 0, 0);
+        imma_u8s8(acc[mt][1], af, bB[kb], 0, 0, 0, 0);
+      } else {
+        imma_u8s8(acc[mt][0], af, bA[kb], acc[mt][0][0], acc[mt][0][1], acc[mt][0][2], acc[mt][0][3]);
+        imma_u8s8(acc[mt][1], af, bB[kb], acc[mt][1][0], acc[mt][1][1], acc[mt][1][2], acc[mt][1][3]);
+      }
+    }
+  // this lane's accumulator columns belong to head tq, whose scaling, integer
+  // sum and zero term the lanes gid = 2tq computed
+  const int src = 8 * tq;
+  const float inv = ldexpf(1.f, -__shfl_sync(0xffffffffu, e, src));
+  // symmetric: sum_d qi (u - off), exact in int32 (|.| < 128 * 2^(BK-1) * 2^QB)
+  const int corr = KASYM ? 0 : (1 << (BK - 1)) * __shfl_sync(0xffffffffu, qsum, src);
+  const float zt = KASYM ? __shfl_sync(0xffffffffu, zs, src) : 0.f;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    float tf[2];
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint32_t t = (uint32_t)acc[mt][0][2 * rr] * 65536u + (uint32_t)acc[mt][0][2 * rr + 1] * 256u +
+                         (uint32_t)acc[mt][1][2 * rr];
+      tf[rr] = fmaf((float)((int)t - corr), inv, zt);
+    }
+    lp[mt] = make_float2(tf[0], tf[1]);
+  }
+}
+
 // O[nt][mt][h] += fv * (s * (sum_t u p - off * sum_t p) [+ z * sum_t p]) for one
 // packed V tile (integer MMA, probabilities as two u8 digits)
 template <int BV, int NT, bool VASYM>
@@ -547,15 +656,18 @@ __device__ __forceinline__ void load_kscales(float2 out[2][NG], const uint16_t* 
 // over tokens; GM: graph mode (geometry from the device step counter; a
 // separate instantiation, because carrying that path costs the argument-fed
 // kernel ~10% through register allocation)
-template <int BK, int BV, int RP, int DT, int NG, int VCH, int GM, int VHY = 0>
+template <int BK, int BV, int RP, int DT, int NG, int VCH, int GM, int VHY = 0, int KOT = 0>
 __global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 4)
 decode_attn_kernel(const DevArgs a) {
+  static_assert(!KOT || (RP == 4 && NG == 4 && !GM && !VHY), "keys over tokens: GQA <= 4, eager, non-hybrid");
   constexpr int NT = RP / 4;
   constexpr int kStages = stages_for(RP);
   extern __shared__ __align__(128) uint8_t dyn[];
   __shared__ AttnStatic<RP> sm;
   // channel-grouped values: probability digits per (channel group, head)
   __shared__ __align__(16) uint8_t pdc_s[VCH ? kWarps : 1][VCH ? NG : 1][RP][2][kTile];
+  // keys grouped over tokens: the pair's query heads in fp32
+  __shared__ __align__(16) float qk_s[KOT ? RP : 1][KOT ? kD : 4];
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tq = lane & 3;
   const int R = a.R;
@@ -586,8 +698,12 @@ decode_attn_kernel(const DevArgs a) {
 
   const int64_t kbh = (int64_t)b * a.Hkv + hk;
   const uint8_t* kcodes = a.k.codes ? a.k.codes + kbh * a.k.cap_tiles * tile_bytes(BK) : nullptr;
-  const uint16_t* kscale = a.k.scale ? a.k.scale + kbh * a.k.cap_tiles * 32 * NG : nullptr;
-  const uint16_t* kzero = a.k.zero ? a.k.zero + kbh * a.k.cap_tiles * 32 * NG : nullptr;
+  // K scales: per (token, channel group) [tiles][32][NG], or (keys grouped
+  // over tokens) per (token group, dim) [groups][128]
+  const int kgs = a.k.group == 32 ? 5 : (a.k.group == 64 ? 6 : 7);
+  const int64_t ksc_pair = KOT ? ((a.k.cap_tiles * 32) >> kgs) * kD : a.k.cap_tiles * 32 * NG;
+  const uint16_t* kscale = a.k.scale ? a.k.scale + kbh * ksc_pair : nullptr;
+  const uint16_t* kzero = a.k.zero ? a.k.zero + kbh * ksc_pair : nullptr;
   const uint8_t* vcodes = a.v.codes ? a.v.codes + kbh * a.v.cap_tiles * tile_bytes(BV) : nullptr;
   // V token-group size is 32, 64 or 128: divide by shifting
   const int vgs = a.v.group == 32 ? 5 : (a.v.group == 64 ? 6 : 7);
@@ -660,14 +776,22 @@ decode_attn_kernel(const DevArgs a) {
     const int64_t g0 = (t0 - vs) >> vgs, g1 = (t0 + n_in * kTile - 1 - vs) >> vgs;
     const uint32_t nvg = (uint32_t)(g1 - g0 + 1);
     uint8_t* st = ring + slot * SBC;
-    const uint32_t kb = n_in * (TBK + 64 * NG * (1 + kasym));
+    // keys grouped over tokens: the stage's token groups' scales (256 B each)
+    const int64_t kg0 = (t0 - ks) >> kgs;
+    const uint32_t nkg = KOT ? (uint32_t)(((t0 + n_in * kTile - 1 - ks) >> kgs) - kg0 + 1) : 0u;
+    const uint32_t kb = KOT ? n_in * TBK + nkg * 256 * (1 + kasym) : n_in * (TBK + 64 * NG * (1 + kasym));
     const uint32_t vb = n_in * TBV + (VCH ? n_in * 64 * NG : nvg * 256) * (1 + vasym) +
                         (VHY ? n_in * TBV2 + nvg * (256 + 256 + 16) : 0);
     fence_proxy_async();
     mbar_arrive_tx(bar, kb + vb);
     bulk_g2s(st, kcodes + tk * TBK, n_in * TBK, bar);
-    bulk_g2s(st + o_ks, kscale + tk * 32 * NG, n_in * 64 * NG, bar);
-    if (kasym) bulk_g2s(st + o_kz, kzero + tk * 32 * NG, n_in * 64 * NG, bar);
+    if (KOT) {
+      bulk_g2s(st + o_ks, kscale + kg0 * kD, nkg * 256, bar);
+      if (kasym) bulk_g2s(st + o_kz, kzero + kg0 * kD, nkg * 256, bar);
+    } else {
+      bulk_g2s(st + o_ks, kscale + tk * 32 * NG, n_in * 64 * NG, bar);
+      if (kasym) bulk_g2s(st + o_kz, kzero + tk * 32 * NG, n_in * 64 * NG, bar);
+    }
     bulk_g2s(st + o_vc, vcodes + tv * TBV, n_in * TBV, bar);
     if (VCH) {
       bulk_g2s(st + o_vs, vscale + tv * 32 * NG, n_in * 64 * NG, bar);
@@ -717,6 +841,12 @@ decode_attn_kernel(const DevArgs a) {
     bulk_g2s(&sm.qp, src, kH, &sm.prep_bar);
     if (any_dense) bulk_g2s(&sm.qp.bd, src + kH, kDn, &sm.prep_bar);
   }
+  if constexpr (KOT) {
+    for (int i = threadIdx.x; i < RP * kD; i += kWarps * 32) {
+      const int h = i / kD, d = i % kD;
+      qk_s[h][d] = h < R ? to_f<DT>(a.q[b * a.q_b + (int64_t)(hk * R + h) * a.q_h + d]) : 0.f;
+    }
+  }
   __syncthreads();  // barrier initialisation (and graph-mode geometry) visible to every thread
   bool failed = !mbar_wait_bounded(&sm.prep_bar, 0, kWaitLimit);
   int i_done = 0;
@@ -761,20 +891,32 @@ decode_attn_kernel(const DevArgs a) {
       KRow<BK> rw[4];
       float2 sc[2][NG], zc[2][NG];
       load_krows<BK>(rw, sg + warp * TBK, lane);
-      load_kscales<DT, NG>(sc, reinterpret_cast<const uint16_t*>(sg + o_ks + warp * 64 * NG) + gid * 4 * NG);
-      if (kasym)
-        load_kscales<DT, NG>(zc, reinterpret_cast<const uint16_t*>(sg + o_kz + warp * 64 * NG) + gid * 4 * NG);
+      if constexpr (!KOT) {
+        load_kscales<DT, NG>(sc, reinterpret_cast<const uint16_t*>(sg + o_ks + warp * 64 * NG) + gid * 4 * NG);
+        if (kasym)
+          load_kscales<DT, NG>(zc, reinterpret_cast<const uint16_t*>(sg + o_kz + warp * 64 * NG) + gid * 4 * NG);
+      }
       float2 lp[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) lp[nt][0] = lp[nt][1] = make_float2(0.f, 0.f);
-      if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.qp.bk, ctf, qsf, lane, lp);
-      else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.qp.bk, ctf, qsf, lane, lp);
+      if constexpr (KOT) {
+        // the tile's token group among the groups staged with this stage
+        const int kgo = ((t0 - ks) >> kgs) - ((a.t_first + (tile - warp) * kTile - ks) >> kgs);
+        const uint16_t* sp = reinterpret_cast<const uint16_t*>(sg + o_ks) + kgo * kD;
+        const uint16_t* zp = reinterpret_cast<const uint16_t*>(sg + o_kz) + kgo * kD;
+        if (kasym) k_tok_logits<BK, DT, true>(rw, sp, zp, qk_s, lane, lp[0]);
+        else k_tok_logits<BK, DT, false>(rw, sp, zp, qk_s, lane, lp[0]);
+      } else {
+        if (kasym) k_packed_logits<BK, NT, NG, true>(rw, sc, zc, sm.qp.bk, ctf, qsf, lane, lp);
+        else k_packed_logits<BK, NT, NG, false>(rw, sc, zc, sm.qp.bk, ctf, qsf, lane, lp);
+      }
+      const float cpk = KOT ? a.scale_log2 : cp;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const bool head_ok = nt * 4 + tq < R;
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
-          const float2 xs = __fmul2_rn(lp[nt][m], f2(cp));
+          const float2 xs = __fmul2_rn(lp[nt][m], f2(cpk));
           x[nt][2 * m] = head_ok ? xs.x : -INFINITY;
           x[nt][2 * m + 1] = head_ok ? xs.y : -INFINITY;
         }
@@ -798,7 +940,18 @@ decode_attn_kernel(const DevArgs a) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) ld[nt][j] = 0.f;
       }
-      if (kp_any) {
+      if (KOT && kp_any) {
+        if constexpr (KOT) {
+          // keys grouped over tokens: the tile is wholly packed (its token
+          // groups start at the sink, which the values share)
+          KRow<BK> rw[4];
+          const int64_t ti = (t0 - ks) >> 5;
+          load_krows<BK>(rw, kcodes + ti * tile_bytes(BK), lane);
+          const int64_t g = (t0 - ks) >> kgs;
+          if (kasym) k_tok_logits<BK, DT, true>(rw, kscale + g * kD, kzero + g * kD, qk_s, lane, lp[0]);
+          else k_tok_logits<BK, DT, false>(rw, kscale + g * kD, nullptr, qk_s, lane, lp[0]);
+        }
+      } else if (kp_any) {
         KRow<BK> rw[4];
         float sc[4][NG], zc[4][NG];
 #pragma unroll
@@ -863,7 +1016,8 @@ decode_attn_kernel(const DevArgs a) {
         for (int j = 0; j < 4; ++j)
           x[nt][j] = (!head_ok || src[j] == 0)
                          ? -INFINITY
-                         : (src[j] == 1 ? (j & 1 ? lp[nt][j >> 1].y : lp[nt][j >> 1].x) * cp : ld[nt][j] * cd);
+                         : (src[j] == 1 ? (j & 1 ? lp[nt][j >> 1].y : lp[nt][j >> 1].x) * (KOT ? a.scale_log2 : cp)
+                                        : ld[nt][j] * cd);
       }
     }
 

@@ -9,9 +9,9 @@
 
 namespace innerq {
 
-template <int BK, int DT, int BV, int RP, int NG, int VCH, int GM, int VHY = 0>
+template <int BK, int DT, int BV, int RP, int NG, int VCH, int GM, int VHY = 0, int KOT = 0>
 cudaError_t attn_go(const DevArgs& a, dim3 grid, cudaStream_t s) {
-  auto kern = decode_attn_kernel<BK, BV, RP, DT, NG, VCH, GM, VHY>;
+  auto kern = decode_attn_kernel<BK, BV, RP, DT, NG, VCH, GM, VHY, KOT>;
   const int smem = attn_dyn_smem(BK, BV, NG, a.k.asym, a.v.asym, RP, VHY);
   int dev = 0;
   cudaGetDevice(&dev);
@@ -30,6 +30,13 @@ cudaError_t attn_go_ng(const DevArgs& a, int ng, dim3 grid, cudaStream_t s) {
   if (a.v.hyb) {
     if constexpr (GM == 0) {
       if (ng == 4 && !a.v.chan) return attn_go<BK, DT, BV, RP, 4, 0, 0, 1>(a, grid, s);
+    }
+    return cudaErrorNotSupported;
+  }
+  // keys grouped over tokens (KIVI): GQA <= 4, eager launches (make_plan)
+  if (a.k.otok) {
+    if constexpr (GM == 0 && RP == 4) {
+      return a.v.chan ? attn_go<BK, DT, BV, 4, 4, 1, 0, 0, 1>(a, grid, s) : attn_go<BK, DT, BV, 4, 4, 0, 0, 0, 1>(a, grid, s);
     }
     return cudaErrorNotSupported;
   }

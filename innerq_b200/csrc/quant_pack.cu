@@ -631,7 +631,9 @@ __device__ __forceinline__ void pack_col_group(const uint16_t* __restrict__ x0, 
   }
   const int64_t groups_cap = cap_tiles * 32 / group;
   const int64_t gglob = t_abs / group;
-  const int64_t si = (bh * groups_cap + gglob) * kD + col_scale_idx(d);
+  // values: the col layout's dim order; keys (grouped over tokens): natural
+  // dim order, so a lane of the attention pass reads its 4 dims as one word pair
+  const int64_t si = (bh * groups_cap + gglob) * kD + (ROLEV ? col_scale_idx(d) : d);
   scale[si] = from_f<DT>(s);
   if (asym) zero[si] = from_f<DT>(z);
   __syncthreads();
@@ -892,7 +894,7 @@ __device__ __forceinline__ int64_t scale_index(int role_v, int over_token, int g
     const int ng = kD / group;
     return (p >> 5) * 32 * ng + row_scale_idx((int)(p & 31), d / group, ng);
   }
-  return (p / group) * kD + col_scale_idx(d);
+  return (p / group) * kD + (role_v ? col_scale_idx(d) : d);  // keys: natural dim order
 }
 
 // Reference-format views (quant.py return values): int32 codes (magnitudes

@@ -93,11 +93,12 @@ class PackedSide:
     @property
     def fusable(self) -> bool:
         """The fused decode attention reads this side's layout: keys grouped
-        over channels; values over tokens (the InnerQ default) or over
-        channels with the keys' group size (checked by the layer)."""
+        over channels, or over tokens (KIVI) without key normalisation; values
+        over tokens (the InnerQ default) or over channels (group sizes checked
+        by the layer)."""
         if not self.quantize:
             return True
-        return self.role == _lib.ROLE_V or not self.over_token
+        return self.role == _lib.ROLE_V or not self.over_token or not self.normalize
 
     @property
     def n_sink(self) -> int:

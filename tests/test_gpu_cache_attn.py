@@ -69,10 +69,11 @@ def test_layer_matches_reference_fixture(cache_golden, name):
     assert layer.get_mask_sizes(1) == (kin.shape[2] + 1, 0)
 
 
-def test_kivi_layout_materialised_and_not_fused():
+def test_kivi_layout_materialised_and_fused():
     """KIVI (keys grouped over tokens, values over channels, asymmetric) runs
     through the packed store and the dequant kernel, bit-exact with the
-    reference; the fused kernel refuses token-grouped keys."""
+    reference, and the fused kernel reads it (1e-3 vs the fp32 dequantize);
+    GQA 8 and normalised token-grouped keys are refused by the fused kernel."""
     from innerq_b200.attention import decode_attention
     from innerq_b200.cache import InnerqDynamicLayer
     from innerq_b200._lib import InnerqError
@@ -86,9 +87,14 @@ def test_kivi_layout_materialised_and_not_fused():
         Kr, Vr = ol.update(to_np32(k[:, :, t:t + 1]), to_np32(v[:, :, t:t + 1]))
     np.testing.assert_array_equal(to_np32(K), Kr)
     np.testing.assert_array_equal(to_np32(V), Vr)
-    assert not layer.key_side.fusable and not layer._fusable()
+    assert layer.key_side.fusable and layer._fusable()
+    q = synth_q(1, 8)
+    K32, V32 = _oracle_kv32(ol)
+    ref32, _ = C.attention(to_np32(q), K32, V32)
+    out = decode_attention(q, layer.key_side, layer.value_side)
+    assert_close_rel(to_np32(out), ref32[:, :, 0], 1e-3, "kivi fused")
     with pytest.raises(InnerqError):
-        decode_attention(synth_q(1, 8), layer.key_side, layer.value_side)
+        decode_attention(synth_q(1, 16), layer.key_side, layer.value_side)  # GQA 8
 
 
 def _oracle_kv32(ol):
@@ -129,6 +135,23 @@ CASES_VCH = [
 ]
 
 
+# keys grouped over tokens (KIVI, cache.py:87; presets kivi / kivi_sink of
+# run_lmeval.sh): (case, values over tokens?, value flush)
+CASES_KOT = [
+    ((2, 2, "asymmetric", "asymmetric", 4, "fp16", 32, 32, 0, 128, False, 1000, 40), False, 1),
+    ((2, 2, "asymmetric", "asymmetric", 4, "fp16", 32, 32, 32, 96, False, 700, 33), False, 1),
+    ((4, 4, "symmetric", "symmetric", 2, "bf16", 64, 64, 0, 64, False, 900, 5), True, 64),
+    ((3, 3, "asymmetric", "symmetric", 1, "fp16", 128, 32, 4, 32, False, 1060, 3), True, 32),
+    ((2, 4, "symmetric", "asymmetric", 4, "fp16", 32, 32, 0, 32, False, 40, 30), False, 32),  # tiny middle
+]
+
+
+@pytest.mark.parametrize("case", CASES_KOT, ids=[f"k{i}" for i in range(len(CASES_KOT))])
+def test_decode_attention_keys_over_tokens(case):
+    c, vot, vflush = case
+    _check_case(c, value_over_token=vot, key_over_token=True, value_flush=vflush)
+
+
 @pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
 def test_decode_attention_vs_oracle(case):
     _check_case(case, value_over_token=True)
@@ -139,15 +162,17 @@ def test_decode_attention_value_channel_groups(case):
     _check_case(case, value_over_token=False)
 
 
-def _check_case(case, value_over_token):
+def _check_case(case, value_over_token, key_over_token=False, value_flush=None):
     from innerq_b200.attention import decode_attention, decode_attention_partials
     from innerq_b200.cache import InnerqDynamicLayer
     bk, bv, km, vm, R, dtype, gk, gv, sink, recent, norm, T0, steps = case
+    if value_flush is None:
+        value_flush = gv if value_over_token else 32
     kw = dict(k_bits=bk, v_bits=bv, key_quantize_mode=km, value_quantize_mode=vm,
               key_group_size=gk, value_group_size=gv, key_w_sink=sink, value_w_sink=sink,
-              key_w_recent=recent, value_w_recent=recent, key_flush_size=1,
-              value_flush_size=gv if value_over_token else 32, key_normalize=norm,
-              value_quantize_over_token=value_over_token)
+              key_w_recent=recent, value_w_recent=recent, key_flush_size=gk if key_over_token else 1,
+              value_flush_size=value_flush, key_normalize=norm,
+              value_quantize_over_token=value_over_token, key_quantize_over_token=key_over_token)
     Hkv, B = 2, 2
     k, v = synth_kv(B, Hkv, T0 + steps, dtype=dtype, seed=T0)
     layer = InnerqDynamicLayer(cfg(**kw), 0)

@@ -17,7 +17,7 @@ PRESETS = {
     "innerq_hybrid": dict(k_bits=3, v_bits=2, key_flush_size=1, value_flush_size=32, key_w_sink=32,
                           value_w_sink=32, key_w_recent=96, value_w_recent=96, key_normalize=True,
                           value_quantize_mode="hybrid"),
-    # kivi: asymmetric keys over tokens, values over channels (materialised path)
+    # kivi: asymmetric keys over tokens, values over channels
     "kivi": dict(k_bits=2, v_bits=2, key_flush_size=32, value_flush_size=1, key_w_recent=128,
                  value_w_recent=128, key_quantize_over_token=True, value_quantize_over_token=False,
                  key_quantize_mode="asymmetric", value_quantize_mode="asymmetric"),
