@@ -141,7 +141,7 @@ def layer_bytes(layer, B, Hkv, Hq, graph_steps=None):
     k, v = layer.key_side, layer.value_side
     (knq, knr), (vnq, vnr) = ((k.n_q, k.n_recent), (v.n_q, v.n_recent)) if graph_steps is None else \
         (k.state_after(graph_steps), v.state_after(graph_steps))
-    per_bh = side_bytes(knq, k.n_sink, knr, k.bits, k.group, False, k.mode == 1, k.normalize) \
+    per_bh = side_bytes(knq, k.n_sink, knr, k.bits, k.group, k.over_token, k.mode == 1, k.normalize) \
         + side_bytes(vnq, v.n_sink, vnr, v.bits, v.group, v.over_token, v.mode == 1)
     if getattr(v, "zp", None) is not None and v.over_token:
         # hybrid values: the asymmetric (bits-1)-bit set, its scales and zeros, the mask
@@ -927,6 +927,9 @@ SWEEP = [
     ("C4 (1 GPU, 4 layers)", 8, 64, 131072, 2, 32, "tokens", "symmetric"),
     # the innerq_hybrid preset (scripts/run_lmeval.sh:133-151): 3-bit K, 2-bit hybrid V
     ("C1 innerq_hybrid", 32, 32, 32768, (3, 2), 32, "tokens", "hybrid"),
+    # the kivi preset (scripts/run_lmeval.sh:54-72): 2-bit asymmetric keys
+    # grouped over tokens, 2-bit asymmetric values grouped over channels
+    ("C1 kivi", 32, 32, 32768, 2, 32, "channels", "kivi"),
 ]
 
 
@@ -957,10 +960,15 @@ def run_sweep(a):
         done.add(key)
         kb_, vb_ = bits if isinstance(bits, tuple) else (bits, bits)
         a2 = types.SimpleNamespace(kbits=kb_, vbits=vb_, group=group, v_layout=vlay,
-                                   mode="symmetric" if mode == "hybrid" else mode)
+                                   mode="symmetric" if mode in ("hybrid", "kivi") else mode)
         kw = cache_kw(a2)
         if mode == "hybrid":
             kw["value_quantize_mode"] = "hybrid"
+        if mode == "kivi":
+            kw.update(key_quantize_over_token=True, value_quantize_over_token=False,
+                      key_quantize_mode="asymmetric", value_quantize_mode="asymmetric",
+                      key_flush_size=32, value_flush_size=1, key_w_sink=0, value_w_sink=0,
+                      key_w_recent=128, value_w_recent=128, key_normalize=False)
         bits = kb_
         hkv = a.sweep_hkv or 8
         hq = hq * hkv // 8
