@@ -60,6 +60,16 @@ def test_c1_asymmetric_b32():
     _run(_bench_kw(4, 32, mode="asymmetric"), 32, 8, 32, 32768, seed=4)
 
 
+def test_c1_kivi_b32():
+    """The kivi preset (run_lmeval.sh:54-72: 2-bit asymmetric keys grouped over
+    tokens, values over channels, recent 128, no sink) at C1 B32 x 32768."""
+    kw = dict(k_bits=2, v_bits=2, key_group_size=32, value_group_size=32, key_flush_size=32,
+              value_flush_size=1, key_w_recent=128, value_w_recent=128, key_quantize_over_token=True,
+              value_quantize_over_token=False, key_quantize_mode="asymmetric",
+              value_quantize_mode="asymmetric")
+    _run(kw, 32, 8, 32, 32768, steps=40, seed=6)
+
+
 def test_c4_shape_131072():
     """C4: 70B attention shape (Hq 64 / Hkv 8, GQA 8), B 8, 131072 tokens, 2-bit K and V, G32."""
     _run(_bench_kw(2, 32), 8, 8, 64, 131072, seed=5)
