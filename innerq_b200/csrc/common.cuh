@@ -239,6 +239,31 @@ template <int DT> __device__ __forceinline__ uint32_t absmax2(uint32_t m, uint32
   return pair_bits<DT>(__hmax2(as_pair<DT>(m), __habs2(as_pair<DT>(a))));
 }
 
+// max(m, a) / min(m, a) per half, in the dtype (exact)
+template <int DT> __device__ __forceinline__ uint32_t max2(uint32_t m, uint32_t a) {
+  return pair_bits<DT>(__hmax2(as_pair<DT>(m), as_pair<DT>(a)));
+}
+template <int DT> __device__ __forceinline__ uint32_t min2(uint32_t m, uint32_t a) {
+  return pair_bits<DT>(__hmin2(as_pair<DT>(m), as_pair<DT>(a)));
+}
+
+// Asymmetric codes c = #{cuts at or below rnd_dt(a - z)} of the two elements
+// of w in bytes 0 and 2; z2: the two zero points (the group minima) as dtype
+// bits.  The packed subtraction rounds a - z once to the dtype; the
+// reference's fp32 subtraction then dtype rounding gives the same value,
+// because the difference of two dtype values is exact in fp32 unless their
+// exponents lie more than 13 (fp16; 16 for bf16) apart, and then both
+// roundings return the larger operand.
+template <int DT, int BITS>
+__device__ __forceinline__ uint32_t asym_codes2(uint32_t w, uint32_t z2, const uint32_t* cb) {
+  constexpr int QM = (1 << BITS) - 1;
+  const auto d = __hsub2(as_pair<DT>(w), as_pair<DT>(z2));
+  auto acc = as_pair<DT>(Pair<DT>::kBase);
+#pragma unroll
+  for (int k = 0; k < QM; ++k) acc = __hadd2(acc, __hge2(d, as_pair<DT>(cb[k])));
+  return pair_bits<DT>(acc);
+}
+
 // Offset-binary symmetric codes of the two elements of w in bytes 0 and 2;
 // cb[k]: the cut of code k + 1 rounded up to the dtype, for (half 0, half 1)
 template <int DT, int BITS>

@@ -379,20 +379,41 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
   const int r = (int)(p & 31), gid = r & 7, j = r >> 3;
   uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
   const int kpg = group >> 5;  // 32-dim blocks per group
-  if constexpr (!ASYM) {
-    // symmetric: the group max in the dtype (exact), codes two elements per
-    // word (sym_codes2), moved into the row-layout words by byte permutes
-    float mx;
-    {
+  if constexpr (!ASYM || BITS <= 3) {
+    // symmetric (and 2 / 3-bit asymmetric): the group max (and min) in the
+    // dtype (exact), codes two elements per word (sym_codes2 / asym_codes2),
+    // moved into the row-layout words by byte permutes
+    constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
+    float s, z = 0.f;
+    if constexpr (!ASYM) {
       uint32_t m2 = 0u;
 #pragma unroll
       for (int w = 0; w < 16; ++w) m2 = absmax2<DT>(m2, raw[w]);
-      mx = fmaxf(to_f<DT>((uint16_t)(m2 & 0xffffu)), to_f<DT>((uint16_t)(m2 >> 16)));
+      float mx = fmaxf(to_f<DT>((uint16_t)(m2 & 0xffffu)), to_f<DT>((uint16_t)(m2 >> 16)));
+      if (group >= 64) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      if (group >= 128) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      s = rnd<DT>(div_qmax<DT, QM>(mx));
+    } else {
+      uint32_t hi = raw[0], lo = raw[0];
+#pragma unroll
+      for (int w = 1; w < 16; ++w) {
+        hi = max2<DT>(hi, raw[w]);
+        lo = min2<DT>(lo, raw[w]);
+      }
+      float mx = fmaxf(to_f<DT>((uint16_t)(hi & 0xffffu)), to_f<DT>((uint16_t)(hi >> 16)));
+      float mn = fminf(to_f<DT>((uint16_t)(lo & 0xffffu)), to_f<DT>((uint16_t)(lo >> 16)));
+      if (group >= 64) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
+      }
+      if (group >= 128) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
+      }
+      s = rnd<DT>(div_qmax<DT, QM>(rnd<DT>(mx - mn)));
+      z = mn;
     }
-    if (group >= 64) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    if (group >= 128) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float s = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx));
-    constexpr int QM = (1 << (BITS - 1)) - 1;
+    const uint32_t z2 = (uint32_t)from_f<DT>(z) * 0x00010001u;
     uint32_t cb[QM];
     {
       float cut[QM];
@@ -400,9 +421,15 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
 #pragma unroll
       for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[k]) * 0x00010001u;
     }
+    auto codes2 = [&](uint32_t w) -> uint32_t {
+      if constexpr (ASYM) return asym_codes2<DT, BITS>(w, z2, cb);
+      else return sym_codes2<DT, BITS>(w, cb);
+    };
     if (valid && kb % kpg == 0) {
       const int ng = kD / group, g = kb / kpg;
-      scale[(bh * cap_tiles + ti) * 32 * ng + row_scale_idx(r, g, ng)] = from_f<DT>(s);
+      const int64_t si = (bh * cap_tiles + ti) * 32 * ng + row_scale_idx(r, g, ng);
+      scale[si] = from_f<DT>(s);
+      if (ASYM) zero[si] = from_f<DT>(z);
     }
     // word w holds elements 2w, 2w+1 = dims kb*32 + hf*16 + 4*tq + i with
     // hf = w >> 3, tq = (w >> 1) & 3, i = 2*(w & 1) + (half)
@@ -413,7 +440,7 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int w = hf * 8 + 2 * tq;
-        P[hf] = __byte_perm(sym_codes2<DT, BITS>(raw[w], cb), sym_codes2<DT, BITS>(raw[w + 1], cb), 0x6420);
+        P[hf] = __byte_perm(codes2(raw[w]), codes2(raw[w + 1]), 0x6420);
       }
       if constexpr (BITS == 4) {
         // nibble 2i + hf
@@ -689,20 +716,38 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
   auto val = [&](int t, int e) -> float {
     return to_f<DT>((uint16_t)(e ? (raw[t] >> 16) : (raw[t] & 0xffffu)));
   };
-  if constexpr (!ASYM) {
-    // symmetric: per-dim max in the dtype (exact), codes of both dims of a
-    // token word at once (sym_codes2), 4 tokens' codes gathered into the
+  if constexpr (!ASYM || BITS <= 3) {
+    // symmetric (and 2 / 3-bit asymmetric): per-dim max (and min) in the
+    // dtype (exact), codes of both dims of a token word at once
+    // (sym_codes2 / asym_codes2), 4 tokens' codes gathered into the
     // [dim][token / 4] byte words by byte permutes
-    constexpr int QM = (1 << (BITS - 1)) - 1;
-    uint32_t m2 = 0u;
+    constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
+    uint32_t hi = 0u, lo = 0u;  // asymmetric: both start at the first token's values
     for (int c0 = 0; c0 < group; c0 += 32) {
       load(c0);
+      if (ASYM && c0 == 0) hi = lo = raw[0];
 #pragma unroll
-      for (int t = 0; t < 32; ++t) m2 = absmax2<DT>(m2, raw[t]);
+      for (int t = 0; t < 32; ++t) {
+        if constexpr (ASYM) {
+          hi = max2<DT>(hi, raw[t]);
+          lo = min2<DT>(lo, raw[t]);
+        } else {
+          hi = absmax2<DT>(hi, raw[t]);
+        }
+      }
     }
-    float s[2];
-    s[0] = rnd<DT>(div_qmax<DT, QM>(to_f<DT>((uint16_t)(m2 & 0xffffu))));
-    s[1] = rnd<DT>(div_qmax<DT, QM>(to_f<DT>((uint16_t)(m2 >> 16))));
+    float s[2], z[2] = {0.f, 0.f};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float mx = to_f<DT>((uint16_t)(e ? hi >> 16 : hi & 0xffffu));
+      if constexpr (ASYM) {
+        z[e] = to_f<DT>((uint16_t)(e ? lo >> 16 : lo & 0xffffu));
+        s[e] = rnd<DT>(div_qmax<DT, QM>(rnd<DT>(mx - z[e])));
+      } else {
+        s[e] = rnd<DT>(div_qmax<DT, QM>(mx));
+      }
+    }
+    const uint32_t z2 = lo;  // the zero points (the minima) as dtype bits
     uint32_t cb[QM];
     {
       float cut[2][QM];
@@ -711,14 +756,18 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
 #pragma unroll
       for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[0][k]) | (cut_bits<DT>(cut[1][k]) << 16);
     }
+    auto codes2 = [&](uint32_t w) -> uint32_t {
+      if constexpr (ASYM) return asym_codes2<DT, BITS>(w, z2, cb);
+      else return sym_codes2<DT, BITS>(w, cb);
+    };
     for (int c0 = 0; c0 < group; c0 += 32) {
       // 3 / 4 bits: the chunk is read again (from L2) rather than kept in
       // registers across the cut computation, which would cost occupancy
       if (group > 32 || BITS > 2) load(c0);
 #pragma unroll
       for (int t4 = 0; t4 < 8; ++t4) {
-        const uint32_t f0 = sym_codes2<DT, BITS>(raw[4 * t4], cb), f1 = sym_codes2<DT, BITS>(raw[4 * t4 + 1], cb);
-        const uint32_t f2 = sym_codes2<DT, BITS>(raw[4 * t4 + 2], cb), f3 = sym_codes2<DT, BITS>(raw[4 * t4 + 3], cb);
+        const uint32_t f0 = codes2(raw[4 * t4]), f1 = codes2(raw[4 * t4 + 1]);
+        const uint32_t f2 = codes2(raw[4 * t4 + 2]), f3 = codes2(raw[4 * t4 + 3]);
         // [f0.b0, f1.b0, f0.b2, f1.b2], [f2.b0, f3.b0, f2.b2, f3.b2]
         const uint32_t p01 = __byte_perm(f0, f1, 0x6240), p23 = __byte_perm(f2, f3, 0x6240);
         cbt[2 * dp][(c0 >> 2) + t4] = __byte_perm(p01, p23, 0x5410);
@@ -729,8 +778,11 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
     const int64_t t_abs = t_off + (int64_t)gi * group;
     const int64_t gglob = t_abs / group;
 #pragma unroll
-    for (int e = 0; e < 2; ++e)
-      scale[(bh * groups_cap + gglob) * kD + col_scale_idx(2 * dp + e)] = from_f<DT>(s[e]);
+    for (int e = 0; e < 2; ++e) {
+      const int64_t si = (bh * groups_cap + gglob) * kD + col_scale_idx(2 * dp + e);
+      scale[si] = from_f<DT>(s[e]);
+      if (ASYM) zero[si] = from_f<DT>(z[e]);
+    }
     __syncthreads();
     store_col_tiles<BITS>(cbt, codes, bh, cap_tiles, t_abs, group / 32, threadIdx.x, 64);
     return;
