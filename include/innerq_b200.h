@@ -24,10 +24,13 @@
  *
  * Built: bits 2, 3, 4; group 32/64/128; symmetric or asymmetric; either
  * group axis for either role (the store, pack, unpack and dequant entry
- * points).  The fused decode attention reads the InnerQ layouts only: K with
- * channel groups and V with token groups (key_quantize_over_token=False,
- * value_quantize_over_token=True, the reference defaults, cache.py:87-88);
- * other layouts (KIVI) are materialised with innerq_dequant.
+ * points).  The fused decode attention reads K with channel groups (the
+ * reference default, cache.py:87) or with token groups (KIVI; GQA <= 4,
+ * eager launches, no key normalisation, the values' sink size) and V with
+ * token groups (cache.py:88 default), channel groups or hybrid token groups;
+ * it refuses the rest with INNERQ_ERR_UNSUPPORTED (materialise those with
+ * innerq_dequant).  Scales / zero points of token groups are [groups][D] per
+ * (batch, head): values in the col layout's dim order, keys in natural order.
  * Values grouped over channels must be appended into a zero-filled store
  * (their codes share words across tokens).
  */
@@ -135,7 +138,7 @@ typedef struct {
   int32_t bits;        /* 2, 3, 4 (ignored when n_q == 0) */
   int32_t group;
   int32_t mode;        /* INNERQ_SYM / INNERQ_ASYM */
-  int32_t over_token;  /* 0 for K (channel groups), 1 for V (token groups) */
+  int32_t over_token;  /* groups over tokens: 1 (V default; K for KIVI) or channels: 0 */
   /* Graph mode only (innerq_attn_args.step set), else 0: n_q / n_recent are
    * the counts at step 0, `recent` is the FIFO buffer base, r0 the window's
    * FIFO offset at step 0 and flush the side's flush size (0: no quantization).
