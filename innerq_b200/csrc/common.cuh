@@ -258,10 +258,24 @@ template <int DT, int BITS>
 __device__ __forceinline__ uint32_t asym_codes2(uint32_t w, uint32_t z2, const uint32_t* cb) {
   constexpr int QM = (1 << BITS) - 1;
   const auto d = __hsub2(as_pair<DT>(w), as_pair<DT>(z2));
-  auto acc = as_pair<DT>(Pair<DT>::kBase);
+  if constexpr (BITS == 4) {
+    // 15 cuts: a binary search per half, four packed compares (all-ones /
+    // all-zero masks) and per-half selects of the next cut by bit logic
+    auto ge = [&](uint32_t c) -> uint32_t { return __hge2_mask(d, as_pair<DT>(c)); };
+    auto sel = [](uint32_t m, uint32_t a, uint32_t b) -> uint32_t { return (m & a) | (~m & b); };
+    const uint32_t m3 = ge(cb[7]);
+    const uint32_t m2 = ge(sel(m3, cb[11], cb[3]));
+    const uint32_t m1 = ge(sel(m3, sel(m2, cb[13], cb[9]), sel(m2, cb[5], cb[1])));
+    const uint32_t c0 = sel(m3, sel(m2, sel(m1, cb[14], cb[12]), sel(m1, cb[10], cb[8])),
+                            sel(m2, sel(m1, cb[6], cb[4]), sel(m1, cb[2], cb[0])));
+    const uint32_t m0 = ge(c0);
+    return (m3 & 0x00080008u) | (m2 & 0x00040004u) | (m1 & 0x00020002u) | (m0 & 0x00010001u);
+  } else {
+    auto acc = as_pair<DT>(Pair<DT>::kBase);
 #pragma unroll
-  for (int k = 0; k < QM; ++k) acc = __hadd2(acc, __hge2(d, as_pair<DT>(cb[k])));
-  return pair_bits<DT>(acc);
+    for (int k = 0; k < QM; ++k) acc = __hadd2(acc, __hge2(d, as_pair<DT>(cb[k])));
+    return pair_bits<DT>(acc);
+  }
 }
 
 // Offset-binary symmetric codes of the two elements of w in bytes 0 and 2;

@@ -379,130 +379,50 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
   const int r = (int)(p & 31), gid = r & 7, j = r >> 3;
   uint8_t* tb = codes + (bh * cap_tiles + ti) * tile_bytes(BITS);
   const int kpg = group >> 5;  // 32-dim blocks per group
-  if constexpr (!ASYM || BITS <= 3) {
-    // symmetric (and 2 / 3-bit asymmetric): the group max (and min) in the
-    // dtype (exact), codes two elements per word (sym_codes2 / asym_codes2),
-    // moved into the row-layout words by byte permutes
-    constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
-    float s, z = 0.f;
-    if constexpr (!ASYM) {
-      uint32_t m2 = 0u;
-#pragma unroll
-      for (int w = 0; w < 16; ++w) m2 = absmax2<DT>(m2, raw[w]);
-      float mx = fmaxf(to_f<DT>((uint16_t)(m2 & 0xffffu)), to_f<DT>((uint16_t)(m2 >> 16)));
-      if (group >= 64) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      if (group >= 128) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      s = rnd<DT>(div_qmax<DT, QM>(mx));
-    } else {
-      uint32_t hi = raw[0], lo = raw[0];
-#pragma unroll
-      for (int w = 1; w < 16; ++w) {
-        hi = max2<DT>(hi, raw[w]);
-        lo = min2<DT>(lo, raw[w]);
-      }
-      float mx = fmaxf(to_f<DT>((uint16_t)(hi & 0xffffu)), to_f<DT>((uint16_t)(hi >> 16)));
-      float mn = fminf(to_f<DT>((uint16_t)(lo & 0xffffu)), to_f<DT>((uint16_t)(lo >> 16)));
-      if (group >= 64) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
-      }
-      if (group >= 128) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
-      }
-      s = rnd<DT>(div_qmax<DT, QM>(rnd<DT>(mx - mn)));
-      z = mn;
-    }
-    const uint32_t z2 = (uint32_t)from_f<DT>(z) * 0x00010001u;
-    uint32_t cb[QM];
-    {
-      float cut[QM];
-      group_cuts<DT, QM>(s, cut);
-#pragma unroll
-      for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[k]) * 0x00010001u;
-    }
-    auto codes2 = [&](uint32_t w) -> uint32_t {
-      if constexpr (ASYM) return asym_codes2<DT, BITS>(w, z2, cb);
-      else return sym_codes2<DT, BITS>(w, cb);
-    };
-    if (valid && kb % kpg == 0) {
-      const int ng = kD / group, g = kb / kpg;
-      const int64_t si = (bh * cap_tiles + ti) * 32 * ng + row_scale_idx(r, g, ng);
-      scale[si] = from_f<DT>(s);
-      if (ASYM) zero[si] = from_f<DT>(z);
-    }
-    // word w holds elements 2w, 2w+1 = dims kb*32 + hf*16 + 4*tq + i with
-    // hf = w >> 3, tq = (w >> 1) & 3, i = 2*(w & 1) + (half)
-#pragma unroll
-    for (int tq = 0; tq < 4; ++tq) {
-      const int lane2 = gid * 4 + tq;
-      uint32_t P[2];  // hf = 0, 1: the codes of i = 0..3 in bytes 0..3
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int w = hf * 8 + 2 * tq;
-        P[hf] = __byte_perm(codes2(raw[w]), codes2(raw[w + 1]), 0x6420);
-      }
-      if constexpr (BITS == 4) {
-        // nibble 2i + hf
-        if (valid) *reinterpret_cast<uint32_t*>(tb + j * 512 + lane2 * 16 + kb * 4) = P[0] | (P[1] << 4);
-      } else {
-        // low two bits: crumb 4i + (kb&1)*2 + hf of word kb>>1, shared with
-        // block kb^1; 3-bit: bit 2 at 8i + kb*2 + hf of plane H
-        const int sh = (kb & 1) * 4;
-        const uint32_t l0 = BITS == 3 ? P[0] & 0x03030303u : P[0];
-        const uint32_t l1 = BITS == 3 ? P[1] & 0x03030303u : P[1];
-        uint32_t w = (l0 << sh) | (l1 << (sh + 2));
-        w |= __shfl_xor_sync(0xffffffffu, w, 1);
-        if (valid && !(kb & 1))
-          *reinterpret_cast<uint32_t*>(tb + (j >> 1) * 512 + lane2 * 16 + (j & 1) * 8 + (kb >> 1) * 4) = w;
-        if constexpr (BITS == 3) {
-          uint32_t wh = (((P[0] >> 2) & 0x01010101u) << (2 * kb)) | (((P[1] >> 2) & 0x01010101u) << (2 * kb + 1));
-          wh |= __shfl_xor_sync(0xffffffffu, wh, 1);
-          wh |= __shfl_xor_sync(0xffffffffu, wh, 2);
-          if (valid && kb == 0) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = wh;
-        }
-      }
-    }
-    return;
-  }
+  // the group max (and min) in the dtype (exact), codes two elements per
+  // word (sym_codes2 / asym_codes2), moved into the row-layout words by byte
+  // permutes
+  constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
   float s, z = 0.f;
   if constexpr (!ASYM) {
-    float mx = 0.f;
+    uint32_t m2 = 0u;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fabsf(val(e)));
+    for (int w = 0; w < 16; ++w) m2 = absmax2<DT>(m2, raw[w]);
+    float mx = fmaxf(to_f<DT>((uint16_t)(m2 & 0xffffu)), to_f<DT>((uint16_t)(m2 >> 16)));
     if (group >= 64) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     if (group >= 128) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    s = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx));
+    s = rnd<DT>(div_qmax<DT, QM>(mx));
   } else {
-    float mn = INFINITY, mx = -INFINITY;
+    uint32_t hi = raw[0], lo = raw[0];
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      mn = fminf(mn, val(e));
-      mx = fmaxf(mx, val(e));
+    for (int w = 1; w < 16; ++w) {
+      hi = max2<DT>(hi, raw[w]);
+      lo = min2<DT>(lo, raw[w]);
     }
+    float mx = fmaxf(to_f<DT>((uint16_t)(hi & 0xffffu)), to_f<DT>((uint16_t)(hi >> 16)));
+    float mn = fminf(to_f<DT>((uint16_t)(lo & 0xffffu)), to_f<DT>((uint16_t)(lo >> 16)));
     if (group >= 64) {
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
     }
     if (group >= 128) {
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
     }
-    s = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx - mn)));
+    s = rnd<DT>(div_qmax<DT, QM>(rnd<DT>(mx - mn)));
     z = mn;
   }
-  constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
-  float cut[QM];
-  group_cuts<DT, QM>(s, cut);
-  // offset-binary code of element e (dim kb*32 + e, e = half*16 + 4*tq + i)
-  auto code = [&](int e) -> uint32_t {
-    const float v = val(e);
-    if constexpr (!ASYM) {
-      const int c = code_by_cuts<QM>(fabsf(v), cut);
-      return (uint32_t)((v < 0.f ? -c : c) + (1 << (BITS - 1)));
-    } else {
-      return (uint32_t)code_by_cuts<QM>(rnd<DT>(v - z), cut);
-    }
+  const uint32_t z2 = (uint32_t)from_f<DT>(z) * 0x00010001u;
+  uint32_t cb[QM];
+  {
+    float cut[QM];
+    group_cuts<DT, QM>(s, cut);
+#pragma unroll
+    for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[k]) * 0x00010001u;
+  }
+  auto codes2 = [&](uint32_t w) -> uint32_t {
+    if constexpr (ASYM) return asym_codes2<DT, BITS>(w, z2, cb);
+    else return sym_codes2<DT, BITS>(w, cb);
   };
   if (valid && kb % kpg == 0) {
     const int ng = kD / group, g = kb / kpg;
@@ -510,34 +430,32 @@ pack_rows_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
     scale[si] = from_f<DT>(s);
     if (ASYM) zero[si] = from_f<DT>(z);
   }
-  // row layout words (see common.cuh) for each tq: the 8 codes i = 0..3,
-  // half = 0..1 at dims kb*32 + half*16 + 4*tq + i
+  // word w holds elements 2w, 2w+1 = dims kb*32 + hf*16 + 4*tq + i with
+  // hf = w >> 3, tq = (w >> 1) & 3, i = 2*(w & 1) + (half)
 #pragma unroll
   for (int tq = 0; tq < 4; ++tq) {
     const int lane2 = gid * 4 + tq;
+    uint32_t P[2];  // hf = 0, 1: the codes of i = 0..3 in bytes 0..3
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int w = hf * 8 + 2 * tq;
+      P[hf] = __byte_perm(codes2(raw[w]), codes2(raw[w + 1]), 0x6420);
+    }
     if constexpr (BITS == 4) {
-      uint32_t w = 0u;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) w |= code(hf * 16 + 4 * tq + i) << (4 * (2 * i + hf));
-      if (valid) *reinterpret_cast<uint32_t*>(tb + j * 512 + lane2 * 16 + kb * 4) = w;
+      // nibble 2i + hf
+      if (valid) *reinterpret_cast<uint32_t*>(tb + j * 512 + lane2 * 16 + kb * 4) = P[0] | (P[1] << 4);
     } else {
-      // low two bits: word kb>>1 of the row's 8 bytes, crumb 4i + (kb&1)*2 + half,
-      // shared with the neighbouring block kb^1
-      uint32_t w = 0u, wh = 0u;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const uint32_t c = code(hf * 16 + 4 * tq + i);
-          w |= (c & 3u) << (2 * (4 * i + (kb & 1) * 2 + hf));
-          if (BITS == 3) wh |= ((c >> 2) & 1u) << (8 * i + kb * 2 + hf);
-        }
+      // low two bits: crumb 4i + (kb&1)*2 + hf of word kb>>1, shared with
+      // block kb^1; 3-bit: bit 2 at 8i + kb*2 + hf of plane H
+      const int sh = (kb & 1) * 4;
+      const uint32_t l0 = BITS == 3 ? P[0] & 0x03030303u : P[0];
+      const uint32_t l1 = BITS == 3 ? P[1] & 0x03030303u : P[1];
+      uint32_t w = (l0 << sh) | (l1 << (sh + 2));
       w |= __shfl_xor_sync(0xffffffffu, w, 1);
       if (valid && !(kb & 1))
         *reinterpret_cast<uint32_t*>(tb + (j >> 1) * 512 + lane2 * 16 + (j & 1) * 8 + (kb >> 1) * 4) = w;
       if constexpr (BITS == 3) {
+        uint32_t wh = (((P[0] >> 2) & 0x01010101u) << (2 * kb)) | (((P[1] >> 2) & 0x01010101u) << (2 * kb + 1));
         wh |= __shfl_xor_sync(0xffffffffu, wh, 1);
         wh |= __shfl_xor_sync(0xffffffffu, wh, 2);
         if (valid && kb == 0) *reinterpret_cast<uint32_t*>(tb + 1024 + lane2 * 16 + j * 4) = wh;
@@ -713,128 +631,61 @@ pack_cols_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, int64_t
 #pragma unroll
     for (int t = 0; t < 32; ++t) raw[t] = *reinterpret_cast<const uint32_t*>(x0 + (int64_t)(c0 + t) * st);
   };
-  auto val = [&](int t, int e) -> float {
-    return to_f<DT>((uint16_t)(e ? (raw[t] >> 16) : (raw[t] & 0xffffu)));
-  };
-  if constexpr (!ASYM || BITS <= 3) {
-    // symmetric (and 2 / 3-bit asymmetric): per-dim max (and min) in the
-    // dtype (exact), codes of both dims of a token word at once
-    // (sym_codes2 / asym_codes2), 4 tokens' codes gathered into the
-    // [dim][token / 4] byte words by byte permutes
-    constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
-    uint32_t hi = 0u, lo = 0u;  // asymmetric: both start at the first token's values
-    for (int c0 = 0; c0 < group; c0 += 32) {
-      load(c0);
-      if (ASYM && c0 == 0) hi = lo = raw[0];
-#pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        if constexpr (ASYM) {
-          hi = max2<DT>(hi, raw[t]);
-          lo = min2<DT>(lo, raw[t]);
-        } else {
-          hi = absmax2<DT>(hi, raw[t]);
-        }
-      }
-    }
-    float s[2], z[2] = {0.f, 0.f};
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float mx = to_f<DT>((uint16_t)(e ? hi >> 16 : hi & 0xffffu));
-      if constexpr (ASYM) {
-        z[e] = to_f<DT>((uint16_t)(e ? lo >> 16 : lo & 0xffffu));
-        s[e] = rnd<DT>(div_qmax<DT, QM>(rnd<DT>(mx - z[e])));
-      } else {
-        s[e] = rnd<DT>(div_qmax<DT, QM>(mx));
-      }
-    }
-    const uint32_t z2 = lo;  // the zero points (the minima) as dtype bits
-    uint32_t cb[QM];
-    {
-      float cut[2][QM];
-      group_cuts<DT, QM>(s[0], cut[0]);
-      group_cuts<DT, QM>(s[1], cut[1]);
-#pragma unroll
-      for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[0][k]) | (cut_bits<DT>(cut[1][k]) << 16);
-    }
-    auto codes2 = [&](uint32_t w) -> uint32_t {
-      if constexpr (ASYM) return asym_codes2<DT, BITS>(w, z2, cb);
-      else return sym_codes2<DT, BITS>(w, cb);
-    };
-    for (int c0 = 0; c0 < group; c0 += 32) {
-      // 3 / 4 bits: the chunk is read again (from L2) rather than kept in
-      // registers across the cut computation, which would cost occupancy
-      if (group > 32 || BITS > 2) load(c0);
-#pragma unroll
-      for (int t4 = 0; t4 < 8; ++t4) {
-        const uint32_t f0 = codes2(raw[4 * t4]), f1 = codes2(raw[4 * t4 + 1]);
-        const uint32_t f2 = codes2(raw[4 * t4 + 2]), f3 = codes2(raw[4 * t4 + 3]);
-        // [f0.b0, f1.b0, f0.b2, f1.b2], [f2.b0, f3.b0, f2.b2, f3.b2]
-        const uint32_t p01 = __byte_perm(f0, f1, 0x6240), p23 = __byte_perm(f2, f3, 0x6240);
-        cbt[2 * dp][(c0 >> 2) + t4] = __byte_perm(p01, p23, 0x5410);
-        cbt[2 * dp + 1][(c0 >> 2) + t4] = __byte_perm(p01, p23, 0x7632);
-      }
-    }
-    const int64_t groups_cap = cap_tiles * 32 / group;
-    const int64_t t_abs = t_off + (int64_t)gi * group;
-    const int64_t gglob = t_abs / group;
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int64_t si = (bh * groups_cap + gglob) * kD + col_scale_idx(2 * dp + e);
-      scale[si] = from_f<DT>(s[e]);
-      if (ASYM) zero[si] = from_f<DT>(z[e]);
-    }
-    __syncthreads();
-    store_col_tiles<BITS>(cbt, codes, bh, cap_tiles, t_abs, group / 32, threadIdx.x, 64);
-    return;
-  }
-  float mx0 = ASYM ? -INFINITY : 0.f, mx1 = mx0, mn0 = INFINITY, mn1 = INFINITY;
+  // per-dim max (and min) in the dtype (exact), codes of both dims of a
+  // token word at once
+  // (sym_codes2 / asym_codes2), 4 tokens' codes gathered into the
+  // [dim][token / 4] byte words by byte permutes
+  constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
+  uint32_t hi = 0u, lo = 0u;  // asymmetric: both start at the first token's values
   for (int c0 = 0; c0 < group; c0 += 32) {
     load(c0);
+    if (ASYM && c0 == 0) hi = lo = raw[0];
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
-      if (ASYM) {
-        mx0 = fmaxf(mx0, val(t, 0)); mx1 = fmaxf(mx1, val(t, 1));
-        mn0 = fminf(mn0, val(t, 0)); mn1 = fminf(mn1, val(t, 1));
+      if constexpr (ASYM) {
+        hi = max2<DT>(hi, raw[t]);
+        lo = min2<DT>(lo, raw[t]);
       } else {
-        mx0 = fmaxf(mx0, fabsf(val(t, 0))); mx1 = fmaxf(mx1, fabsf(val(t, 1)));
+        hi = absmax2<DT>(hi, raw[t]);
       }
     }
   }
   float s[2], z[2] = {0.f, 0.f};
-  if (ASYM) {
-    s[0] = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx0 - mn0)));
-    s[1] = rnd<DT>(div_qmax<DT, (1 << BITS) - 1>(rnd<DT>(mx1 - mn1)));
-    z[0] = mn0; z[1] = mn1;
-  } else {
-    s[0] = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx0));
-    s[1] = rnd<DT>(div_qmax<DT, (1 << (BITS - 1)) - 1>(mx1));
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float mx = to_f<DT>((uint16_t)(e ? hi >> 16 : hi & 0xffffu));
+    if constexpr (ASYM) {
+      z[e] = to_f<DT>((uint16_t)(e ? lo >> 16 : lo & 0xffffu));
+      s[e] = rnd<DT>(div_qmax<DT, QM>(rnd<DT>(mx - z[e])));
+    } else {
+      s[e] = rnd<DT>(div_qmax<DT, QM>(mx));
+    }
   }
-  constexpr int QM = ASYM ? (1 << BITS) - 1 : (1 << (BITS - 1)) - 1;
-  float cut[2][QM];
-  group_cuts<DT, QM>(s[0], cut[0]);
-  group_cuts<DT, QM>(s[1], cut[1]);
+  const uint32_t z2 = lo;  // the zero points (the minima) as dtype bits
+  uint32_t cb[QM];
+  {
+    float cut[2][QM];
+    group_cuts<DT, QM>(s[0], cut[0]);
+    group_cuts<DT, QM>(s[1], cut[1]);
+#pragma unroll
+    for (int k = 0; k < QM; ++k) cb[k] = cut_bits<DT>(cut[0][k]) | (cut_bits<DT>(cut[1][k]) << 16);
+  }
+  auto codes2 = [&](uint32_t w) -> uint32_t {
+    if constexpr (ASYM) return asym_codes2<DT, BITS>(w, z2, cb);
+    else return sym_codes2<DT, BITS>(w, cb);
+  };
   for (int c0 = 0; c0 < group; c0 += 32) {
-    if (group > 32) load(c0);
+    // 3 / 4 bits: the chunk is read again (from L2) rather than kept in
+    // registers across the cut computation, which would cost occupancy
+    if (group > 32 || BITS > 2) load(c0);
 #pragma unroll
     for (int t4 = 0; t4 < 8; ++t4) {
-      uint32_t w[2] = {0u, 0u};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float xe = val(4 * t4 + i, e);
-          uint32_t uc;
-          if (ASYM) {
-            uc = (uint32_t)code_by_cuts<QM>(rnd<DT>(xe - z[e]), cut[e]);
-          } else {
-            const int c = code_by_cuts<QM>(fabsf(xe), cut[e]);
-            uc = (uint32_t)((xe < 0.f ? -c : c) + (1 << (BITS - 1)));
-          }
-          w[e] |= uc << (8 * i);
-        }
-      }
-      cbt[2 * dp][(c0 >> 2) + t4] = w[0];
-      cbt[2 * dp + 1][(c0 >> 2) + t4] = w[1];
+      const uint32_t f0 = codes2(raw[4 * t4]), f1 = codes2(raw[4 * t4 + 1]);
+      const uint32_t f2 = codes2(raw[4 * t4 + 2]), f3 = codes2(raw[4 * t4 + 3]);
+      // [f0.b0, f1.b0, f0.b2, f1.b2], [f2.b0, f3.b0, f2.b2, f3.b2]
+      const uint32_t p01 = __byte_perm(f0, f1, 0x6240), p23 = __byte_perm(f2, f3, 0x6240);
+      cbt[2 * dp][(c0 >> 2) + t4] = __byte_perm(p01, p23, 0x5410);
+      cbt[2 * dp + 1][(c0 >> 2) + t4] = __byte_perm(p01, p23, 0x7632);
     }
   }
   const int64_t groups_cap = cap_tiles * 32 / group;
