@@ -365,7 +365,8 @@ class DynamicCache(Cache):
 
     # --------------------------------------------------------- serialisation
     FORMAT = "innerq_b200.DynamicCache"
-    FORMAT_VERSION = 1
+    # 2: scales of keys grouped over tokens in natural dim order
+    FORMAT_VERSION = 2
 
     def state_dict(self) -> dict:
         """Every layer's packed cache as host tensors and plain values (no
