@@ -217,8 +217,6 @@ class InnerqDynamicLayer(CacheLayerMixin):
             raise NotImplementedError("graph mode needs a prefilled layer on the fused attention path")
         if isinstance(self._k, HybridSide) or isinstance(self._v, HybridSide):
             raise NotImplementedError("graph mode does not cover hybrid stores")
-        if self._k.quantize and self._k.over_token:
-            raise NotImplementedError("graph mode does not cover keys grouped over tokens")
         self._k.graph_begin(max_steps)
         self._v.graph_begin(max_steps)
         self._gstep = step

@@ -137,11 +137,10 @@ int make_plan(const innerq_attn_args* a, Plan& p) {
       return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: hybrid values need keys in groups of 32 (use innerq_dequant)");
   }
   // keys grouped over tokens (KIVI, cache.py:87): the query is scaled per
-  // token group inside the kernel; built for GQA <= 4, eager launches,
-  // unnormalised keys, the values' sink size, non-hybrid values
+  // token group inside the kernel; built for GQA <= 4, unnormalised keys,
+  // the values' sink size, non-hybrid values
   if (packed(a->k) && a->k.over_token) {
     if (p.R > 4) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens need GQA <= 4");
-    if (a->step) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens in graph mode");
     if (a->key_norm) return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: normalised keys grouped over tokens");
     if (a->k.n_sink != a->v.n_sink)
       return fail(INNERQ_ERR_UNSUPPORTED, "fused attention: keys grouped over tokens need the values' sink size");
@@ -465,7 +464,8 @@ int innerq_append_step(const innerq_append_args* a, const int64_t* step, void* s
       if (a->flush % a->group || a->n_q % a->group)
         return fail(INNERQ_ERR_ARG, "token groups need flush (%d) and n_q (%d) divisible by group %d",
                     a->flush, a->n_q, a->group);
-      g.mode = 1;
+      if (a->norm_f) return fail(INNERQ_ERR_UNSUPPORTED, "normalisation with token groups");
+      g.mode = a->role == INNERQ_ROLE_V ? 1 : 4;
     } else {
       if (a->norm_f && a->role == INNERQ_ROLE_V) return fail(INNERQ_ERR_ARG, "normalised values");
       g.mode = a->role == INNERQ_ROLE_V ? 2 : 0;

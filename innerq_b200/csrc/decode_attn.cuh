@@ -659,7 +659,7 @@ __device__ __forceinline__ void load_kscales(float2 out[2][NG], const uint16_t* 
 template <int BK, int BV, int RP, int DT, int NG, int VCH, int GM, int VHY = 0, int KOT = 0>
 __global__ void __launch_bounds__(kWarps * 32, RP == 4 ? 4 : 4)
 decode_attn_kernel(const DevArgs a) {
-  static_assert(!KOT || (RP == 4 && NG == 4 && !GM && !VHY), "keys over tokens: GQA <= 4, eager, non-hybrid");
+  static_assert(!KOT || (RP == 4 && NG == 4 && !VHY), "keys over tokens: GQA <= 4, non-hybrid");
   constexpr int NT = RP / 4;
   constexpr int kStages = stages_for(RP);
   extern __shared__ __align__(128) uint8_t dyn[];

@@ -33,10 +33,10 @@ cudaError_t attn_go_ng(const DevArgs& a, int ng, dim3 grid, cudaStream_t s) {
     }
     return cudaErrorNotSupported;
   }
-  // keys grouped over tokens (KIVI): GQA <= 4, eager launches (make_plan)
+  // keys grouped over tokens (KIVI): GQA <= 4 (make_plan)
   if (a.k.otok) {
-    if constexpr (GM == 0 && RP == 4) {
-      return a.v.chan ? attn_go<BK, DT, BV, 4, 4, 1, 0, 0, 1>(a, grid, s) : attn_go<BK, DT, BV, 4, 4, 0, 0, 0, 1>(a, grid, s);
+    if constexpr (RP == 4) {
+      return a.v.chan ? attn_go<BK, DT, BV, 4, 4, 1, GM, 0, 1>(a, grid, s) : attn_go<BK, DT, BV, 4, 4, 0, GM, 0, 1>(a, grid, s);
     }
     return cudaErrorNotSupported;
   }

@@ -719,7 +719,8 @@ pack_col_token_kernel(const uint16_t* __restrict__ x, int64_t sb, int64_t sh, in
 // counter (steps taken, this one included) and the state at step 0, so the
 // launch replays from a CUDA graph.  Grid (H, B), 128 threads.
 // MODE 0: channel groups, row layout (keys); 1: token groups, col layout
-// (values); 2: channel groups, col layout (values); 3: no quantization.
+// (values); 2: channel groups, col layout (values); 3: no quantization;
+// 4: token groups, row layout (keys grouped over tokens, KIVI).
 // --------------------------------------------------------------------------
 struct AppendDev {
   const uint16_t* x;
@@ -754,9 +755,10 @@ __global__ void __launch_bounds__(128) append_step_kernel(const AppendDev a, con
   const int64_t t0 = (int64_t)a.n_q + (int64_t)a.flush * k0;
   if (f0 + a.flush > a.fifo_cap || t0 + a.flush > a.cap_tiles * 32) return;  // beyond the reserved capacity
   __syncthreads();  // the new token may be one of those flushed
-  if (MODE == 1) {
+  if (MODE == 1 || MODE == 4) {
+    // token groups: values (col layout) or keys (row layout, KIVI)
     for (int g = 0; g < a.flush; g += a.group) {
-      pack_col_group<DT, BITS, 1>(fifo + (int64_t)(f0 + g) * a.f_t, a.f_t, a.group, a.asym, a.codes, a.scale,
+      pack_col_group<DT, BITS, MODE == 1 ? 1 : 0>(fifo + (int64_t)(f0 + g) * a.f_t, a.f_t, a.group, a.asym, a.codes, a.scale,
                                   a.zero, a.cap_tiles, t0 + g, bh);
       __syncthreads();
     }
@@ -1024,6 +1026,7 @@ cudaError_t launch_append_step(const AppendArgs& g, const int64_t* step, cudaStr
     case 0: DT_DISPATCH(dt, BITS_DISPATCH(bits, e = launch_pdl(append_step_kernel<DTC, BC, 0>, grid, dim3(128), 0, s, a, step))); break;
     case 1: DT_DISPATCH(dt, BITS_DISPATCH(bits, e = launch_pdl(append_step_kernel<DTC, BC, 1>, grid, dim3(128), 0, s, a, step))); break;
     case 2: DT_DISPATCH(dt, BITS_DISPATCH(bits, e = launch_pdl(append_step_kernel<DTC, BC, 2>, grid, dim3(128), 0, s, a, step))); break;
+    case 4: DT_DISPATCH(dt, BITS_DISPATCH(bits, e = launch_pdl(append_step_kernel<DTC, BC, 4>, grid, dim3(128), 0, s, a, step))); break;
     default: DT_DISPATCH(dt, (e = launch_pdl(append_step_kernel<DTC, 4, 3>, grid, dim3(128), 0, s, a, step))); break;
   }
   return e;

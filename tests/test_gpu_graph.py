@@ -16,6 +16,10 @@ PRESETS = {
                         value_w_sink=32, key_w_recent=96, value_w_recent=96, key_normalize=True),
     "v_channels": dict(k_bits=4, v_bits=4, key_flush_size=1, value_flush_size=32,
                        value_quantize_over_token=False, key_w_recent=32, value_w_recent=32),
+    # kivi (run_lmeval.sh:54-72): keys grouped over tokens, values over channels
+    "kivi": dict(k_bits=2, v_bits=2, key_flush_size=32, value_flush_size=1, key_w_recent=128,
+                 value_w_recent=128, key_quantize_over_token=True, value_quantize_over_token=False,
+                 key_quantize_mode="asymmetric", value_quantize_mode="asymmetric"),
     "gqa8_2bit_asym": dict(k_bits=2, v_bits=2, key_flush_size=1, value_flush_size=32,
                            key_quantize_mode="asymmetric", value_quantize_mode="asymmetric",
                            key_w_sink=4, value_w_sink=4),
