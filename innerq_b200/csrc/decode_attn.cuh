@@ -1107,17 +1107,14 @@ decode_attn_kernel(const DevArgs a) {
         }
         }
       } else if (vpacked) {
-        int ps = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           // round to nearest on the FMA pipe: adding 1.5*2^23 leaves the integer
           // in the low mantissa bits (pt*65535 < 2^22)
           const int v = __float_as_int(fmaf(pt[j], 65535.f, 12582912.f)) - 0x4B400000;
-          ps += v;
           sm.pd_s[warp][head][0][gid + 8 * j] = (uint8_t)(v >> 8);
           sm.pd_s[warp][head][1][gid + 8 * j] = (uint8_t)(v & 255);
         }
-        psum[nt] = gid_isum(ps);
         fv[nt] = wt * (1.f / 65535.f);
       }
       if (!vpacked) {
@@ -1162,6 +1159,14 @@ decode_attn_kernel(const DevArgs a) {
         const int head = nt * 4 + (gid >> 1), digit = gid & 1;
         pb[nt][0] = *reinterpret_cast<const uint32_t*>(&sm.pd_s[warp][head][digit][4 * tq]);
         pb[nt][1] = *reinterpret_cast<const uint32_t*>(&sm.pd_s[warp][head][digit][16 + 4 * tq]);
+        // the tile's probability sum of head tq (+4nt): an all-ones A operand
+        // sums each digit column (hi, lo) over the 32 tokens
+        {
+          const uint32_t ones[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
+          int acc[4];
+          imma_u8u8(acc, ones, pb[nt], 0, 0, 0, 0);
+          psum[nt] = acc[0] * 256 + acc[1];
+        }
         offp[nt] = (float)(voff * psum[nt]);
         zf[nt] = (float)psum[nt] * fv[nt];
       }
