@@ -190,12 +190,6 @@ __device__ __forceinline__ float gid_sum(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 16);
   return v;
 }
-__device__ __forceinline__ int gid_isum(int v) {
-  v += __shfl_xor_sync(0xffffffffu, v, 4);
-  v += __shfl_xor_sync(0xffffffffu, v, 8);
-  v += __shfl_xor_sync(0xffffffffu, v, 16);
-  return v;
-}
 
 // words of one packed K token row (row layout): b=4: 4, b=2: 2, b=3: L0 L1 H
 template <int BITS> struct KRow { uint32_t w[BITS == 4 ? 4 : 3]; };
@@ -1085,16 +1079,13 @@ decode_attn_kernel(const DevArgs a) {
                                pin[3] ? p23.y : 0.f};
           const float mg = gid_max(fmaxf(fmaxf(pr[0], pr[1]), fmaxf(pr[2], pr[3])));
           const float inv = mg > 0.f ? __fdividef(65000.f, mg) : 0.f;
-          int ps = 0;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int v = __float_as_int(fmaf(pr[j], inv, 12582912.f)) - 0x4B400000;
-            ps += v;
             pdc_s[warp][g][head][0][gid + 8 * j] = (uint8_t)(v >> 8);
             pdc_s[warp][g][head][1][gid + 8 * j] = (uint8_t)(v & 255);
           }
           fvg[nt][g] = wt * mg * (1.f / 65000.f);
-          offg[nt][g] = (float)(voff * gid_isum(ps));
           if (vasym) {
             const float2 z01 = __fmul2_rn(make_float2(pt[0], pt[1]), vzc[0][g]);
             const float2 z23 = __fmul2_rn(make_float2(pt[2], pt[3]), vzc[VCH ? 1 : 0][g]);
@@ -1141,6 +1132,14 @@ decode_attn_kernel(const DevArgs a) {
           const int head = nt * 4 + (gid >> 1), digit = gid & 1;
           const uint32_t pb[2] = {*reinterpret_cast<const uint32_t*>(&pdc_s[warp][g][head][digit][4 * tq]),
                                   *reinterpret_cast<const uint32_t*>(&pdc_s[warp][g][head][digit][16 + 4 * tq])};
+          if (mt % MPG == 0) {
+            // the group's digit sums of head tq (+4nt), hi and lo: an
+            // all-ones A operand sums each B column over the 32 tokens
+            const uint32_t ones[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
+            int sacc[4];
+            imma_u8u8(sacc, ones, pb, 0, 0, 0, 0);
+            offg[nt][g] = (float)(voff * (sacc[0] * 256 + sacc[1]));
+          }
           int acc[4];
           imma_u8u8(acc, af, pb, 0, 0, 0, 0);
           const float t0f = (float)(acc[0] * 256 + acc[1]), t1f = (float)(acc[2] * 256 + acc[3]);
